@@ -1,0 +1,164 @@
+/* rt_b200.h: the C ABI of the B200 Q8_0 weight products (librt_b200.so).
+ *
+ * It keeps the reference runtime's product entry points (Lasimeri/Intel-Phi-APL, src/card/rt.h)
+ * with their prototypes unchanged, so the code the APL compiler generates for every Q8_0 product
+ * (src/apl/compiler/em.apl:601-617) links against this library as it is. What changes is where
+ * the data lives and who computes:
+ *
+ *   - w, x, y (and z, idx) are DEVICE pointers in HBM on the calling thread's current CUDA device;
+ *   - w is a matrix in the row-split Q8_0 layout (gemv_s_bytes / gemv_s_repack below), not the
+ *     reference's form I;
+ *   - the products run as sm_100a CUDA kernels; y is bit-identical to the reference's host model
+ *     for t < 16 tokens (fp32, same rounding order) and within 2e-3 (relative, rms floor) for the
+ *     tensor-core path at t >= 16 (fp16 operands, fp32 sums);
+ *   - by default every product call returns with its results in y (the reference's team_run is
+ *     blocking too); rt_b200_set_async makes them stream-ordered instead.
+ *
+ * Preconditions, as the reference states them (src/card/rt.h:5-8, src/card/gemv.h:1): cols a
+ * multiple of 32. Unlike the reference, rows need not be a multiple of 16 and every argument is
+ * checked: a call that cannot run does nothing and records an error for rt_b200_last_error(). The
+ * reference's functions are void and check nothing (src/card/rt.c:205-285).
+ *
+ * Thread safety: one calling thread per struct rt, as in the reference (its queue is static
+ * state, src/card/rt.c:217-226); different struct rt may be used from different threads. */
+#ifndef RT_B200_H
+#define RT_B200_H
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define RTB_API __attribute__((visibility("default")))
+#else
+#define RTB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+struct team;
+struct gemm_chain;
+
+/* The reference's runtime state, field for field (src/card/rt.h:19-26), so generated code that
+ * declares one compiles unchanged. Here `chain` holds this library's device context (stream,
+ * queue, error word, scratch); team and gemm_chain stay NULL; threads is stored, not used. */
+struct rt {
+    struct team *team;
+    char *frame;
+    void *chain;
+    struct gemm_chain *gemm_chain;
+    int threads;
+    int last;
+};
+
+/* ---------------------------------------------------------------- the reference's products */
+
+/* src/card/rt.h:39 (rt.c:179-203). Binds R to the current CUDA device: creates its stream, error
+ * word and queue. 0, or -1 (no device, no memory). `threads` is kept in R->threads only. */
+RTB_API int rt_init(struct rt *R, int threads);
+
+/* src/card/rt.h:62 (rt.c:205-214). y[rows] = W x, W rows x cols Q8_0 (row-split), x[cols]. */
+RTB_API void rt_gemv(struct rt *R, const void *w, long rows, long cols, const float *x, float *y);
+
+/* src/card/rt.h:65-69 (rt.c:217-285). The round: queue up to RT_BATCH products that do not read
+ * each other's results, then rt_gemv_go runs all of them in one launch per kind and clears the
+ * queue. rt_gemv_open marks the point where the reference starts its read-ahead before x has
+ * landed; on B200 it does nothing (the launch at go takes microseconds). */
+#define RT_BATCH 8
+RTB_API void rt_gemv_q(struct rt *R, const void *w, long rows, long cols, const float *x, float *y);
+RTB_API void rt_gemv_open(struct rt *R);
+RTB_API void rt_gemv_go(struct rt *R);
+
+/* src/card/rt.h:71-72 (rt.c:244-265). Y = X W^T for t tokens: x [t cols], y [t rows], rows
+ * contiguous. One pass over the weights serves up to 4 tokens on CUDA cores (t < 16, exact); from
+ * t = 16 the tensor cores take the whole product in one pass. */
+RTB_API void rt_gemm(struct rt *R, const void *w, long rows, long cols, const float *x, long t, float *y);
+RTB_API void rt_gemm_q(struct rt *R, const void *w, long rows, long cols, const float *x, long t, float *y);
+
+/* src/card/rt.h:85 (rt.c:484-501). z[cols] = row `row` of W dequantised: z[i] = (float)q * d. */
+RTB_API void rt_q8_row(const void *w, long cols, long row, float *z);
+
+/* ---------------------------------------------------------------- load side */
+
+/* Bytes of a rows x cols matrix in the row-split layout: each row holds its cols int8 quants
+ * (16-byte aligned) then its cols/32 fp16 scales padded to a multiple of 8. Equals the GGUF size
+ * rows*cols*34/32 when cols is a multiple of 256. Replaces gemv_i_bytes (src/card/gemv.h:51). */
+RTB_API long gemv_s_bytes(long rows, long cols);
+
+/* GGUF Q8_0 rows (per 32 columns: fp16 d, 32 int8 q) -> the row-split layout, on the device.
+ * q8 and out are device pointers; out == q8 (in place) is allowed when cols % 256 == 0, as the
+ * reference repacks in place at load (src/card/gemv.c:42-52, src/card/engine.c:303-316).
+ * Returns 0 or an RTB_E* code. Replaces gemv_i_repack (src/card/gemv.h:55). */
+RTB_API int gemv_s_repack(const void *q8, long rows, long cols, void *out);
+
+/* ---------------------------------------------------------------- fused products
+ * The reference runs these as separate queued gemvs plus host work (src/apl/qwen35.apl:124-126,
+ * 170-172; src/apl/compiler/em.apl:820-840). Here each is one pass in the queued round. */
+
+/* h[t][rows] = silu(Wg x)[t] * (Wu x)[t]: the SwiGLU gate and up products fused, each product in
+ * the reference's exact order before the fp32 silu(g)*u = g/(1+exp(-g))*u. t >= 1. */
+RTB_API void rt_gemm_silu_q(struct rt *R, const void *w_gate, const void *w_up, long rows, long cols, const float *x,
+                    long t, float *h);
+RTB_API void rt_gemm_silu(struct rt *R, const void *w_gate, const void *w_up, long rows, long cols, const float *x, long t,
+                  float *h);
+
+/* y[i] = row idx[i] of W times x, i < n: the draft head's product over a subset of the output
+ * matrix's rows (DraftLogits, src/apl/qwen35.apl:170-172; the reference takes a row prefix,
+ * this takes any list). W has w_rows rows; idx is a device array of n int32 row numbers. An index
+ * outside [0, w_rows) is not read: its y is NaN and the call reports RTB_EKERNEL. */
+RTB_API void rt_gemv_rows_q(struct rt *R, const void *w, long w_rows, const int32_t *idx, long n, long cols,
+                            const float *x, float *y);
+RTB_API void rt_gemv_rows(struct rt *R, const void *w, long w_rows, const int32_t *idx, long n, long cols,
+                          const float *x, float *y);
+
+/* ---------------------------------------------------------------- B200 runtime controls */
+
+enum {
+    RTB_OK = 0,
+    RTB_EINVAL = 1,   /* an argument the products cannot take (size, alignment, null) */
+    RTB_ECUDA = 2,    /* a CUDA runtime call failed */
+    RTB_EKERNEL = 3,  /* a kernel reported a bounded wait that gave up (error word) */
+    RTB_ENOMEM = 4,   /* device memory */
+    RTB_ENOTINIT = 5, /* R was not initialised by rt_init */
+    RTB_EQUEUE = 6,   /* more than RT_BATCH*2 queued products */
+    RTB_ENCCL = 7,    /* a collective failed */
+};
+
+/* The first error since the last call (0 if none), for R (or, with R NULL, for the calling
+ * thread's calls that take no R: rt_q8_row, gemv_s_repack); reading it clears it. If msg is not
+ * NULL, up to n bytes of a description are written there. */
+RTB_API int rt_b200_last_error(struct rt *R, char *msg, size_t n);
+
+/* 0: every product call returns after its results are in y (default). 1: calls only enqueue on
+ * R's stream; rt_b200_sync waits and returns the first error. */
+RTB_API void rt_b200_set_async(struct rt *R, int on);
+RTB_API int rt_b200_sync(struct rt *R);
+
+/* R's CUDA stream (a cudaStream_t); set_stream makes R use the caller's stream instead (NULL:
+ * back to R's own). */
+RTB_API void *rt_b200_stream(struct rt *R);
+RTB_API void rt_b200_set_stream(struct rt *R, void *stream);
+
+/* Frees what rt_init made. R can be initialised again. */
+RTB_API void rt_b200_free(struct rt *R);
+
+/* ---------------------------------------------------------------- row sharding over GPUs
+ * One process per GPU. With world > 1, every product's w is this rank's row shard (rows/world
+ * consecutive rows, rank-major, rows % world == 0) while rows, y and t keep the whole product's
+ * meaning: each rank computes its rows and an NCCL all-gather over NVLink fills y on every rank.
+ * nccl_id is the 128-byte ncclUniqueId from rt_b200_nccl_id on rank 0, passed to every rank by
+ * the caller. 0 or an RTB_E* code. */
+RTB_API int rt_b200_nccl_id(void *out128);
+RTB_API int rt_b200_shard(struct rt *R, int rank, int world, const void *nccl_id);
+
+/* ---------------------------------------------------------------- synthetic inputs (benchmarks, tests)
+ * Rows [row0, row0+rows) of a seeded Q8_0 matrix with w ~ sigma*N(0,1), written in the row-split
+ * layout to dst (device); and n seeded fp32 values ~ sigma*N(0,1). The values are the same bits
+ * the CPU generator of the tests produces for the same (seed, stream, index). 0 or RTB_E*. */
+RTB_API int rtb_synth_q8_0(void *dst, long row0, long rows, long cols, uint64_t seed, uint64_t stream, float sigma);
+RTB_API int rtb_synth_f32(float *dst, long n, uint64_t seed, uint64_t stream, float sigma);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

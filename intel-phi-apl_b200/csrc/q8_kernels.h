@@ -1,0 +1,62 @@
+// q8_kernels.h: what the host shim (rt_b200.cu) sees of the kernels: the job tables and the
+// launchers. Plain pointers and integers; every pointer is device memory.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace q8 {
+
+constexpr int MAX_JOBS = 16;  // products one launch serves (a round: the reference queues <= 8)
+constexpr int GEMV_MAX_T = 4; // tokens per pass of the CUDA-core kernel (larger t: several passes)
+
+// One product of the CUDA-core kernel: y[t][o] = sum_k W[row(o)][k] * x[t][k] for o < rows,
+// t < m, in the reference's rounding order. row(o) = idx ? idx[o] : o. With w2 set the job is a
+// fused SwiGLU pair: y[t][o] = silu((Wg x)[o]) * (Wu x)[o], w = Wg, w2 = Wu.
+struct GemvJob {
+    const uint8_t *w;   // row-split layout (q8_layout.h)
+    const uint8_t *w2;  // the up matrix of a SwiGLU pair, or null
+    const int32_t *idx; // row gather list, or null
+    const float *x;     // [m][ldx]
+    float *y;           // [m][ldy]
+    long long rows;     // outputs per token
+    long long src_rows; // rows of w (a gather's indices are checked against it)
+    long long ldx, ldy;
+    int cols;           // a multiple of 32
+    int m;              // tokens, 1..GEMV_MAX_T
+    int tiles;          // row tiles of this job (filled by the launcher)
+    int tile0;          // its first tile in the launch (filled by the launcher)
+};
+
+struct GemvParams {
+    GemvJob job[MAX_JOBS];
+    int njobs;
+    int total_tiles;
+    unsigned *err; // the context's device error word
+};
+
+// Launches the exact CUDA-core product over p.job[0..njobs) (all with the same m). Fills the
+// tile fields. grid_limit 0 = one CTA per SM.
+cudaError_t launch_gemv(GemvParams &p, int num_sms, int grid_limit, cudaStream_t stream);
+
+// ---- the tensor-core gemm (t >= 16): y[t][o] = sum_k fp16(W)[o][k] * fp16(x)[t][k], fp32 sums
+struct GemmJob {
+    const uint8_t *w;   // row-split layout
+    const uint8_t *w2;  // SwiGLU up matrix, or null
+    const __half *xh;   // [t][cols] fp16 (converted by the launcher into scratch)
+    float *y;           // [t][ldy]
+    long long rows;
+    long long ldy;
+    int cols;
+    int t;
+};
+
+// ---- utilities
+cudaError_t launch_repack(const uint8_t *gguf, long long rows, int cols, uint8_t *out, cudaStream_t stream);
+cudaError_t launch_synth_q8(uint8_t *out_split, long long row0, long long rows, int cols, uint64_t seed,
+                            uint64_t stream_id, float sigma, cudaStream_t stream);
+cudaError_t launch_synth_f32(float *out, long long n, uint64_t seed, uint64_t stream_id, float sigma,
+                             cudaStream_t stream);
+cudaError_t launch_q8_row(const uint8_t *w, int cols, long long row, float *z, cudaStream_t stream);
+
+}  // namespace q8

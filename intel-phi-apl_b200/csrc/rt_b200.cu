@@ -1,0 +1,552 @@
+// rt_b200.cu: the C ABI of include/rt_b200.h. Host code only: argument checks, the queued round,
+// the split of a product into kernel launches, row sharding with an NCCL all-gather, and the
+// error state. The reference's counterparts are src/card/rt.c:179-285 (products) and 484-501
+// (rt_q8_row); there the work runs on a thread team, here on the GPU.
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "../../include/rt_b200.h"
+#include "q8_kernels.h"
+#include "q8_layout.h"
+
+namespace {
+
+constexpr int TC_MIN_T = 16; // from this many tokens the product is a dense contraction: tensor cores
+
+enum Kind { K_GEMM, K_SILU, K_ROWS };
+
+struct Item {
+    Kind kind;
+    const uint8_t *w, *w2;
+    const int32_t *idx;
+    const float *x;
+    float *y;
+    long long rows, cols, t;
+    long long src_rows; // rows of w (a gather's bound)
+};
+
+struct Ctx {
+    int device = 0, num_sms = 148;
+    cudaStream_t own_stream = nullptr, stream = nullptr;
+    bool async = false;
+    unsigned *d_err = nullptr;
+    int status = RTB_OK;
+    char msg[256] = {0};
+    std::vector<Item> queue;
+    int rank = 0, world = 1;
+    ncclComm_t comm = nullptr;
+    void *scratch = nullptr; // grows on demand (the tensor-core path's fp16 x)
+    size_t scratch_bytes = 0;
+};
+
+// Errors of the calls that take no struct rt.
+thread_local int t_status = RTB_OK;
+thread_local char t_msg[256];
+
+void set_err(int *status, char *msg, int code, const char *fmt, va_list ap) {
+    if (*status != RTB_OK)
+        return; // keep the first
+    *status = code;
+    vsnprintf(msg, 256, fmt, ap);
+}
+
+void ctx_err(Ctx *c, int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    set_err(&c->status, c->msg, code, fmt, ap);
+    va_end(ap);
+}
+
+void thread_err(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    set_err(&t_status, t_msg, code, fmt, ap);
+    va_end(ap);
+}
+
+Ctx *ctx_of(struct rt *R) {
+    if (!R || !R->chain) {
+        thread_err(RTB_ENOTINIT, "struct rt not initialised by rt_init");
+        return nullptr;
+    }
+    return static_cast<Ctx *>(R->chain);
+}
+
+bool cuda_ok(Ctx *c, cudaError_t e, const char *what) {
+    if (e == cudaSuccess)
+        return true;
+    ctx_err(c, e == cudaErrorMemoryAllocation ? RTB_ENOMEM : RTB_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+    return false;
+}
+
+bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+bool check_product(Ctx *c, const char *fn, const void *w, long long rows, long long cols, const float *x, long long t,
+                   const float *y) {
+    if (!w || !x || !y) {
+        ctx_err(c, RTB_EINVAL, "%s: null pointer", fn);
+        return false;
+    }
+    if (rows < 1 || cols < Q8_QK || cols % Q8_QK || t < 1 || cols > (1ll << 30) || rows > (1ll << 40)) {
+        ctx_err(c, RTB_EINVAL, "%s: rows %lld cols %lld t %lld (cols a multiple of 32, all >= 1)", fn, rows, cols, t);
+        return false;
+    }
+    if (!aligned(w, 16) || !aligned(x, 16) || !aligned(y, 4)) {
+        ctx_err(c, RTB_EINVAL, "%s: w and x must be 16-byte aligned, y 4-byte aligned", fn);
+        return false;
+    }
+    if (c->world > 1 && rows % c->world) {
+        ctx_err(c, RTB_EINVAL, "%s: rows %lld not divisible by the %d shards", fn, rows, c->world);
+        return false;
+    }
+    return true;
+}
+
+bool read_error_word(Ctx *c) {
+    unsigned h = 0;
+    if (!cuda_ok(c, cudaMemcpyAsync(&h, c->d_err, sizeof h, cudaMemcpyDeviceToHost, c->stream), "read error word"))
+        return false;
+    if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "synchronize"))
+        return false;
+    if (h) {
+        ctx_err(c, RTB_EKERNEL, "kernel error word 0x%x (a bounded wait gave up)", h);
+        cuda_ok(c, cudaMemsetAsync(c->d_err, 0, sizeof(unsigned), c->stream), "clear error word");
+        return false;
+    }
+    return true;
+}
+
+bool finish(Ctx *c) {
+    if (c->async)
+        return true;
+    return read_error_word(c);
+}
+
+// The output rows this rank computes of a product with `rows` rows, and where they start.
+void shard_rows(const Ctx *c, long long rows, long long *lr, long long *r0) {
+    *lr = rows / c->world;
+    *r0 = (long long)c->rank * *lr;
+}
+
+// One CUDA-core launch per group of jobs with the same token count.
+bool flush_gemv(Ctx *c, std::vector<q8::GemvJob> &jobs) {
+    while (!jobs.empty()) {
+        const int m = jobs[0].m;
+        q8::GemvParams p;
+        memset(&p, 0, sizeof p);
+        p.err = c->d_err;
+        std::vector<q8::GemvJob> rest;
+        for (const q8::GemvJob &j : jobs) {
+            if (j.m == m && p.njobs < q8::MAX_JOBS)
+                p.job[p.njobs++] = j;
+            else
+                rest.push_back(j);
+        }
+        if (!cuda_ok(c, q8::launch_gemv(p, c->num_sms, 0, c->stream), "gemv launch"))
+            return false;
+        jobs.swap(rest);
+    }
+    return true;
+}
+
+// Splits the items into kernel jobs (passes of <= 4 tokens on CUDA cores), launches them, then
+// all-gathers the sharded outputs.
+bool run_items(Ctx *c, const std::vector<Item> &items) {
+    std::vector<q8::GemvJob> jobs;
+    for (const Item &it : items) {
+        long long lr = it.rows, r0 = 0;
+        if (it.kind != K_ROWS)
+            shard_rows(c, it.rows, &lr, &r0);
+        const long long rb = q8s_row_bytes(it.cols);
+        (void)rb;
+        // Tensor-core path for t >= TC_MIN_T lands here in a later launch kind; until then every
+        // t runs on the exact CUDA-core kernel in passes of GEMV_MAX_T tokens.
+        for (long long k = 0; k < it.t; k += q8::GEMV_MAX_T) {
+            q8::GemvJob j;
+            memset(&j, 0, sizeof j);
+            j.w = it.w;
+            j.w2 = it.kind == K_SILU ? it.w2 : nullptr;
+            j.idx = it.kind == K_ROWS ? it.idx : nullptr;
+            j.x = it.x + k * it.cols;
+            j.ldx = it.cols;
+            j.ldy = it.rows;
+            j.y = it.y + k * it.rows + r0;
+            j.rows = lr;
+            j.src_rows = it.kind == K_ROWS ? it.src_rows : lr;
+            j.cols = int(it.cols);
+            j.m = int(it.t - k < q8::GEMV_MAX_T ? it.t - k : q8::GEMV_MAX_T);
+            jobs.push_back(j);
+        }
+    }
+    if (!flush_gemv(c, jobs))
+        return false;
+    if (c->world > 1) {
+        if (ncclGroupStart() != ncclSuccess) {
+            ctx_err(c, RTB_ENCCL, "ncclGroupStart");
+            return false;
+        }
+        for (const Item &it : items) {
+            if (it.kind == K_ROWS)
+                continue; // the gather list is not sharded
+            long long lr, r0;
+            shard_rows(c, it.rows, &lr, &r0);
+            for (long long k = 0; k < it.t; ++k) {
+                float *yt = it.y + k * it.rows;
+                ncclResult_t e = ncclAllGather(yt + r0, yt, size_t(lr), ncclFloat32, c->comm, c->stream);
+                if (e != ncclSuccess) {
+                    ncclGroupEnd();
+                    ctx_err(c, RTB_ENCCL, "ncclAllGather: %s", ncclGetErrorString(e));
+                    return false;
+                }
+            }
+        }
+        ncclResult_t e = ncclGroupEnd();
+        if (e != ncclSuccess) {
+            ctx_err(c, RTB_ENCCL, "ncclGroupEnd: %s", ncclGetErrorString(e));
+            return false;
+        }
+    }
+    return true;
+}
+
+bool run_now(Ctx *c, const Item &it) {
+    std::vector<Item> one(1, it);
+    return run_items(c, one) && finish(c);
+}
+
+bool enqueue(Ctx *c, const Item &it) {
+    if (c->queue.size() >= size_t(2 * RT_BATCH)) {
+        ctx_err(c, RTB_EQUEUE, "more than %d products queued before rt_gemv_go", 2 * RT_BATCH);
+        return false;
+    }
+    c->queue.push_back(it);
+    return true;
+}
+
+Item make_item(Kind k, const void *w, const void *w2, const int32_t *idx, long long rows, long long cols,
+               const float *x, long long t, float *y) {
+    Item it;
+    it.kind = k;
+    it.w = static_cast<const uint8_t *>(w);
+    it.w2 = static_cast<const uint8_t *>(w2);
+    it.idx = idx;
+    it.x = x;
+    it.y = y;
+    it.rows = rows;
+    it.cols = cols;
+    it.t = t;
+    it.src_rows = rows;
+    return it;
+}
+
+} // namespace
+
+extern "C" {
+
+int rt_init(struct rt *R, int threads) {
+    if (!R)
+        return -1;
+    Ctx *c = new (std::nothrow) Ctx();
+    if (!c)
+        return -1;
+    if (cudaGetDevice(&c->device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, c->device) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
+        delete c;
+        return -1;
+    }
+    c->stream = c->own_stream;
+    if (cudaMalloc(&c->d_err, sizeof(unsigned)) != cudaSuccess || cudaMemset(c->d_err, 0, sizeof(unsigned)) != cudaSuccess) {
+        cudaStreamDestroy(c->own_stream);
+        delete c;
+        return -1;
+    }
+    c->queue.reserve(2 * RT_BATCH);
+    R->team = nullptr;
+    R->chain = c;
+    R->gemm_chain = nullptr;
+    R->threads = threads;
+    return 0;
+}
+
+void rt_b200_free(struct rt *R) {
+    if (!R || !R->chain)
+        return;
+    Ctx *c = static_cast<Ctx *>(R->chain);
+    cudaStreamSynchronize(c->stream);
+    if (c->comm)
+        ncclCommDestroy(c->comm);
+    cudaFree(c->scratch);
+    cudaFree(c->d_err);
+    cudaStreamDestroy(c->own_stream);
+    delete c;
+    R->chain = nullptr;
+}
+
+void rt_gemv(struct rt *R, const void *w, long rows, long cols, const float *x, float *y) {
+    Ctx *c = ctx_of(R);
+    if (c && check_product(c, "rt_gemv", w, rows, cols, x, 1, y))
+        run_now(c, make_item(K_GEMM, w, nullptr, nullptr, rows, cols, x, 1, y));
+}
+
+void rt_gemm(struct rt *R, const void *w, long rows, long cols, const float *x, long t, float *y) {
+    Ctx *c = ctx_of(R);
+    if (c && check_product(c, "rt_gemm", w, rows, cols, x, t, y))
+        run_now(c, make_item(K_GEMM, w, nullptr, nullptr, rows, cols, x, t, y));
+}
+
+void rt_gemv_q(struct rt *R, const void *w, long rows, long cols, const float *x, float *y) {
+    Ctx *c = ctx_of(R);
+    if (c && check_product(c, "rt_gemv_q", w, rows, cols, x, 1, y))
+        enqueue(c, make_item(K_GEMM, w, nullptr, nullptr, rows, cols, x, 1, y));
+}
+
+void rt_gemm_q(struct rt *R, const void *w, long rows, long cols, const float *x, long t, float *y) {
+    Ctx *c = ctx_of(R);
+    if (c && check_product(c, "rt_gemm_q", w, rows, cols, x, t, y))
+        enqueue(c, make_item(K_GEMM, w, nullptr, nullptr, rows, cols, x, t, y));
+}
+
+void rt_gemv_open(struct rt *R) { (void)ctx_of(R); }
+
+void rt_gemv_go(struct rt *R) {
+    Ctx *c = ctx_of(R);
+    if (!c)
+        return;
+    std::vector<Item> items;
+    items.swap(c->queue);
+    if (!items.empty() && run_items(c, items))
+        finish(c);
+}
+
+void rt_gemm_silu_q(struct rt *R, const void *w_gate, const void *w_up, long rows, long cols, const float *x, long t,
+                    float *h) {
+    Ctx *c = ctx_of(R);
+    if (!c)
+        return;
+    if (!w_up) {
+        ctx_err(c, RTB_EINVAL, "rt_gemm_silu_q: null w_up");
+        return;
+    }
+    if (!aligned(w_up, 16)) {
+        ctx_err(c, RTB_EINVAL, "rt_gemm_silu_q: w_up must be 16-byte aligned");
+        return;
+    }
+    if (check_product(c, "rt_gemm_silu_q", w_gate, rows, cols, x, t, h))
+        enqueue(c, make_item(K_SILU, w_gate, w_up, nullptr, rows, cols, x, t, h));
+}
+
+void rt_gemm_silu(struct rt *R, const void *w_gate, const void *w_up, long rows, long cols, const float *x, long t,
+                  float *h) {
+    Ctx *c = ctx_of(R);
+    if (!c)
+        return;
+    if (!w_up || !aligned(w_up, 16)) {
+        ctx_err(c, RTB_EINVAL, "rt_gemm_silu: w_up null or not 16-byte aligned");
+        return;
+    }
+    if (check_product(c, "rt_gemm_silu", w_gate, rows, cols, x, t, h))
+        run_now(c, make_item(K_SILU, w_gate, w_up, nullptr, rows, cols, x, t, h));
+}
+
+static bool check_rows(Ctx *c, const char *fn, long w_rows, const int32_t *idx, long n) {
+    if (!idx || n < 1 || w_rows < 1) {
+        ctx_err(c, RTB_EINVAL, "%s: null idx, n < 1 or w_rows < 1", fn);
+        return false;
+    }
+    if (!aligned(idx, 4)) {
+        ctx_err(c, RTB_EINVAL, "%s: idx must be 4-byte aligned", fn);
+        return false;
+    }
+    return true;
+}
+
+void rt_gemv_rows_q(struct rt *R, const void *w, long w_rows, const int32_t *idx, long n, long cols, const float *x,
+                    float *y) {
+    Ctx *c = ctx_of(R);
+    if (!c || !check_rows(c, "rt_gemv_rows_q", w_rows, idx, n))
+        return;
+    const int world = c->world;
+    c->world = 1; // a gather list is not sharded: check as a plain product
+    const bool ok = check_product(c, "rt_gemv_rows_q", w, n, cols, x, 1, y);
+    c->world = world;
+    if (ok) {
+        Item it = make_item(K_ROWS, w, nullptr, idx, n, cols, x, 1, y);
+        it.src_rows = w_rows;
+        enqueue(c, it);
+    }
+}
+
+void rt_gemv_rows(struct rt *R, const void *w, long w_rows, const int32_t *idx, long n, long cols, const float *x,
+                  float *y) {
+    Ctx *c = ctx_of(R);
+    if (!c || !check_rows(c, "rt_gemv_rows", w_rows, idx, n))
+        return;
+    const int world = c->world;
+    c->world = 1;
+    const bool ok = check_product(c, "rt_gemv_rows", w, n, cols, x, 1, y);
+    c->world = world;
+    if (ok) {
+        Item it = make_item(K_ROWS, w, nullptr, idx, n, cols, x, 1, y);
+        it.src_rows = w_rows;
+        run_now(c, it);
+    }
+}
+
+void rt_q8_row(const void *w, long cols, long row, float *z) {
+    if (!w || !z || cols < Q8_QK || cols % Q8_QK || row < 0 || !aligned(w, 16)) {
+        thread_err(RTB_EINVAL, "rt_q8_row: bad argument (cols %ld row %ld)", cols, row);
+        return;
+    }
+    cudaError_t e = q8::launch_q8_row(static_cast<const uint8_t *>(w), int(cols), row, z, 0);
+    if (e == cudaSuccess)
+        e = cudaStreamSynchronize(0);
+    if (e != cudaSuccess)
+        thread_err(RTB_ECUDA, "rt_q8_row: %s", cudaGetErrorString(e));
+}
+
+long gemv_s_bytes(long rows, long cols) {
+    if (rows < 0 || cols < 0 || cols % Q8_QK)
+        return -1;
+    return long(q8s_bytes(rows, cols));
+}
+
+int gemv_s_repack(const void *q8, long rows, long cols, void *out) {
+    if (!q8 || !out || rows < 1 || cols < Q8_QK || cols % Q8_QK) {
+        thread_err(RTB_EINVAL, "gemv_s_repack: bad argument");
+        return RTB_EINVAL;
+    }
+    if (q8 == out && q8s_row_bytes(cols) != q8_gguf_row_bytes(cols)) {
+        thread_err(RTB_EINVAL, "gemv_s_repack: in place needs cols %% 256 == 0");
+        return RTB_EINVAL;
+    }
+    if (q8 != out) { // the two must not overlap
+        const uintptr_t a = reinterpret_cast<uintptr_t>(q8), b = reinterpret_cast<uintptr_t>(out);
+        const uintptr_t an = uintptr_t(rows * q8_gguf_row_bytes(cols)), bn = uintptr_t(q8s_bytes(rows, cols));
+        if (a < b + bn && b < a + an) {
+            thread_err(RTB_EINVAL, "gemv_s_repack: input and output overlap (not in place)");
+            return RTB_EINVAL;
+        }
+    }
+    if (!aligned(out, 16)) {
+        thread_err(RTB_EINVAL, "gemv_s_repack: out must be 16-byte aligned");
+        return RTB_EINVAL;
+    }
+    cudaError_t e = q8::launch_repack(static_cast<const uint8_t *>(q8), rows, int(cols), static_cast<uint8_t *>(out), 0);
+    if (e == cudaSuccess)
+        e = cudaStreamSynchronize(0);
+    if (e != cudaSuccess) {
+        thread_err(RTB_ECUDA, "gemv_s_repack: %s", cudaGetErrorString(e));
+        return RTB_ECUDA;
+    }
+    return RTB_OK;
+}
+
+int rt_b200_last_error(struct rt *R, char *msg, size_t n) {
+    int *status = &t_status;
+    char *m = t_msg;
+    if (R && R->chain) {
+        Ctx *c = static_cast<Ctx *>(R->chain);
+        status = &c->status;
+        m = c->msg;
+    }
+    const int s = *status;
+    if (msg && n) {
+        strncpy(msg, s ? m : "", n - 1);
+        msg[n - 1] = 0;
+    }
+    *status = RTB_OK;
+    m[0] = 0;
+    return s;
+}
+
+void rt_b200_set_async(struct rt *R, int on) {
+    Ctx *c = ctx_of(R);
+    if (c)
+        c->async = on != 0;
+}
+
+int rt_b200_sync(struct rt *R) {
+    Ctx *c = ctx_of(R);
+    if (!c)
+        return RTB_ENOTINIT;
+    read_error_word(c);
+    return c->status;
+}
+
+void *rt_b200_stream(struct rt *R) {
+    Ctx *c = ctx_of(R);
+    return c ? static_cast<void *>(c->stream) : nullptr;
+}
+
+void rt_b200_set_stream(struct rt *R, void *stream) {
+    Ctx *c = ctx_of(R);
+    if (c)
+        c->stream = stream ? static_cast<cudaStream_t>(stream) : c->own_stream;
+}
+
+int rt_b200_nccl_id(void *out128) {
+    if (!out128)
+        return RTB_EINVAL;
+    ncclUniqueId id;
+    if (ncclGetUniqueId(&id) != ncclSuccess)
+        return RTB_ENCCL;
+    static_assert(sizeof(id) == 128, "ncclUniqueId is 128 bytes");
+    memcpy(out128, &id, sizeof id);
+    return RTB_OK;
+}
+
+int rt_b200_shard(struct rt *R, int rank, int world, const void *nccl_id) {
+    Ctx *c = ctx_of(R);
+    if (!c)
+        return RTB_ENOTINIT;
+    if (world < 1 || rank < 0 || rank >= world || (world > 1 && !nccl_id)) {
+        ctx_err(c, RTB_EINVAL, "rt_b200_shard: rank %d world %d", rank, world);
+        return RTB_EINVAL;
+    }
+    if (c->comm) {
+        ncclCommDestroy(c->comm);
+        c->comm = nullptr;
+    }
+    c->rank = rank;
+    c->world = world;
+    if (world == 1)
+        return RTB_OK;
+    ncclUniqueId id;
+    memcpy(&id, nccl_id, sizeof id);
+    ncclResult_t e = ncclCommInitRank(&c->comm, world, id, rank);
+    if (e != ncclSuccess) {
+        c->comm = nullptr;
+        c->world = 1;
+        c->rank = 0;
+        ctx_err(c, RTB_ENCCL, "ncclCommInitRank: %s", ncclGetErrorString(e));
+        return RTB_ENCCL;
+    }
+    return RTB_OK;
+}
+
+int rtb_synth_q8_0(void *dst, long row0, long rows, long cols, uint64_t seed, uint64_t stream, float sigma) {
+    if (!dst || rows < 1 || row0 < 0 || cols < Q8_QK || cols % Q8_QK || !aligned(dst, 16))
+        return RTB_EINVAL;
+    cudaError_t e = q8::launch_synth_q8(static_cast<uint8_t *>(dst), row0, rows, int(cols), seed, stream, sigma, 0);
+    if (e == cudaSuccess)
+        e = cudaStreamSynchronize(0);
+    return e == cudaSuccess ? RTB_OK : RTB_ECUDA;
+}
+
+int rtb_synth_f32(float *dst, long n, uint64_t seed, uint64_t stream, float sigma) {
+    if (!dst || n < 1)
+        return RTB_EINVAL;
+    cudaError_t e = q8::launch_synth_f32(dst, n, seed, stream, sigma, 0);
+    if (e == cudaSuccess)
+        e = cudaStreamSynchronize(0);
+    return e == cudaSuccess ? RTB_OK : RTB_ECUDA;
+}
+
+} // extern "C"

@@ -1,0 +1,221 @@
+"""ctypes binding of librt_b200.so (include/rt_b200.h) for Python callers: the tests and bench.py.
+
+It mirrors the reference runtime's product interface (src/card/rt.h:39, 62-72, 85): the same
+names (rt_init, rt_gemv, rt_gemv_q, rt_gemv_open, rt_gemv_go, rt_gemm, rt_gemm_q, rt_q8_row), the
+same argument meaning and order. Arguments are device addresses (ints, e.g. a torch tensor's
+``data_ptr()``). Where the reference has no error path (its functions are void), this binding
+raises ``RtError`` with the library's recorded message after a call that could not run.
+
+There is no fallback: if the CUDA library is missing, ``load()`` raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "librt_b200.so")
+
+RT_BATCH = 8
+RTB_OK = 0
+ERRORS = {1: "RTB_EINVAL", 2: "RTB_ECUDA", 3: "RTB_EKERNEL", 4: "RTB_ENOMEM", 5: "RTB_ENOTINIT", 6: "RTB_EQUEUE",
+          7: "RTB_ENCCL"}
+
+# The entry points include/rt_b200.h declares, all of which the library must export.
+EXPORTS = ("rt_init", "rt_gemv", "rt_gemv_q", "rt_gemv_open", "rt_gemv_go", "rt_gemm", "rt_gemm_q", "rt_q8_row",
+           "gemv_s_bytes", "gemv_s_repack", "rt_gemm_silu_q", "rt_gemm_silu", "rt_gemv_rows_q", "rt_gemv_rows",
+           "rt_b200_last_error", "rt_b200_set_async", "rt_b200_sync", "rt_b200_stream", "rt_b200_set_stream",
+           "rt_b200_free", "rt_b200_nccl_id", "rt_b200_shard", "rtb_synth_q8_0", "rtb_synth_f32")
+
+
+class RtError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{ERRORS.get(code, code)}: {msg}")
+        self.code = code
+
+
+class StructRt(C.Structure):
+    """struct rt of src/card/rt.h:19-26, field for field."""
+    _fields_ = [("team", C.c_void_p), ("frame", C.c_char_p), ("chain", C.c_void_p), ("gemm_chain", C.c_void_p),
+                ("threads", C.c_int), ("last", C.c_int)]
+
+
+_lib = None
+_L = C.c_long
+_P = C.c_void_p
+
+
+def load() -> C.CDLL:
+    """The CUDA library; raises if it has not been built (python intel-phi-apl_b200/build.py)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise FileNotFoundError(f"{LIB_PATH} missing: build it with intel-phi-apl_b200/build.py")
+    lib = C.CDLL(LIB_PATH)
+    R = C.POINTER(StructRt)
+    sig = {
+        "rt_init": ([R, C.c_int], C.c_int),
+        "rt_gemv": ([R, _P, _L, _L, _P, _P], None),
+        "rt_gemv_q": ([R, _P, _L, _L, _P, _P], None),
+        "rt_gemv_open": ([R], None),
+        "rt_gemv_go": ([R], None),
+        "rt_gemm": ([R, _P, _L, _L, _P, _L, _P], None),
+        "rt_gemm_q": ([R, _P, _L, _L, _P, _L, _P], None),
+        "rt_q8_row": ([_P, _L, _L, _P], None),
+        "gemv_s_bytes": ([_L, _L], _L),
+        "gemv_s_repack": ([_P, _L, _L, _P], C.c_int),
+        "rt_gemm_silu_q": ([R, _P, _P, _L, _L, _P, _L, _P], None),
+        "rt_gemm_silu": ([R, _P, _P, _L, _L, _P, _L, _P], None),
+        "rt_gemv_rows_q": ([R, _P, _L, _P, _L, _L, _P, _P], None),
+        "rt_gemv_rows": ([R, _P, _L, _P, _L, _L, _P, _P], None),
+        "rt_b200_last_error": ([R, C.c_char_p, C.c_size_t], C.c_int),
+        "rt_b200_set_async": ([R, C.c_int], None),
+        "rt_b200_sync": ([R], C.c_int),
+        "rt_b200_stream": ([R], _P),
+        "rt_b200_set_stream": ([R, _P], None),
+        "rt_b200_free": ([R], None),
+        "rt_b200_nccl_id": ([_P], C.c_int),
+        "rt_b200_shard": ([R, C.c_int, C.c_int, _P], C.c_int),
+        "rtb_synth_q8_0": ([_P, _L, _L, _L, C.c_uint64, C.c_uint64, C.c_float], C.c_int),
+        "rtb_synth_f32": ([_P, _L, C.c_uint64, C.c_uint64, C.c_float], C.c_int),
+    }
+    for name, (args, res) in sig.items():
+        f = getattr(lib, name)
+        f.argtypes = args
+        f.restype = res
+    _lib = lib
+    return lib
+
+
+def last_error(rt: "Runtime | None" = None) -> tuple[int, str]:
+    buf = C.create_string_buffer(256)
+    code = load().rt_b200_last_error(C.byref(rt.R) if rt is not None else None, buf, 256)
+    return code, buf.value.decode(errors="replace")
+
+
+def _check(rt: "Runtime | None") -> None:
+    code, msg = last_error(rt)
+    if code != RTB_OK:
+        raise RtError(code, msg)
+
+
+def gemv_s_bytes(rows: int, cols: int) -> int:
+    return load().gemv_s_bytes(rows, cols)
+
+
+def gemv_s_repack(q8: int, rows: int, cols: int, out: int) -> None:
+    code = load().gemv_s_repack(q8, rows, cols, out)
+    if code:
+        _check(None)
+        raise RtError(code, "gemv_s_repack")
+
+
+def q8_row(w: int, cols: int, row: int, z: int) -> None:
+    load().rt_q8_row(w, cols, row, z)
+    _check(None)
+
+
+def synth_q8_0(dst: int, row0: int, rows: int, cols: int, seed: int, stream: int, sigma: float = 0.02) -> None:
+    code = load().rtb_synth_q8_0(dst, row0, rows, cols, seed, stream, sigma)
+    if code:
+        raise RtError(code, "rtb_synth_q8_0")
+
+
+def synth_f32(dst: int, n: int, seed: int, stream: int, sigma: float = 1.0) -> None:
+    code = load().rtb_synth_f32(dst, n, seed, stream, sigma)
+    if code:
+        raise RtError(code, "rtb_synth_f32")
+
+
+def nccl_id() -> bytes:
+    buf = C.create_string_buffer(128)
+    code = load().rt_b200_nccl_id(buf)
+    if code:
+        raise RtError(code, "rt_b200_nccl_id")
+    return buf.raw
+
+
+class Runtime:
+    """One struct rt bound to the current CUDA device (rt_init)."""
+
+    def __init__(self, threads: int = 1):
+        self.lib = load()
+        self.R = StructRt()
+        if self.lib.rt_init(C.byref(self.R), threads) != 0:
+            raise RtError(5, "rt_init failed (no CUDA device?)")
+        self._ref = C.byref(self.R)
+
+    def close(self) -> None:
+        if self.R.chain:
+            self.lib.rt_b200_free(self._ref)
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # -- the reference's products (device addresses)
+    def gemv(self, w: int, rows: int, cols: int, x: int, y: int) -> None:
+        self.lib.rt_gemv(self._ref, w, rows, cols, x, y)
+        _check(self)
+
+    def gemv_q(self, w: int, rows: int, cols: int, x: int, y: int) -> None:
+        self.lib.rt_gemv_q(self._ref, w, rows, cols, x, y)
+        _check(self)
+
+    def gemv_open(self) -> None:
+        self.lib.rt_gemv_open(self._ref)
+
+    def gemv_go(self) -> None:
+        self.lib.rt_gemv_go(self._ref)
+        _check(self)
+
+    def gemm(self, w: int, rows: int, cols: int, x: int, t: int, y: int) -> None:
+        self.lib.rt_gemm(self._ref, w, rows, cols, x, t, y)
+        _check(self)
+
+    def gemm_q(self, w: int, rows: int, cols: int, x: int, t: int, y: int) -> None:
+        self.lib.rt_gemm_q(self._ref, w, rows, cols, x, t, y)
+        _check(self)
+
+    # -- fused products
+    def gemm_silu(self, wg: int, wu: int, rows: int, cols: int, x: int, t: int, h: int) -> None:
+        self.lib.rt_gemm_silu(self._ref, wg, wu, rows, cols, x, t, h)
+        _check(self)
+
+    def gemm_silu_q(self, wg: int, wu: int, rows: int, cols: int, x: int, t: int, h: int) -> None:
+        self.lib.rt_gemm_silu_q(self._ref, wg, wu, rows, cols, x, t, h)
+        _check(self)
+
+    def gemv_rows(self, w: int, w_rows: int, idx: int, n: int, cols: int, x: int, y: int) -> None:
+        self.lib.rt_gemv_rows(self._ref, w, w_rows, idx, n, cols, x, y)
+        _check(self)
+
+    def gemv_rows_q(self, w: int, w_rows: int, idx: int, n: int, cols: int, x: int, y: int) -> None:
+        self.lib.rt_gemv_rows_q(self._ref, w, w_rows, idx, n, cols, x, y)
+        _check(self)
+
+    # -- controls
+    def set_async(self, on: bool) -> None:
+        self.lib.rt_b200_set_async(self._ref, 1 if on else 0)
+
+    def sync(self) -> None:
+        code = self.lib.rt_b200_sync(self._ref)
+        if code:
+            _check(self)
+            raise RtError(code, "rt_b200_sync")
+
+    def stream(self) -> int:
+        return self.lib.rt_b200_stream(self._ref) or 0
+
+    def set_stream(self, stream: int | None) -> None:
+        self.lib.rt_b200_set_stream(self._ref, stream or None)
+
+    def shard(self, rank: int, world: int, nid: bytes | None) -> None:
+        buf = C.create_string_buffer(nid, 128) if nid is not None else None
+        code = self.lib.rt_b200_shard(self._ref, rank, world, buf)
+        if code:
+            _check(self)
+            raise RtError(code, "rt_b200_shard")

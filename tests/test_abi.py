@@ -1,0 +1,56 @@
+"""The C ABI library on CPU: it loads, exports every function include/rt_b200.h declares, keeps
+struct rt's layout, and computes sizes without a GPU. No product runs here."""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "rt_b200.h")
+
+
+def declared_functions() -> list[str]:
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = re.findall(r"^\s*(?:RTB_API\s+)?(?:const\s+)?[a-z_0-9]+\s*\**\s*([a-z_0-9]+)\s*\(", text, flags=re.M)
+    return [n for n in names if n not in ("if", "return")]
+
+
+def test_header_declares_the_reference_products():
+    names = set(declared_functions())
+    # src/card/rt.h:39, 62-72, 85
+    for f in ("rt_init", "rt_gemv", "rt_gemv_q", "rt_gemv_open", "rt_gemv_go", "rt_gemm", "rt_gemm_q", "rt_q8_row"):
+        assert f in names, f
+
+
+def test_library_exports_every_declared_symbol(rtb):
+    lib = rtb.load()
+    names = declared_functions()
+    assert len(names) >= 20
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(names) == set(rtb.EXPORTS)
+
+
+def test_struct_rt_layout(rtb):
+    # src/card/rt.h:19-26 on x86-64: four pointers then two ints
+    assert C.sizeof(rtb.StructRt) == 40
+    assert rtb.StructRt.threads.offset == 32 and rtb.StructRt.last.offset == 36
+
+
+def test_split_sizes(rtb, oracle):
+    for rows, cols in [(1, 32), (7, 96), (4096, 4096), (12288, 4096), (4096, 12288), (151936, 4096)]:
+        assert rtb.gemv_s_bytes(rows, cols) == oracle.port().q8o_split_bytes(rows, cols)
+    assert rtb.gemv_s_bytes(4096, 4096) == 4096 * 4096 * 34 // 32
+    assert rtb.gemv_s_bytes(4, 33) == -1
+
+
+def test_calls_without_init_record_an_error(rtb):
+    lib = rtb.load()
+    R = rtb.StructRt()
+    lib.rt_gemv(C.byref(R), None, 16, 32, None, None)  # R.chain NULL: no device work attempted
+    code, msg = rtb.last_error(None)
+    assert code == 5 and "rt_init" in msg
+    assert rtb.last_error(None)[0] == 0  # reading clears

@@ -1,0 +1,272 @@
+"""Parity of the B200 products with the reference (GPU).
+
+Every product goes through the C ABI of librt_b200.so (rt_gemv, rt_gemm, the queued round, ...)
+on device buffers; the checker is the CPU oracle (oracle/), itself pinned to the reference's own
+host-model output (tests/test_oracle.py), and for the golden cases the reference's y directly.
+
+Bar: for t < 16 tokens the CUDA-core path computes the reference's rounding sequence, so y must
+equal the reference bit for bit (compared as uint32 patterns). The fused SwiGLU adds an fp32
+silu(g)*u after two exact products: within 1e-5 relative (rms floor) of the F64 value.
+"""
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+SEED = 20261201
+
+
+def rel_err(y: np.ndarray, ref: np.ndarray) -> float:
+    """max |y - ref| / max(|ref|, rms(ref)): relative error with an rms floor for outputs near 0."""
+    ref = ref.astype(np.float64)
+    rms = float(np.sqrt(np.mean(ref ** 2))) or 1.0
+    return float(np.max(np.abs(y.astype(np.float64) - ref) / np.maximum(np.abs(ref), rms)))
+
+
+def bits_equal(a: np.ndarray, b: np.ndarray) -> bool:
+    return np.array_equal(np.ascontiguousarray(a, dtype=np.float32).view(np.uint32),
+                          np.ascontiguousarray(b, dtype=np.float32).view(np.uint32))
+
+
+class Mat:
+    """A seeded Q8_0 matrix on the device (row-split layout, made by the GPU generator) and the
+    same matrix's GGUF bytes on the host (made by the CPU generator)."""
+
+    def __init__(self, torch, rtb, oracle, rows, cols, stream, host=True):
+        self.rows, self.cols = rows, cols
+        self.dev = torch.empty(rtb.gemv_s_bytes(rows, cols), dtype=torch.uint8, device="cuda")
+        rtb.synth_q8_0(self.dev.data_ptr(), 0, rows, cols, SEED, stream)
+        self.q8 = oracle.synth_q8_0(rows, cols, SEED, stream) if host else None
+
+    @property
+    def ptr(self) -> int:
+        return self.dev.data_ptr()
+
+
+def dev(torch, a: np.ndarray):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def xs(oracle, t, cols, stream):
+    return np.stack([oracle.synth_f32(cols, SEED, stream + 1000 * k) for k in range(t)]).astype(np.float32)
+
+
+# ---------------------------------------------------------------- inputs and layout
+
+@pytest.mark.parametrize("rows,cols", [(1, 32), (5, 96), (64, 4096), (3, 4128)])
+def test_gpu_generator_matches_cpu(cuda, rtb, oracle, rows, cols):
+    m = Mat(cuda, rtb, oracle, rows, cols, 7)
+    assert np.array_equal(m.dev.cpu().numpy(), oracle.repack_split(m.q8, rows, cols))
+    x = cuda.empty(1000, dtype=cuda.float32, device="cuda")
+    rtb.synth_f32(x.data_ptr(), 1000, SEED, 9)
+    assert bits_equal(x.cpu().numpy(), oracle.synth_f32(1000, SEED, 9))
+
+
+@pytest.mark.parametrize("rows,cols,in_place", [(37, 4096, True), (16, 96, False), (9, 12288, True), (4, 4128, False)])
+def test_repack(cuda, rtb, oracle, rows, cols, in_place):
+    q8 = oracle.synth_q8_0(rows, cols, SEED, 3)
+    want = oracle.repack_split(q8, rows, cols)
+    src = dev(cuda, q8)
+    if in_place:
+        rtb.gemv_s_repack(src.data_ptr(), rows, cols, src.data_ptr())
+        got = src
+    else:
+        got = cuda.empty(rtb.gemv_s_bytes(rows, cols), dtype=cuda.uint8, device="cuda")
+        rtb.gemv_s_repack(src.data_ptr(), rows, cols, got.data_ptr())
+    assert np.array_equal(got.cpu().numpy(), want)
+
+
+# ---------------------------------------------------------------- the reference's golden y
+
+def _golden():
+    z = np.load(os.path.join(GOLDEN, "ref_vectors.npz"))
+    return z, json.loads(bytes(z["meta"]).decode())
+
+
+@pytest.mark.parametrize("case", range(9))
+def test_reference_golden_vectors(cuda, runtime, rtb, oracle, case):
+    """y of the reference's own gemv_i_thread / gemm_i_thread, reproduced bit for bit on B200."""
+    z, meta = _golden()
+    m = meta[case]
+    rows, cols, t = m["rows"], m["cols"], m["t"]
+    q8 = oracle.synth_q8_0(rows, cols, m["seed"], m["w_stream"])
+    x = np.stack([oracle.synth_f32(cols, m["seed"], m["x_stream"] + 1000 * k) for k in range(t)])
+    w = dev(cuda, oracle.repack_split(q8, rows, cols))
+    xd = dev(cuda, x)
+    y = cuda.full((t, rows), float("nan"), dtype=cuda.float32, device="cuda")
+    if t == 1:
+        runtime.gemv(w.data_ptr(), rows, cols, xd.data_ptr(), y.data_ptr())
+    else:
+        runtime.gemm(w.data_ptr(), rows, cols, xd.data_ptr(), t, y.data_ptr())
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), z[f"{m['name']}.y"])
+
+
+# ---------------------------------------------------------------- gemv
+
+@pytest.mark.parametrize("rows,cols", [
+    (4096, 4096),
+    (8192, 4096),    # fused QKV
+    (4096, 12288),   # down
+    (1, 32), (7, 64), (13, 4096), (100, 12288), (33, 4128), (9, 8192), (257, 1056),
+])
+def test_gemv_bit_exact(cuda, runtime, rtb, oracle, rows, cols):
+    m = Mat(cuda, rtb, oracle, rows, cols, 11)
+    x = xs(oracle, 1, cols, 12)
+    y = cuda.full((rows,), float("nan"), dtype=cuda.float32, device="cuda")
+    runtime.gemv(m.ptr, rows, cols, dev(cuda, x).data_ptr(), y.data_ptr())
+    assert bits_equal(y.cpu().numpy(), oracle.gemv(m.q8, rows, cols, x[0]))
+
+
+def test_gemv_output_head_full_size(cuda, runtime, rtb, oracle):
+    """BASELINE config 2's output head, 151936 x 4096, every output bit for bit."""
+    rows, cols = 151936, 4096
+    m = Mat(cuda, rtb, oracle, rows, cols, 13)
+    x = xs(oracle, 1, cols, 14)
+    y = cuda.empty((rows,), dtype=cuda.float32, device="cuda")
+    runtime.gemv(m.ptr, rows, cols, dev(cuda, x).data_ptr(), y.data_ptr())
+    assert bits_equal(y.cpu().numpy(), oracle.gemv(m.q8, rows, cols, x[0]))
+
+
+# ---------------------------------------------------------------- gemm on CUDA cores (t < 16)
+
+@pytest.mark.parametrize("t", [2, 3, 4, 5, 8, 9, 15])
+@pytest.mark.parametrize("rows,cols", [(256, 4096), (40, 12288), (17, 96)])
+def test_gemm_small_t_bit_exact(cuda, runtime, rtb, oracle, t, rows, cols):
+    m = Mat(cuda, rtb, oracle, rows, cols, 21)
+    x = xs(oracle, t, cols, 22)
+    y = cuda.full((t, rows), float("nan"), dtype=cuda.float32, device="cuda")
+    runtime.gemm(m.ptr, rows, cols, dev(cuda, x).data_ptr(), t, y.data_ptr())
+    assert bits_equal(y.cpu().numpy(), oracle.gemm(m.q8, rows, cols, x, t))
+
+
+def test_gemm_each_token_equals_gemv(cuda, runtime, rtb, oracle):
+    """The reference's gate: gemm of t tokens == one gemv per token, bit for bit
+    (scripts/check.sh:132-149 of the reference)."""
+    rows, cols, t = 1888, 512, 9
+    m = Mat(cuda, rtb, oracle, rows, cols, 23, host=False)
+    x = dev(cuda, xs(oracle, t, cols, 24))
+    y = cuda.empty((t, rows), dtype=cuda.float32, device="cuda")
+    runtime.gemm(m.ptr, rows, cols, x.data_ptr(), t, y.data_ptr())
+    for k in range(t):
+        y1 = cuda.empty((rows,), dtype=cuda.float32, device="cuda")
+        runtime.gemv(m.ptr, rows, cols, x[k].data_ptr(), y1.data_ptr())
+        assert bits_equal(y[k].cpu().numpy(), y1.cpu().numpy())
+
+
+# ---------------------------------------------------------------- fused products
+
+@pytest.mark.parametrize("t", [1, 2, 5])
+def test_swiglu_fused(cuda, runtime, rtb, oracle, t):
+    rows, cols = 1536, 4096
+    g = Mat(cuda, rtb, oracle, rows, cols, 31)
+    u = Mat(cuda, rtb, oracle, rows, cols, 32)
+    x = xs(oracle, t, cols, 33)
+    h = cuda.full((t, rows), float("nan"), dtype=cuda.float32, device="cuda")
+    runtime.gemm_silu(g.ptr, u.ptr, rows, cols, dev(cuda, x).data_ptr(), t, h.data_ptr())
+    yg = oracle.gemm(g.q8, rows, cols, x, t).astype(np.float64)
+    yu = oracle.gemm(u.q8, rows, cols, x, t).astype(np.float64)
+    want = yg / (1.0 + np.exp(-yg)) * yu
+    assert rel_err(h.cpu().numpy(), want) < 1e-5
+
+
+def test_draft_head_gather(cuda, runtime, rtb, oracle):
+    """32,768 seeded rows of the 151,936 x 4096 output matrix."""
+    rows, cols, n = 151936, 4096, 32768
+    m = Mat(cuda, rtb, oracle, rows, cols, 41, host=False)
+    idx = np.sort(np.random.default_rng(SEED).choice(rows, n, replace=False)).astype(np.int32)
+    idx = np.random.default_rng(SEED + 1).permutation(idx).astype(np.int32)
+    x = xs(oracle, 1, cols, 42)
+    y = cuda.empty((n,), dtype=cuda.float32, device="cuda")
+    runtime.gemv_rows(m.ptr, rows, dev(cuda, idx).data_ptr(), n, cols, dev(cuda, x).data_ptr(), y.data_ptr())
+    rb = rtb.gemv_s_bytes(1, cols)
+    sel = m.dev.view(rows, rb)[cuda.from_numpy(idx.astype(np.int64)).cuda()].cpu().numpy().reshape(-1)
+    q8 = oracle.unpack_split(sel, n, cols)
+    assert bits_equal(y.cpu().numpy(), oracle.gemv(q8, n, cols, x[0]))
+
+
+def test_queued_round(cuda, runtime, rtb, oracle):
+    """One round (rt_gemv_q ... rt_gemv_go): products of several shapes, a SwiGLU pair, a gather
+    and a 2-token gemm run in one go, each exact."""
+    cols = 4096
+    a = Mat(cuda, rtb, oracle, 8192, cols, 51)
+    b = Mat(cuda, rtb, oracle, 4096, cols, 52)
+    g = Mat(cuda, rtb, oracle, 512, cols, 53)
+    u = Mat(cuda, rtb, oracle, 512, cols, 54)
+    x = xs(oracle, 2, cols, 55)
+    xd = dev(cuda, x)
+    ya = cuda.empty(8192, dtype=cuda.float32, device="cuda")
+    yb = cuda.empty((2, 4096), dtype=cuda.float32, device="cuda")
+    h = cuda.empty(512, dtype=cuda.float32, device="cuda")
+    idx = np.array([4095, 0, 17, 17, 2048], dtype=np.int32)
+    yr = cuda.empty(5, dtype=cuda.float32, device="cuda")
+    runtime.gemv_q(a.ptr, 8192, cols, xd.data_ptr(), ya.data_ptr())
+    runtime.gemm_q(b.ptr, 4096, cols, xd.data_ptr(), 2, yb.data_ptr())
+    runtime.gemm_silu_q(g.ptr, u.ptr, 512, cols, xd.data_ptr(), 1, h.data_ptr())
+    idx_d = dev(cuda, idx)
+    runtime.gemv_rows_q(b.ptr, 4096, idx_d.data_ptr(), 5, cols, xd.data_ptr(), yr.data_ptr())
+    runtime.gemv_open()
+    runtime.gemv_go()
+    assert bits_equal(ya.cpu().numpy(), oracle.gemv(a.q8, 8192, cols, x[0]))
+    yb_ref = oracle.gemm(b.q8, 4096, cols, x, 2)
+    assert bits_equal(yb.cpu().numpy(), yb_ref)
+    assert bits_equal(yr.cpu().numpy(), yb_ref[0][idx])
+    yg = oracle.gemv(g.q8, 512, cols, x[0]).astype(np.float64)
+    yu = oracle.gemv(u.q8, 512, cols, x[0]).astype(np.float64)
+    assert rel_err(h.cpu().numpy(), yg / (1 + np.exp(-yg)) * yu) < 1e-5
+
+
+# ---------------------------------------------------------------- rt_q8_row, modes, errors
+
+def test_q8_row(cuda, rtb, oracle):
+    rows, cols = 40, 4128
+    m = Mat(cuda, rtb, oracle, rows, cols, 61)
+    z = cuda.empty(cols, dtype=cuda.float32, device="cuda")
+    for r in (0, 17, 39):
+        rtb.q8_row(m.ptr, cols, r, z.data_ptr())
+        blk = m.q8.reshape(rows, cols // 32, 34)[r]
+        d = blk[:, :2].copy().view(np.float16).astype(np.float32)
+        q = blk[:, 2:].view(np.int8).astype(np.float32)
+        assert bits_equal(z.cpu().numpy(), (q * d).reshape(-1))
+
+
+def test_async_mode_and_stream(cuda, rtb, oracle):
+    rt = rtb.Runtime()
+    try:
+        rt.set_async(True)
+        rows, cols = 2048, 4096
+        m = Mat(cuda, rtb, oracle, rows, cols, 71)
+        x = xs(oracle, 3, cols, 72)
+        xd = dev(cuda, x)
+        ys = [cuda.empty(rows, dtype=cuda.float32, device="cuda") for _ in range(3)]
+        for k in range(3):
+            rt.gemv(m.ptr, rows, cols, xd[k].data_ptr(), ys[k].data_ptr())
+        rt.sync()
+        want = oracle.gemm(m.q8, rows, cols, x, 3)
+        for k in range(3):
+            assert bits_equal(ys[k].cpu().numpy(), want[k])
+    finally:
+        rt.close()
+
+
+def test_bad_arguments_raise_and_leave_the_gpu_usable(cuda, runtime, rtb, oracle):
+    m = Mat(cuda, rtb, oracle, 16, 64, 81)
+    x = dev(cuda, xs(oracle, 1, 64, 82))
+    y = cuda.empty(16, dtype=cuda.float32, device="cuda")
+    with pytest.raises(rtb.RtError) as e:
+        runtime.gemv(m.ptr, 16, 33, x.data_ptr(), y.data_ptr())
+    assert e.value.code == 1
+    with pytest.raises(rtb.RtError):
+        runtime.gemv(m.ptr, 0, 64, x.data_ptr(), y.data_ptr())
+    with pytest.raises(rtb.RtError):
+        runtime.gemv(m.ptr, 16, 64, x.data_ptr() + 4, y.data_ptr())  # x not 16-byte aligned
+    with pytest.raises(rtb.RtError):
+        runtime.gemm(m.ptr, 16, 64, x.data_ptr(), 0, y.data_ptr())
+    runtime.gemv(m.ptr, 16, 64, x.data_ptr(), y.data_ptr())  # still works
+    assert bits_equal(y.cpu().numpy(), oracle.gemv(m.q8, 16, 64, x.cpu().numpy()[0]))
