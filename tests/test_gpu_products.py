@@ -119,8 +119,9 @@ def test_reference_golden_vectors(cuda, runtime, rtb, oracle, case):
 def test_gemv_bit_exact(cuda, runtime, rtb, oracle, rows, cols):
     m = Mat(cuda, rtb, oracle, rows, cols, 11)
     x = xs(oracle, 1, cols, 12)
+    xd = dev(cuda, x)
     y = cuda.full((rows,), float("nan"), dtype=cuda.float32, device="cuda")
-    runtime.gemv(m.ptr, rows, cols, dev(cuda, x).data_ptr(), y.data_ptr())
+    runtime.gemv(m.ptr, rows, cols, xd.data_ptr(), y.data_ptr())
     assert bits_equal(y.cpu().numpy(), oracle.gemv(m.q8, rows, cols, x[0]))
 
 
@@ -129,8 +130,9 @@ def test_gemv_output_head_full_size(cuda, runtime, rtb, oracle):
     rows, cols = 151936, 4096
     m = Mat(cuda, rtb, oracle, rows, cols, 13)
     x = xs(oracle, 1, cols, 14)
+    xd = dev(cuda, x)
     y = cuda.empty((rows,), dtype=cuda.float32, device="cuda")
-    runtime.gemv(m.ptr, rows, cols, dev(cuda, x).data_ptr(), y.data_ptr())
+    runtime.gemv(m.ptr, rows, cols, xd.data_ptr(), y.data_ptr())
     assert bits_equal(y.cpu().numpy(), oracle.gemv(m.q8, rows, cols, x[0]))
 
 
@@ -141,8 +143,9 @@ def test_gemv_output_head_full_size(cuda, runtime, rtb, oracle):
 def test_gemm_small_t_bit_exact(cuda, runtime, rtb, oracle, t, rows, cols):
     m = Mat(cuda, rtb, oracle, rows, cols, 21)
     x = xs(oracle, t, cols, 22)
+    xd = dev(cuda, x)
     y = cuda.full((t, rows), float("nan"), dtype=cuda.float32, device="cuda")
-    runtime.gemm(m.ptr, rows, cols, dev(cuda, x).data_ptr(), t, y.data_ptr())
+    runtime.gemm(m.ptr, rows, cols, xd.data_ptr(), t, y.data_ptr())
     assert bits_equal(y.cpu().numpy(), oracle.gemm(m.q8, rows, cols, x, t))
 
 
@@ -168,8 +171,9 @@ def test_swiglu_fused(cuda, runtime, rtb, oracle, t):
     g = Mat(cuda, rtb, oracle, rows, cols, 31)
     u = Mat(cuda, rtb, oracle, rows, cols, 32)
     x = xs(oracle, t, cols, 33)
+    xd = dev(cuda, x)
     h = cuda.full((t, rows), float("nan"), dtype=cuda.float32, device="cuda")
-    runtime.gemm_silu(g.ptr, u.ptr, rows, cols, dev(cuda, x).data_ptr(), t, h.data_ptr())
+    runtime.gemm_silu(g.ptr, u.ptr, rows, cols, xd.data_ptr(), t, h.data_ptr())
     yg = oracle.gemm(g.q8, rows, cols, x, t).astype(np.float64)
     yu = oracle.gemm(u.q8, rows, cols, x, t).astype(np.float64)
     want = yg / (1.0 + np.exp(-yg)) * yu
@@ -183,8 +187,9 @@ def test_draft_head_gather(cuda, runtime, rtb, oracle):
     idx = np.sort(np.random.default_rng(SEED).choice(rows, n, replace=False)).astype(np.int32)
     idx = np.random.default_rng(SEED + 1).permutation(idx).astype(np.int32)
     x = xs(oracle, 1, cols, 42)
+    idx_d, xd = dev(cuda, idx), dev(cuda, x)  # held: a freed tensor's memory can be reused at once
     y = cuda.empty((n,), dtype=cuda.float32, device="cuda")
-    runtime.gemv_rows(m.ptr, rows, dev(cuda, idx).data_ptr(), n, cols, dev(cuda, x).data_ptr(), y.data_ptr())
+    runtime.gemv_rows(m.ptr, rows, idx_d.data_ptr(), n, cols, xd.data_ptr(), y.data_ptr())
     rb = rtb.gemv_s_bytes(1, cols)
     sel = m.dev.view(rows, rb)[cuda.from_numpy(idx.astype(np.int64)).cuda()].cpu().numpy().reshape(-1)
     q8 = oracle.unpack_split(sel, n, cols)
@@ -270,3 +275,26 @@ def test_bad_arguments_raise_and_leave_the_gpu_usable(cuda, runtime, rtb, oracle
         runtime.gemm(m.ptr, 16, 64, x.data_ptr(), 0, y.data_ptr())
     runtime.gemv(m.ptr, 16, 64, x.data_ptr(), y.data_ptr())  # still works
     assert bits_equal(y.cpu().numpy(), oracle.gemv(m.q8, 16, 64, x.cpu().numpy()[0]))
+
+
+def test_gather_index_out_of_range_is_reported_not_read(cuda, runtime, rtb, oracle):
+    """An index outside [0, w_rows) is never copied: its y is NaN and the call reports
+    RTB_EKERNEL; the other rows are exact and the runtime stays usable."""
+    rows, cols = 64, 256
+    m = Mat(cuda, rtb, oracle, rows, cols, 91)
+    x = xs(oracle, 1, cols, 92)
+    xd = dev(cuda, x)
+    idx = np.array([3, rows, 5, -1, 63], dtype=np.int32)
+    idx_d = dev(cuda, idx)
+    y = cuda.zeros(5, dtype=cuda.float32, device="cuda")
+    with pytest.raises(rtb.RtError) as e:
+        runtime.gemv_rows(m.ptr, rows, idx_d.data_ptr(), 5, cols, xd.data_ptr(), y.data_ptr())
+    assert e.value.code == 3
+    got = y.cpu().numpy()
+    assert np.isnan(got[1]) and np.isnan(got[3])
+    want = oracle.gemv(m.q8, rows, cols, x[0])
+    assert bits_equal(got[[0, 2, 4]], want[[3, 5, 63]])
+    ok = np.array([1, 2], dtype=np.int32)
+    ok_d = dev(cuda, ok)
+    runtime.gemv_rows(m.ptr, rows, ok_d.data_ptr(), 2, cols, xd.data_ptr(), y.data_ptr())
+    assert bits_equal(y.cpu().numpy()[:2], want[[1, 2]])
