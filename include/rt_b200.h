@@ -135,7 +135,7 @@ RTB_API void rt_b200_set_async(struct rt *R, int on);
 RTB_API int rt_b200_sync(struct rt *R);
 
 /* R's CUDA stream (a cudaStream_t); set_stream makes R use the caller's stream instead (NULL:
- * back to R's own). */
+ * back to R's own; the legacy default stream is cudaStreamLegacy, not NULL). */
 RTB_API void *rt_b200_stream(struct rt *R);
 RTB_API void rt_b200_set_stream(struct rt *R, void *stream);
 

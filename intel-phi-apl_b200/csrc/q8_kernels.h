@@ -43,13 +43,19 @@ cudaError_t launch_gemv(GemvParams &p, int num_sms, int grid_limit, cudaStream_t
 struct GemmJob {
     const uint8_t *w;   // row-split layout
     const uint8_t *w2;  // SwiGLU up matrix, or null
-    const __half *xh;   // [t][cols] fp16 (converted by the launcher into scratch)
+    const float *x;     // [t][ldx] fp32 (rounded to fp16 into scratch by the launcher)
     float *y;           // [t][ldy]
     long long rows;
-    long long ldy;
+    long long ldx, ldy;
     int cols;
     int t;
 };
+
+// Scratch (device bytes) launch_gemm_tc needs for these jobs: their x in fp16.
+size_t gemm_tc_scratch_bytes(const GemmJob *jobs, int n);
+// Up to 8 jobs in one persistent launch (plus one fp16 conversion of each x).
+cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scratch_bytes, int num_sms,
+                           unsigned *err, cudaStream_t stream);
 
 // ---- utilities
 cudaError_t launch_repack(const uint8_t *gguf, long long rows, int cols, uint8_t *out, cudaStream_t stream);

@@ -58,16 +58,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Waits for the barrier's phase with this parity to complete; false after WAIT_LIMIT_CYCLES.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-    if (mbar_try_wait(bar, parity))
-        return true;
+// The slow path of mbar_wait, out of line: keeps the kernels' hot loops small.
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t *bar, uint32_t parity) {
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
         if (clock64() - t0 > WAIT_LIMIT_CYCLES)
             return false;
     }
     return true;
+}
+
+// Waits for the barrier's phase with this parity to complete; false after WAIT_LIMIT_CYCLES.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity);
 }
 
 // An L2 policy for data read once (the weights): evict first, so the small operands that every

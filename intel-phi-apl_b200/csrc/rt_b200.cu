@@ -93,7 +93,8 @@ bool check_product(Ctx *c, const char *fn, const void *w, long long rows, long l
         ctx_err(c, RTB_EINVAL, "%s: null pointer", fn);
         return false;
     }
-    if (rows < 1 || cols < Q8_QK || cols % Q8_QK || t < 1 || cols > (1ll << 30) || rows > (1ll << 40)) {
+    if (rows < 1 || cols < Q8_QK || cols % Q8_QK || t < 1 || cols > (1ll << 30) || rows > (1ll << 40) ||
+        (t >= TC_MIN_T && (rows > (1ll << 31) || t > (1 << 20)))) {
         ctx_err(c, RTB_EINVAL, "%s: rows %lld cols %lld t %lld (cols a multiple of 32, all >= 1)", fn, rows, cols, t);
         return false;
     }
@@ -155,18 +156,59 @@ bool flush_gemv(Ctx *c, std::vector<q8::GemvJob> &jobs) {
     return true;
 }
 
-// Splits the items into kernel jobs (passes of <= 4 tokens on CUDA cores), launches them, then
-// all-gathers the sharded outputs.
+bool ensure_scratch(Ctx *c, size_t bytes) {
+    if (bytes <= c->scratch_bytes)
+        return true;
+    if (c->scratch && !cuda_ok(c, cudaStreamSynchronize(c->stream), "synchronize before scratch growth"))
+        return false;
+    cudaFree(c->scratch);
+    c->scratch = nullptr;
+    c->scratch_bytes = 0;
+    if (!cuda_ok(c, cudaMalloc(&c->scratch, bytes), "scratch"))
+        return false;
+    c->scratch_bytes = bytes;
+    return true;
+}
+
+// One tensor-core launch per 8 jobs (t >= TC_MIN_T), their x converted into the scratch.
+bool flush_tc(Ctx *c, std::vector<q8::GemmJob> &jobs) {
+    for (size_t i = 0; i < jobs.size(); i += 8) {
+        const int n = int(jobs.size() - i < 8 ? jobs.size() - i : 8);
+        const size_t need = q8::gemm_tc_scratch_bytes(&jobs[i], n);
+        if (!ensure_scratch(c, need))
+            return false;
+        if (!cuda_ok(c, q8::launch_gemm_tc(&jobs[i], n, c->scratch, c->scratch_bytes, c->num_sms, c->d_err, c->stream),
+                     "tensor-core gemm launch"))
+            return false;
+    }
+    jobs.clear();
+    return true;
+}
+
+// Splits the items into kernel jobs (t >= 16: one tensor-core job; else passes of <= 4 tokens on
+// CUDA cores), launches them, then all-gathers the sharded outputs.
 bool run_items(Ctx *c, const std::vector<Item> &items) {
     std::vector<q8::GemvJob> jobs;
+    std::vector<q8::GemmJob> tc;
     for (const Item &it : items) {
         long long lr = it.rows, r0 = 0;
         if (it.kind != K_ROWS)
             shard_rows(c, it.rows, &lr, &r0);
-        const long long rb = q8s_row_bytes(it.cols);
-        (void)rb;
-        // Tensor-core path for t >= TC_MIN_T lands here in a later launch kind; until then every
-        // t runs on the exact CUDA-core kernel in passes of GEMV_MAX_T tokens.
+        if (it.kind != K_ROWS && it.t >= TC_MIN_T) {
+            q8::GemmJob g;
+            memset(&g, 0, sizeof g);
+            g.w = it.w;
+            g.w2 = it.kind == K_SILU ? it.w2 : nullptr;
+            g.x = it.x;
+            g.ldx = it.cols;
+            g.y = it.y + r0;
+            g.ldy = it.rows;
+            g.rows = lr;
+            g.cols = int(it.cols);
+            g.t = int(it.t);
+            tc.push_back(g);
+            continue;
+        }
         for (long long k = 0; k < it.t; k += q8::GEMV_MAX_T) {
             q8::GemvJob j;
             memset(&j, 0, sizeof j);
@@ -184,7 +226,7 @@ bool run_items(Ctx *c, const std::vector<Item> &items) {
             jobs.push_back(j);
         }
     }
-    if (!flush_gemv(c, jobs))
+    if (!flush_gemv(c, jobs) || !flush_tc(c, tc))
         return false;
     if (c->world > 1) {
         if (ncclGroupStart() != ncclSuccess) {

@@ -18,6 +18,7 @@ LIB_PATH = os.path.join(HERE, "librt_b200.so")
 
 RT_BATCH = 8
 RTB_OK = 0
+CUDA_STREAM_LEGACY = 0x1  # cudaStreamLegacy
 ERRORS = {1: "RTB_EINVAL", 2: "RTB_ECUDA", 3: "RTB_EKERNEL", 4: "RTB_ENOMEM", 5: "RTB_ENOTINIT", 6: "RTB_EQUEUE",
           7: "RTB_ENCCL"}
 
@@ -211,7 +212,13 @@ class Runtime:
         return self.lib.rt_b200_stream(self._ref) or 0
 
     def set_stream(self, stream: int | None) -> None:
-        self.lib.rt_b200_set_stream(self._ref, stream or None)
+        """Run on `stream` (a cudaStream_t handle, e.g. torch's ``cuda_stream``). Handle 0 is the
+        legacy default stream and goes to the library as cudaStreamLegacy; None restores the
+        runtime's own stream."""
+        if stream is None:
+            self.lib.rt_b200_set_stream(self._ref, None)
+        else:
+            self.lib.rt_b200_set_stream(self._ref, stream if stream != 0 else CUDA_STREAM_LEGACY)
 
     def shard(self, rank: int, world: int, nid: bytes | None) -> None:
         buf = C.create_string_buffer(nid, 128) if nid is not None else None

@@ -6,7 +6,9 @@ host-model output (tests/test_oracle.py), and for the golden cases the reference
 
 Bar: for t < 16 tokens the CUDA-core path computes the reference's rounding sequence, so y must
 equal the reference bit for bit (compared as uint32 patterns). The fused SwiGLU adds an fp32
-silu(g)*u after two exact products: within 1e-5 relative (rms floor) of the F64 value.
+silu(g)*u after two exact products: within 1e-5 relative (rms floor) of the F64 value. From
+t = 16 the tensor cores run the product on fp16 operands with fp32 sums: within TC_TOL = 2e-3
+as max |y - ref| / max(|ref|, rms(ref)) against the reference's fp32 y.
 """
 from __future__ import annotations
 
@@ -21,6 +23,8 @@ from conftest import GOLDEN
 pytestmark = pytest.mark.gpu
 
 SEED = 20261201
+TC_MIN_T = 16
+TC_TOL = 2e-3
 
 
 def rel_err(y: np.ndarray, ref: np.ndarray) -> float:
@@ -105,7 +109,10 @@ def test_reference_golden_vectors(cuda, runtime, rtb, oracle, case):
         runtime.gemv(w.data_ptr(), rows, cols, xd.data_ptr(), y.data_ptr())
     else:
         runtime.gemm(w.data_ptr(), rows, cols, xd.data_ptr(), t, y.data_ptr())
-    assert np.array_equal(y.cpu().numpy().view(np.uint32), z[f"{m['name']}.y"])
+    if t < TC_MIN_T:
+        assert np.array_equal(y.cpu().numpy().view(np.uint32), z[f"{m['name']}.y"])
+    else:  # tensor cores: fp16 operands
+        assert rel_err(y.cpu().numpy(), z[f"{m['name']}.y"].view(np.float32)) < TC_TOL
 
 
 # ---------------------------------------------------------------- gemv
@@ -298,3 +305,71 @@ def test_gather_index_out_of_range_is_reported_not_read(cuda, runtime, rtb, orac
     ok_d = dev(cuda, ok)
     runtime.gemv_rows(m.ptr, rows, ok_d.data_ptr(), 2, cols, xd.data_ptr(), y.data_ptr())
     assert bits_equal(y.cpu().numpy()[:2], want[[1, 2]])
+
+
+# ---------------------------------------------------------------- gemm on tensor cores (t >= 16)
+
+@pytest.mark.parametrize("t", [16, 17, 40, 64, 300])
+@pytest.mark.parametrize("rows,cols", [(4096, 4096), (200, 12288), (129, 96), (1, 4128)])
+def test_gemm_tensor_cores(cuda, runtime, rtb, oracle, t, rows, cols):
+    """BASELINE config 4 sizes and ragged ones: row tiles cut by the matrix end, K not a
+    multiple of the 64-column stage, several token passes (t = 300 > 256)."""
+    m = Mat(cuda, rtb, oracle, rows, cols, 101)
+    x = xs(oracle, t, cols, 102)
+    xd = dev(cuda, x)
+    y = cuda.full((t, rows), float("nan"), dtype=cuda.float32, device="cuda")
+    runtime.gemm(m.ptr, rows, cols, xd.data_ptr(), t, y.data_ptr())
+    got = y.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert rel_err(got, oracle.gemm(m.q8, rows, cols, x, t)) < TC_TOL
+
+
+@pytest.mark.parametrize("rows,cols", [(12288, 4096), (4096, 12288)])
+def test_gemm_prompt_512(cuda, runtime, rtb, oracle, rows, cols):
+    """BASELINE config 4 at M = 512 on gate/up and down shapes; checked on a row sample (the CPU
+    oracle over all rows would take minutes) plus full-output properties."""
+    t = 512
+    m = Mat(cuda, rtb, oracle, rows, cols, 111, host=False)
+    x = xs(oracle, t, cols, 112)
+    xd = dev(cuda, x)
+    y = cuda.full((t, rows), float("nan"), dtype=cuda.float32, device="cuda")
+    runtime.gemm(m.ptr, rows, cols, xd.data_ptr(), t, y.data_ptr())
+    got = y.cpu().numpy()
+    assert np.isfinite(got).all()
+    sel = np.sort(np.random.default_rng(3).choice(rows, 96, replace=False))
+    q8 = np.concatenate([oracle.synth_q8_0(1, cols, SEED, 111, row0=int(r)) for r in sel])
+    want = oracle.gemm(q8, len(sel), cols, x, t)
+    assert rel_err(got[:, sel], want) < TC_TOL
+
+
+@pytest.mark.parametrize("t", [16, 48])
+def test_swiglu_tensor_cores(cuda, runtime, rtb, oracle, t):
+    rows, cols = 1536, 4096
+    g = Mat(cuda, rtb, oracle, rows, cols, 121)
+    u = Mat(cuda, rtb, oracle, rows, cols, 122)
+    x = xs(oracle, t, cols, 123)
+    xd = dev(cuda, x)
+    h = cuda.full((t, rows), float("nan"), dtype=cuda.float32, device="cuda")
+    runtime.gemm_silu(g.ptr, u.ptr, rows, cols, xd.data_ptr(), t, h.data_ptr())
+    yg = oracle.gemm(g.q8, rows, cols, x, t).astype(np.float64)
+    yu = oracle.gemm(u.q8, rows, cols, x, t).astype(np.float64)
+    assert rel_err(h.cpu().numpy(), yg / (1.0 + np.exp(-yg)) * yu) < 2 * TC_TOL
+
+
+def test_tensor_core_round_mixed_with_cuda_core(cuda, runtime, rtb, oracle):
+    """A queued round holding a t = 1 product, a t = 2 product and a t = 24 product."""
+    cols = 4096
+    a = Mat(cuda, rtb, oracle, 1024, cols, 131)
+    x = xs(oracle, 24, cols, 132)
+    xd = dev(cuda, x)
+    y1 = cuda.empty(1024, dtype=cuda.float32, device="cuda")
+    y2 = cuda.empty((2, 1024), dtype=cuda.float32, device="cuda")
+    y24 = cuda.empty((24, 1024), dtype=cuda.float32, device="cuda")
+    runtime.gemv_q(a.ptr, 1024, cols, xd.data_ptr(), y1.data_ptr())
+    runtime.gemm_q(a.ptr, 1024, cols, xd.data_ptr(), 2, y2.data_ptr())
+    runtime.gemm_q(a.ptr, 1024, cols, xd.data_ptr(), 24, y24.data_ptr())
+    runtime.gemv_go()
+    want = oracle.gemm(a.q8, 1024, cols, x, 24)
+    assert bits_equal(y1.cpu().numpy(), want[0])
+    assert bits_equal(y2.cpu().numpy(), want[:2])
+    assert rel_err(y24.cpu().numpy(), want) < TC_TOL
