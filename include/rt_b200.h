@@ -134,6 +134,13 @@ RTB_API int rt_b200_last_error(struct rt *R, char *msg, size_t n);
 RTB_API void rt_b200_set_async(struct rt *R, int on);
 RTB_API int rt_b200_sync(struct rt *R);
 
+/* 1: the caller vouches that no kernel between products writes the weight matrices (model
+ * weights are read-only after load). Each product kernel is then launched with programmatic
+ * dependent launch and streams its weights while the previous kernel on the stream finishes; it
+ * still waits for that kernel before reading x or a row list and before writing y. 0 (default):
+ * products start after the previous kernel completes, as plain stream order. */
+RTB_API void rt_b200_set_overlap(struct rt *R, int on);
+
 /* R's CUDA stream (a cudaStream_t); set_stream makes R use the caller's stream instead (NULL:
  * back to R's own; the legacy default stream is cudaStreamLegacy, not NULL). */
 RTB_API void *rt_b200_stream(struct rt *R);

@@ -60,6 +60,9 @@ struct TcParams {
     unsigned *err;
 };
 
+// The fp16 copy of x is written by the conversion kernel just before this one on the stream: the
+// producer waits for it (a no-op without programmatic launch) before its first x load.
+
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, int c0, int c1, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
@@ -158,10 +161,13 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
                      "r"(TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
+    if (threadIdx.x == 0)
+        grid_launch_dependents();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    grid_wait(); // x (fp16) and the y buffers belong to the kernels before this one
     const int nk = 0; // per job (cols differ): computed in the loops
     (void)nk;
 
@@ -412,7 +418,7 @@ size_t gemm_tc_scratch_bytes(const GemmJob *jobs, int n) {
 }
 
 cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scratch_bytes, int num_sms,
-                           unsigned *err, cudaStream_t stream) {
+                           unsigned *err, cudaStream_t stream, bool pdl) {
     if (n < 1 || n > 8)
         return cudaErrorInvalidValue;
     if (gemm_tc_scratch_bytes(jobs, n) > scratch_bytes || !scratch)
@@ -480,8 +486,17 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
     int grid = num_sms > 0 ? num_sms : 148;
     if (grid > units)
         grid = units;
-    gemm_tc_kernel<<<grid, NT, smem, stream>>>(p);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(NT);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute lattr[1];
+    lattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    lattr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = lattr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, p);
 }
 
 } // namespace q8

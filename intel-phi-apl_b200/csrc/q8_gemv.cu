@@ -15,9 +15,10 @@
 //              of the slot (then frees the slot) and runs the 4 rows' 32-fma chains side by side
 //              (packed in row pairs); the t_b and fp32 scales go to a partial-sum buffer. Two
 //              warps per SM sub-partition, each on a ~5 KB loop body, keep the issue slots busy;
-//   warp 8     chain: one lane per (token, row) runs acc = fma(t_b, d_b, acc) in block order
-//              and writes y (for a SwiGLU pair: silu(gate) * up);
-//   warp 9     copies: issues a stage's bulk copies as soon as its slot is free.
+//   warps 8-9  chain: one lane per (token, row) runs acc = fma(t_b, d_b, acc) in block order and
+//              writes y (for a SwiGLU pair: silu(gate) * up). The chain is serial per row, so
+//              the CTA's tiles alternate between the two chain warps (a tile's chunks stay on one);
+//   warp 10    copies: issues a stage's bulk copies as soon as its slot is free.
 // Barriers: full (copies landed), empty (slot read), tfull/tempty (partial sums). Every wait is
 // bounded: a timeout sets a bit in the context's error word and the CTA leaves.
 #include <cuda_fp16.h>
@@ -36,102 +37,92 @@ constexpr int STAGES = 4;
 constexpr int TBUF = 4;            // partial-sum buffers: compute may run this far ahead of the chain
 constexpr int NC = 256;            // compute threads: (block column, row half) each
 constexpr int NH = R / 2;          // rows per compute thread
-constexpr int CHAIN_WARP = NC / 32, COPY_WARP = CHAIN_WARP + 1;
-constexpr int NT = NC + 64;
+constexpr int NCHAIN = 2;          // chain warps: tile i of the CTA goes to chain warp i % NCHAIN
+constexpr int CHAIN_WARP = NC / 32; // the first chain warp; the copy warp follows the chain warps
+constexpr int COPY_WARP = CHAIN_WARP + NCHAIN;
+constexpr int NT = NC + 32 * NCHAIN + 32;
 constexpr int ROWB = KC + NBK * 2; // a row's slot: quants then scales, 4352 B
 constexpr int SLOT = R * ROWB;
-constexpr int TPAD = NBK + 1;      // partial-sum row stride (floats): conflict-free per lane = row
+constexpr int TPAD = NBK + 4;      // partial-sum row stride (floats): 16-byte rows, conflict-free per lane = row
 static_assert(NC == 2 * NBK, "two compute threads (row halves) per block column of a stage");
 static_assert(ROWB % 16 == 0 && SLOT % 16 == 0, "bulk copy destinations are 16-byte aligned");
 
+// Per-stage row flags (row loaded or not), written by the copy warp, read by the chain warp. When
+// the copy warp fills stage s, compute has released stage s-STAGES, so it has finished stage
+// s-STAGES-1, whose partial-sum wait means the chain finished stage s-STAGES-1-TBUF: a ring of
+// 16 entries is never overwritten while read.
+constexpr int FRING = 16;
+static_assert(FRING >= STAGES + TBUF + 2, "row-flag ring");
+
 template <int MT>
 constexpr size_t smem_bytes() {
-    return size_t(STAGES) * SLOT + size_t(TBUF) * (MT + 1) * R * TPAD * 4 + (STAGES * 2 + TBUF * 2) * 8;
+    return size_t(STAGES) * SLOT + size_t(TBUF) * (MT + 1) * R * TPAD * 4 + (STAGES * 2 + TBUF * 2) * 8 + FRING * R;
 }
 
-__device__ __forceinline__ int find_job(const GemvParams &p, int g) {
-    int j = 0;
-    while (j + 1 < p.njobs && g >= p.job[j + 1].tile0)
-        ++j;
-    return j;
-}
+// One job's fields, cached in registers by every role when its stage sequence enters the job:
+// the per-stage work then touches no kernel parameter.
+struct JobView {
+    const uint8_t *w, *w2;
+    const int32_t *idx;
+    const float *x;
+    float *y;
+    long long rows, src_rows, ldx, ldy, rb;
+    int cols, m, tile0, rpt, nchunk;
+    __device__ __forceinline__ void load(const GemvJob &J) {
+        w = J.w;
+        w2 = J.w2;
+        idx = J.idx;
+        x = J.x;
+        y = J.y;
+        rows = J.rows;
+        src_rows = J.src_rows;
+        ldx = J.ldx;
+        ldy = J.ldy;
+        cols = J.cols;
+        m = J.m;
+        tile0 = J.tile0;
+        rb = q8s_row_bytes(cols);
+        rpt = w2 ? R / 2 : R; // output rows per tile
+        nchunk = (cols + KC - 1) / KC;
+    }
+};
 
 // The CTA's sequence of stages: tiles blockIdx.x, +gridDim.x, ..., each in ceil(cols/KC) chunks.
-// Every role walks its own copy of it.
+// Every role walks its own copy; tiles only grow, so the job index only moves forward.
 struct StageIter {
-    int g, c, job, nchunk;
-    __device__ void start(const GemvParams &p) {
+    int g, c, job;
+    JobView J;
+    __device__ __forceinline__ void start(const GemvParams &p) {
         g = blockIdx.x;
         c = 0;
-        set(p);
+        job = -1;
+        if (g < p.total_tiles)
+            set(p);
     }
-    __device__ void set(const GemvParams &p) {
-        if (g < p.total_tiles) {
-            job = find_job(p, g);
-            nchunk = (p.job[job].cols + KC - 1) / KC;
+    __device__ __forceinline__ void set(const GemvParams &p) {
+        int j = job < 0 ? 0 : job;
+        while (j + 1 < p.njobs && g >= p.job[j + 1].tile0)
+            ++j;
+        if (j != job) {
+            job = j;
+            J.load(p.job[j]);
         }
     }
-    __device__ bool valid(const GemvParams &p) const { return g < p.total_tiles; }
-    __device__ void next(const GemvParams &p) {
-        if (++c == nchunk) {
+    __device__ __forceinline__ bool valid(const GemvParams &p) const { return g < p.total_tiles; }
+    __device__ __forceinline__ void next(const GemvParams &p) {
+        if (++c == J.nchunk) {
             c = 0;
             g += gridDim.x;
-            set(p);
+            if (g < p.total_tiles)
+                set(p);
         }
     }
+    // stage row r: the output index and the matrix it reads
+    __device__ __forceinline__ long long out_row(int r) const { return (long long)(g - J.tile0) * J.rpt + (r % J.rpt); }
+    __device__ __forceinline__ const uint8_t *matrix(int r) const { return (J.w2 && r >= J.rpt) ? J.w2 : J.w; }
 };
 
-// Row r (0..R-1) of a stage: its output index o, the matrix row it reads, whether it exists
-// (valid) and whether it is read (load: a gather index outside the matrix is not).
-struct StageRow {
-    long long o, src;
-    const uint8_t *mat;
-    bool valid, load;
-};
 
-__device__ __forceinline__ StageRow stage_row(const GemvJob &J, int lt, int r) {
-    const int rpt = J.w2 ? R / 2 : R; // output rows per tile
-    StageRow s;
-    s.o = (long long)lt * rpt + (r % rpt);
-    s.mat = (J.w2 && r >= rpt) ? J.w2 : J.w;
-    s.valid = s.o < J.rows;
-    s.src = s.valid && J.idx ? (long long)J.idx[s.o] : s.o;
-    s.load = s.valid && s.src >= 0 && s.src < J.src_rows;
-    return s;
-}
-
-__device__ __forceinline__ void issue_stage(const GemvParams &p, const StageIter &it, uint8_t *slot_base,
-                                            uint64_t *bar, uint64_t pol) {
-    const GemvJob &J = p.job[it.job];
-    const int lt = it.g - J.tile0;
-    const long long rb = q8s_row_bytes(J.cols);
-    const int c0 = it.c * KC;
-    const int nbk = min(KC, J.cols - c0) / Q8_QK;
-    const uint32_t qbytes = uint32_t(nbk) * Q8_QK, dbytes = (uint32_t(nbk) * 2u + 15u) & ~15u;
-    const bool whole = J.cols == KC; // a row is exactly one slot row: one copy
-    StageRow sr[R];
-    uint32_t total = 0;
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-        sr[r] = stage_row(J, lt, r);
-        if (sr[r].load)
-            total += whole ? uint32_t(rb) : qbytes + dbytes;
-    }
-    mbar_arrive_expect_tx(bar, total);
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-        if (!sr[r].load)
-            continue;
-        const uint8_t *src = sr[r].mat + sr[r].src * rb;
-        uint8_t *dst = slot_base + r * ROWB;
-        if (whole) {
-            bulk_g2s(dst, src, uint32_t(rb), bar, pol);
-        } else {
-            bulk_g2s(dst, src + c0, qbytes, bar, pol);
-            bulk_g2s(dst + KC, src + J.cols + (c0 / Q8_QK) * 2, dbytes, bar, pol);
-        }
-    }
-}
 
 // Rows processed side by side by one compute thread: its 4 for one or two tokens; 2 at a time
 // for three or four (the x registers grow with the tokens).
@@ -194,6 +185,7 @@ __global__ void __launch_bounds__(NT, 1) gemv_exact_kernel(const __grid_constant
     uint64_t *empty = full + STAGES;                                      // [STAGES]
     uint64_t *tfull = empty + STAGES;                                     // [TBUF]
     uint64_t *tempty = tfull + TBUF;                                      // [TBUF]
+    uint8_t *rowflag = reinterpret_cast<uint8_t *>(tempty + TBUF);        // [FRING][R]: row was loaded
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
 
     if (tid == 0) {
@@ -206,6 +198,7 @@ __global__ void __launch_bounds__(NT, 1) gemv_exact_kernel(const __grid_constant
             mbar_init(&tempty[b], 1);
         }
         fence_barrier_init();
+        grid_launch_dependents();
     }
     __syncthreads();
 
@@ -213,6 +206,8 @@ __global__ void __launch_bounds__(NT, 1) gemv_exact_kernel(const __grid_constant
         // ---------------------------------------------------------------- compute threads
         float xr[MT][Q8_QK];
         int xjob = -1, xc = -1;
+        const int b = tid % NBK, half = tid / NBK;
+        grid_wait(); // x comes from the previous kernel on the stream
         StageIter it;
         it.start(p);
         for (int s = 0; it.valid(p); it.next(p), ++s) {
@@ -221,17 +216,15 @@ __global__ void __launch_bounds__(NT, 1) gemv_exact_kernel(const __grid_constant
                 report(p.err, ERR_TIMEOUT_FULL);
                 break;
             }
-            const GemvJob &J = p.job[it.job];
             const int c0 = it.c * KC;
-            const int nbk = min(KC, J.cols - c0) / Q8_QK;
-            const int b = tid % NBK, half = tid / NBK;
+            const int nbk = min(KC, it.J.cols - c0) / Q8_QK;
             const bool active = b < nbk;
             if (active && (it.c != xc || it.job != xjob)) {
                 xc = it.c;
                 xjob = it.job;
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt) {
-                    const float4 *xp = reinterpret_cast<const float4 *>(J.x + mt * J.ldx + c0 + b * Q8_QK);
+                    const float4 *xp = reinterpret_cast<const float4 *>(it.J.x + mt * it.J.ldx + c0 + b * Q8_QK);
 #pragma unroll
                     for (int v = 0; v < 8; ++v) {
                         const float4 f = __ldg(xp + v);
@@ -293,80 +286,138 @@ __global__ void __launch_bounds__(NT, 1) gemv_exact_kernel(const __grid_constant
                 break;
             mbar_arrive(&tfull[tb]);
         }
-    } else if (warp == CHAIN_WARP) {
-        // ---------------------------------------------------------------- chain warp
-        const int mt = lane / R, r = lane % R;
+    } else if (warp < COPY_WARP) {
+        // ---------------------------------------------------------------- chain warps
+        const int mt = lane / R, r = lane % R, cw = warp - CHAIN_WARP;
         float acc = 0.0f;
         StageIter it;
         it.start(p);
-        for (int s = 0; it.valid(p); it.next(p), ++s) {
+        for (int s = 0, tile = 0; it.valid(p); ++s) {
+            const bool own = tile % NCHAIN == cw;
             const int tb = s % TBUF;
-            if (!mbar_wait(&tfull[tb], (s / TBUF) & 1)) {
-                report(p.err, ERR_TIMEOUT_TFULL);
-                break;
-            }
-            const GemvJob &J = p.job[it.job];
-            const int lt = it.g - J.tile0;
-            const int nbk = min(KC, J.cols - it.c * KC) / Q8_QK;
-            const StageRow sr = stage_row(J, lt, r);
-            const bool mine = mt < J.m && sr.load;
-            if (it.c == 0)
-                acc = 0.0f;
-            if (mine) {
-                const float *tp = T + tb * MT * R * TPAD + (mt * R + r) * TPAD;
-                const float *dp = TD + tb * R * TPAD + r * TPAD;
-                int b = 0;
-                for (; b + 16 <= nbk; b += 16) { // loads first, then the 16 dependent fmas
-                    float tv[16], dd[16];
-#pragma unroll
-                    for (int k = 0; k < 16; ++k) {
-                        tv[k] = tp[b + k];
-                        dd[k] = dp[b + k];
-                    }
-#pragma unroll
-                    for (int k = 0; k < 16; ++k)
-                        acc = __fmaf_rn(tv[k], dd[k], acc);
+            const bool last_chunk = it.c == it.J.nchunk - 1;
+            if (own) {
+                if (!mbar_wait(&tfull[tb], (s / TBUF) & 1)) {
+                    report(p.err, ERR_TIMEOUT_TFULL);
+                    break;
                 }
-                for (; b < nbk; ++b)
-                    acc = __fmaf_rn(tp[b], dp[b], acc);
-            }
-            __syncwarp();
-            if (lane == 0)
-                mbar_arrive(&tempty[tb]);
-            if (it.c == it.nchunk - 1) {
-                if (J.w2) {
-                    const float up = __shfl_down_sync(0xffffffffu, acc, R / 2);
-                    if (mine && r < R / 2) {
-                        const float silu = acc / (1.0f + expf(-acc));
-                        J.y[mt * J.ldy + sr.o] = silu * up;
+                const int nbk = min(KC, it.J.cols - it.c * KC) / Q8_QK;
+                const long long o = it.out_row(r);
+                const bool valid = o < it.J.rows;
+                const bool loaded = rowflag[(s % FRING) * R + r] != 0;
+                const bool mine = mt < it.J.m && loaded;
+                if (it.c == 0)
+                    acc = 0.0f;
+                if (mine) {
+                    const float *tp = T + tb * MT * R * TPAD + (mt * R + r) * TPAD;
+                    const float *dp = TD + tb * R * TPAD + r * TPAD;
+                    int b = 0;
+                    for (; b + 16 <= nbk; b += 16) { // 128-bit loads first, then 16 dependent fmas
+                        float4 tv[4], dd[4];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            tv[k] = *reinterpret_cast<const float4 *>(tp + b + 4 * k);
+                            dd[k] = *reinterpret_cast<const float4 *>(dp + b + 4 * k);
+                        }
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            acc = __fmaf_rn(tv[k].x, dd[k].x, acc);
+                            acc = __fmaf_rn(tv[k].y, dd[k].y, acc);
+                            acc = __fmaf_rn(tv[k].z, dd[k].z, acc);
+                            acc = __fmaf_rn(tv[k].w, dd[k].w, acc);
+                        }
                     }
-                } else if (mine) {
-                    J.y[mt * J.ldy + sr.o] = acc;
-                } else if (mt < J.m && sr.valid) { // a gather index outside the matrix
-                    J.y[mt * J.ldy + sr.o] = __int_as_float(0x7fc00000);
-                    report(p.err, ERR_BAD_JOB);
+                    for (; b < nbk; ++b)
+                        acc = __fmaf_rn(tp[b], dp[b], acc);
+                }
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive(&tempty[tb]);
+                if (last_chunk) {
+                    if (it.J.w2) {
+                        const float up = __shfl_down_sync(0xffffffffu, acc, R / 2);
+                        if (mine && r < R / 2) {
+                            const float silu = acc / (1.0f + expf(-acc));
+                            it.J.y[mt * it.J.ldy + o] = silu * up;
+                        }
+                    } else if (mine) {
+                        it.J.y[mt * it.J.ldy + o] = acc;
+                    } else if (mt < it.J.m && valid) { // a gather index outside the matrix
+                        it.J.y[mt * it.J.ldy + o] = __int_as_float(0x7fc00000);
+                        report(p.err, ERR_BAD_JOB);
+                    }
                 }
             }
+            if (last_chunk)
+                ++tile;
+            it.next(p);
         }
-    } else if (lane == 0) {
-        // ---------------------------------------------------------------- copy issuer
+    } else {
+        // ---------------------------------------------------------------- copy issuer (one warp:
+        // lane r < R owns stage row r; a gather's row index is loaded one stage ahead)
         const uint64_t pol = policy_evict_first();
+        bool gathers = false;
+        for (int j = 0; j < p.njobs; ++j)
+            gathers |= p.job[j].idx != nullptr;
+        if (!p.early || gathers)
+            grid_wait(); // weights (unless the caller vouches for them) and row lists may be outputs of it
         StageIter it;
         it.start(p);
+        long long src = -1; // this lane's source row for the current stage (gathers: prefetched)
+        if (it.valid(p) && lane < R && it.J.idx) {
+            const long long o = it.out_row(lane);
+            src = o < it.J.rows ? (long long)__ldg(it.J.idx + o) : -1;
+        }
         int s = 0;
         bool ok = true;
-        for (; it.valid(p); it.next(p), ++s) {
+        for (; it.valid(p); ++s) {
             const int slot = s % STAGES;
             if (s >= STAGES && !mbar_wait(&empty[slot], ((s / STAGES) - 1) & 1)) {
                 report(p.err, ERR_TIMEOUT_FULL);
                 ok = false;
                 break;
             }
-            issue_stage(p, it, slots + size_t(slot) * SLOT, &full[slot], pol);
+            const int c0 = it.c * KC;
+            const int nbk = min(KC, it.J.cols - c0) / Q8_QK;
+            const uint32_t qbytes = uint32_t(nbk) * Q8_QK, dbytes = (uint32_t(nbk) * 2u + 15u) & ~15u;
+            const bool whole = it.J.cols == KC; // a row is exactly one slot row: one copy
+            const long long o = it.out_row(lane);
+            const bool valid = lane < R && o < it.J.rows;
+            const long long srow = it.J.idx ? src : o;
+            const bool load = valid && srow >= 0 && srow < it.J.src_rows;
+            const uint8_t *mat = it.matrix(lane);
+            const uint32_t bytes = load ? (whole ? uint32_t(it.J.rb) : qbytes + dbytes) : 0u;
+            const uint32_t total = __reduce_add_sync(0xffffffffu, bytes);
+            if (lane < R)
+                rowflag[(s % FRING) * R + lane] = load ? 1 : 0;
+            const int cur_c = it.c;
+            const int cur_cols = it.J.cols;
+            // the next stage's gather index, loaded now so its latency overlaps this stage
+            it.next(p);
+            if (it.valid(p) && lane < R && it.J.idx) {
+                if (it.c == 0) {
+                    const long long on = it.out_row(lane);
+                    src = on < it.J.rows ? (long long)__ldg(it.J.idx + on) : -1;
+                } // a later chunk of the same tile keeps the same row
+            }
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive_expect_tx(&full[slot], total);
+            __syncwarp();
+            if (load) {
+                const uint8_t *row = mat + srow * (long long)q8s_row_bytes(cur_cols);
+                uint8_t *dst = slots + size_t(slot) * SLOT + lane * ROWB;
+                if (whole) {
+                    bulk_g2s(dst, row, bytes, &full[slot], pol);
+                } else {
+                    bulk_g2s(dst, row + cur_c * KC, qbytes, &full[slot], pol);
+                    bulk_g2s(dst + KC, row + cur_cols + (cur_c * KC / Q8_QK) * 2, dbytes, &full[slot], pol);
+                }
+            }
         }
         // Leave no bulk copy in flight: on the normal path the compute threads consumed every
         // stage; after a timeout, wait (bounded) for the most recent fill of each slot.
-        if (!ok)
+        if (!ok && lane == 0)
             for (int k = max(0, s - STAGES); k < s; ++k)
                 if (!mbar_wait(&full[k % STAGES], (k / STAGES) & 1))
                     report(p.err, ERR_TIMEOUT_DRAIN);
@@ -374,7 +425,7 @@ __global__ void __launch_bounds__(NT, 1) gemv_exact_kernel(const __grid_constant
 }
 
 template <int MT>
-cudaError_t launch_mt(const GemvParams &p, int grid, cudaStream_t stream) {
+cudaError_t launch_mt(const GemvParams &p, int grid, cudaStream_t stream, bool pdl) {
     const size_t smem = smem_bytes<MT>();
     static bool attr_set = false; // per process; the attribute is per function
     if (!attr_set) {
@@ -383,13 +434,22 @@ cudaError_t launch_mt(const GemvParams &p, int grid, cudaStream_t stream) {
             return e;
         attr_set = true;
     }
-    gemv_exact_kernel<MT><<<grid, NT, smem, stream>>>(p);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(NT);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemv_exact_kernel<MT>, p);
 }
 
 } // namespace
 
-cudaError_t launch_gemv(GemvParams &p, int num_sms, int grid_limit, cudaStream_t stream) {
+cudaError_t launch_gemv(GemvParams &p, int num_sms, int grid_limit, cudaStream_t stream, bool pdl) {
     if (p.njobs < 1 || p.njobs > MAX_JOBS)
         return cudaErrorInvalidValue;
     const int m = p.job[0].m;
@@ -410,10 +470,10 @@ cudaError_t launch_gemv(GemvParams &p, int num_sms, int grid_limit, cudaStream_t
     if (grid > tiles)
         grid = tiles;
     switch (m) {
-    case 1: return launch_mt<1>(p, grid, stream);
-    case 2: return launch_mt<2>(p, grid, stream);
-    case 3: return launch_mt<3>(p, grid, stream);
-    default: return launch_mt<4>(p, grid, stream);
+    case 1: return launch_mt<1>(p, grid, stream, pdl);
+    case 2: return launch_mt<2>(p, grid, stream, pdl);
+    case 3: return launch_mt<3>(p, grid, stream, pdl);
+    default: return launch_mt<4>(p, grid, stream, pdl);
     }
 }
 

@@ -32,12 +32,14 @@ struct GemvParams {
     GemvJob job[MAX_JOBS];
     int njobs;
     int total_tiles;
+    int early;     // 1: weights may stream in before the previous kernel on the stream completes
     unsigned *err; // the context's device error word
 };
 
 // Launches the exact CUDA-core product over p.job[0..njobs) (all with the same m). Fills the
-// tile fields. grid_limit 0 = one CTA per SM.
-cudaError_t launch_gemv(GemvParams &p, int num_sms, int grid_limit, cudaStream_t stream);
+// tile fields. grid_limit 0 = one CTA per SM. pdl: launch with programmatic stream serialization
+// (the kernel overlaps the previous one's tail and waits for it before reading x or idx).
+cudaError_t launch_gemv(GemvParams &p, int num_sms, int grid_limit, cudaStream_t stream, bool pdl);
 
 // ---- the tensor-core gemm (t >= 16): y[t][o] = sum_k fp16(W)[o][k] * fp16(x)[t][k], fp32 sums
 struct GemmJob {
@@ -55,7 +57,7 @@ struct GemmJob {
 size_t gemm_tc_scratch_bytes(const GemmJob *jobs, int n);
 // Up to 8 jobs in one persistent launch (plus one fp16 conversion of each x).
 cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scratch_bytes, int num_sms,
-                           unsigned *err, cudaStream_t stream);
+                           unsigned *err, cudaStream_t stream, bool pdl);
 
 // ---- utilities
 cudaError_t launch_repack(const uint8_t *gguf, long long rows, int cols, uint8_t *out, cudaStream_t stream);

@@ -91,6 +91,12 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// Programmatic dependent launch: let the next kernel on the stream start its prologue now, and
+// (in the next kernel) wait until the previous kernel has completed and its writes are visible.
+// Both are no-ops when the kernel was not launched with programmatic stream serialization.
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void grid_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void report(unsigned *err, unsigned bits) {
     if (err)
         atomicOr(err, bits);

@@ -35,6 +35,7 @@ struct Ctx {
     int device = 0, num_sms = 148;
     cudaStream_t own_stream = nullptr, stream = nullptr;
     bool async = false;
+    bool overlap = false; // weights are read-only between products: prefetch them early (PDL)
     unsigned *d_err = nullptr;
     int status = RTB_OK;
     char msg[256] = {0};
@@ -142,6 +143,7 @@ bool flush_gemv(Ctx *c, std::vector<q8::GemvJob> &jobs) {
         q8::GemvParams p;
         memset(&p, 0, sizeof p);
         p.err = c->d_err;
+        p.early = c->overlap ? 1 : 0;
         std::vector<q8::GemvJob> rest;
         for (const q8::GemvJob &j : jobs) {
             if (j.m == m && p.njobs < q8::MAX_JOBS)
@@ -149,7 +151,7 @@ bool flush_gemv(Ctx *c, std::vector<q8::GemvJob> &jobs) {
             else
                 rest.push_back(j);
         }
-        if (!cuda_ok(c, q8::launch_gemv(p, c->num_sms, 0, c->stream), "gemv launch"))
+        if (!cuda_ok(c, q8::launch_gemv(p, c->num_sms, 0, c->stream, c->overlap), "gemv launch"))
             return false;
         jobs.swap(rest);
     }
@@ -177,7 +179,8 @@ bool flush_tc(Ctx *c, std::vector<q8::GemmJob> &jobs) {
         const size_t need = q8::gemm_tc_scratch_bytes(&jobs[i], n);
         if (!ensure_scratch(c, need))
             return false;
-        if (!cuda_ok(c, q8::launch_gemm_tc(&jobs[i], n, c->scratch, c->scratch_bytes, c->num_sms, c->d_err, c->stream),
+        if (!cuda_ok(c, q8::launch_gemm_tc(&jobs[i], n, c->scratch, c->scratch_bytes, c->num_sms, c->d_err, c->stream,
+                                           c->overlap),
                      "tensor-core gemm launch"))
             return false;
     }
@@ -506,6 +509,12 @@ int rt_b200_last_error(struct rt *R, char *msg, size_t n) {
     *status = RTB_OK;
     m[0] = 0;
     return s;
+}
+
+void rt_b200_set_overlap(struct rt *R, int on) {
+    Ctx *c = ctx_of(R);
+    if (c)
+        c->overlap = on != 0;
 }
 
 void rt_b200_set_async(struct rt *R, int on) {

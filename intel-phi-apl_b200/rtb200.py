@@ -25,7 +25,7 @@ ERRORS = {1: "RTB_EINVAL", 2: "RTB_ECUDA", 3: "RTB_EKERNEL", 4: "RTB_ENOMEM", 5:
 # The entry points include/rt_b200.h declares, all of which the library must export.
 EXPORTS = ("rt_init", "rt_gemv", "rt_gemv_q", "rt_gemv_open", "rt_gemv_go", "rt_gemm", "rt_gemm_q", "rt_q8_row",
            "gemv_s_bytes", "gemv_s_repack", "rt_gemm_silu_q", "rt_gemm_silu", "rt_gemv_rows_q", "rt_gemv_rows",
-           "rt_b200_last_error", "rt_b200_set_async", "rt_b200_sync", "rt_b200_stream", "rt_b200_set_stream",
+           "rt_b200_last_error", "rt_b200_set_overlap", "rt_b200_set_async", "rt_b200_sync", "rt_b200_stream", "rt_b200_set_stream",
            "rt_b200_free", "rt_b200_nccl_id", "rt_b200_shard", "rtb_synth_q8_0", "rtb_synth_f32")
 
 
@@ -72,6 +72,7 @@ def load() -> C.CDLL:
         "rt_gemv_rows": ([R, _P, _L, _P, _L, _L, _P, _P], None),
         "rt_b200_last_error": ([R, C.c_char_p, C.c_size_t], C.c_int),
         "rt_b200_set_async": ([R, C.c_int], None),
+        "rt_b200_set_overlap": ([R, C.c_int], None),
         "rt_b200_sync": ([R], C.c_int),
         "rt_b200_stream": ([R], _P),
         "rt_b200_set_stream": ([R, _P], None),
@@ -201,6 +202,10 @@ class Runtime:
     # -- controls
     def set_async(self, on: bool) -> None:
         self.lib.rt_b200_set_async(self._ref, 1 if on else 0)
+
+    def set_overlap(self, on: bool) -> None:
+        """Weights are read-only between products: launch products so they overlap (PDL)."""
+        self.lib.rt_b200_set_overlap(self._ref, 1 if on else 0)
 
     def sync(self) -> None:
         code = self.lib.rt_b200_sync(self._ref)

@@ -373,3 +373,39 @@ def test_tensor_core_round_mixed_with_cuda_core(cuda, runtime, rtb, oracle):
     assert bits_equal(y1.cpu().numpy(), want[0])
     assert bits_equal(y2.cpu().numpy(), want[:2])
     assert rel_err(y24.cpu().numpy(), want) < TC_TOL
+
+
+@pytest.mark.parametrize("overlap", [False, True])
+def test_dependent_chain_async(cuda, rtb, oracle, overlap):
+    """Products whose x is the previous product's y, enqueued back to back (async; with overlap the
+    kernels are launched so that the next one streams its weights while the previous finishes):
+    every y must still see its x complete."""
+    rows = cols = 4096
+    a = Mat(cuda, rtb, oracle, rows, cols, 141)
+    b = Mat(cuda, rtb, oracle, rows, cols, 142)
+    x = xs(oracle, 16, cols, 143)
+    rt = rtb.Runtime()
+    try:
+        rt.set_async(True)
+        rt.set_overlap(overlap)
+        xd = dev(cuda, x)
+        ys = [cuda.empty((16, rows), dtype=cuda.float32, device="cuda") for _ in range(4)]
+        # t = 1 chain: x -> A -> B -> A -> B
+        rt.gemv(a.ptr, rows, cols, xd[0].data_ptr(), ys[0][0].data_ptr())
+        rt.gemv(b.ptr, rows, cols, ys[0][0].data_ptr(), ys[1][0].data_ptr())
+        rt.gemv(a.ptr, rows, cols, ys[1][0].data_ptr(), ys[2][0].data_ptr())
+        rt.gemv(b.ptr, rows, cols, ys[2][0].data_ptr(), ys[3][0].data_ptr())
+        rt.sync()
+        want = x[0]
+        for k, m in enumerate([a, b, a, b]):
+            want = oracle.gemv(m.q8, rows, cols, want)
+            assert bits_equal(ys[k][0].cpu().numpy(), want), k
+        # t = 16 chain on the tensor cores: X -> A -> B
+        rt.gemm(a.ptr, rows, cols, xd.data_ptr(), 16, ys[0].data_ptr())
+        rt.gemm(b.ptr, rows, cols, ys[0].data_ptr(), 16, ys[1].data_ptr())
+        rt.sync()
+        y0 = ys[0].cpu().numpy()
+        assert rel_err(y0, oracle.gemm(a.q8, rows, cols, x, 16)) < TC_TOL
+        assert rel_err(ys[1].cpu().numpy(), oracle.gemm(b.q8, rows, cols, y0, 16)) < TC_TOL
+    finally:
+        rt.close()
