@@ -111,6 +111,17 @@ RTB_API void rt_gemv_rows_q(struct rt *R, const void *w, long w_rows, const int3
 RTB_API void rt_gemv_rows(struct rt *R, const void *w, long w_rows, const int32_t *idx, long n, long cols,
                           const float *x, float *y);
 
+/* No counterpart in the reference. The tensor-core product of rt_gemm (t >= 16 tokens, same kernel
+ * and same results) for callers that cannot allocate device memory: engines that reserve all of
+ * HBM up front or forbid allocation while serving. It needs no rt_init, and its scratch (the fp16
+ * copy of x) is a fixed 8 MiB device array inside this library, so t * cols must be <= 4,194,304;
+ * larger calls return RTB_EINVAL. Runs on `stream` (a cudaStream_t; NULL is the legacy default
+ * stream) and returns after the product is in y: RTB_OK, or RTB_EINVAL / RTB_ECUDA / RTB_EKERNEL.
+ * The first call on a device looks up that array's device address: make it before any stream
+ * capture. All calls share the array, so calls that overlap on the GPU (two threads or two
+ * streams at once) race and must not be made. */
+RTB_API int rt_gemm_static(const void *w, long rows, long cols, const float *x, long t, float *y, void *stream);
+
 /* ---------------------------------------------------------------- B200 runtime controls */
 
 enum {
