@@ -45,7 +45,7 @@ import workload as WL  # noqa: E402
 SEED = 20261201
 METRIC = "Q8_0 weight-product GB/s, 9B decode step (M=1)"
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
-TRAFFIC_PATH = os.path.join(ROOT, "profiles", "gemv_exact_head_traffic.json")
+TRAFFIC_PATH = os.path.join(ROOT, "profiles", "gemv_exact_head_151936x4096.md")
 
 
 def log(*a):
@@ -296,12 +296,13 @@ class Bench:
         dur = statistics.mean(a.elapsed_time(b) for a, b in ev) / 1e3
         nbytes = n * WL.D * 34 // 32 + 4 * WL.D + 4 * n
         peak, how = peaks()
-        traffic = None
+        traffic = None  # ncu dram read+write of one full-head launch, scaled to this shard's rows
         try:
             with open(TRAFFIC_PATH) as f:
-                tr = json.load(f)
-            traffic = tr["dram_bytes_per_row"] * n + tr.get("dram_bytes_fixed", 0)
-        except (OSError, KeyError, ValueError):
+                for line in f:
+                    if line.startswith("traffic_bytes_per_launch:"):
+                        traffic = int(int(line.split(":")[1]) * n / WL.VOCAB)
+        except (OSError, ValueError):
             pass
         achieved = nbytes / dur / 1e9
         return {"kernel": "gemv_exact_kernel<1>", "shape": f"{n}x{WL.D} M=1 (output head shard)", "bound": "hbm",

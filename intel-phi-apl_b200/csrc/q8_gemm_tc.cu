@@ -18,7 +18,7 @@
 //   warp 9      MMA: 4 x tcgen05.mma (M=128, N=BN, K=16) per stage into one of two TMEM
 //               accumulators; tcgen05.commit frees the stage, and at a tile's end the accumulator;
 //   warps 0-3   epilogue: tcgen05.ld of TMEM lanes 32*(warp%4).. -> y (or silu(g)*u for a pair).
-// Every wait is bounded (error word on timeout); no multicast anywhere.
+// Every wait is bounded (error word on timeout); every TMA load is a plain single-CTA load.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>

@@ -1,6 +1,6 @@
 // q8_ptx.cuh: the sm_100a PTX this library's kernels are built from: mbarriers, 1-D bulk
 // (TMA) copies, L2 cache policies, a bounded wait and the error word. Only plain
-// (non-multicast) bulk loads from this GPU's own memory appear here.
+// single-CTA bulk loads from this GPU's own memory appear here.
 #pragma once
 #include <cstdint>
 

@@ -1,0 +1,134 @@
+"""Row sharding over ranks (CPU, gloo, world size 2).
+
+The library's multi-GPU contract (include/rt_b200.h, rt_b200_shard): with `world` ranks, rank k
+holds rows [k*rows/world, (k+1)*rows/world) of every matrix, computes those outputs, and an
+all-gather in rank order rebuilds the whole y on every rank. These tests run that contract on CPU
+ranks with the oracle as the per-rank product and gloo as the collective, and check the rebuilt y
+is the unsharded product bit for bit; bench.py shards the same way (workload.shard_rows).
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import ORACLE, PKG
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank: int, world: int, port: int, case: dict, out) -> None:
+    import sys
+    sys.path.insert(0, ORACLE)
+    sys.path.insert(0, PKG)
+    import oracle as O
+    import workload as WL
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rows, cols, t = case["rows"], case["cols"], case["t"]
+        r0, n = WL.shard_rows(rows, rank, world)
+        q8 = O.synth_q8_0(n, cols, 7, 3, row0=r0)  # this rank's shard only
+        x = np.stack([O.synth_f32(cols, 7, 4 + k) for k in range(t)])
+        y_local = O.gemm(q8, n, cols, x, t, threads=2)  # [t][n]
+        parts = [torch.empty((t, n), dtype=torch.float32) for _ in range(world)]
+        dist.all_gather(parts, torch.from_numpy(y_local))
+        y = torch.cat(parts, dim=1).numpy()  # [t][rows], ranks' slices in rank order
+        if rank == 0:
+            out.put(y)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case", [{"rows": 64, "cols": 256, "t": 1}, {"rows": 96, "cols": 512, "t": 3}])
+def test_row_shards_all_gather_rebuild_the_product(case, oracle):
+    world = 2
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, case, out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    y = out.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    q8 = oracle.synth_q8_0(case["rows"], case["cols"], 7, 3)
+    x = np.stack([oracle.synth_f32(case["cols"], 7, 4 + k) for k in range(case["t"])])
+    want = oracle.gemm(q8, case["rows"], case["cols"], x, case["t"])
+    assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
+
+
+def test_shard_rows_partition():
+    import workload as WL
+    for rows, world in [(4096, 1), (4096, 2), (151936, 8), (12288, 4)]:
+        parts = [WL.shard_rows(rows, k, world) for k in range(world)]
+        assert parts[0][0] == 0 and sum(n for _, n in parts) == rows
+        assert all(parts[k][0] + parts[k][1] == parts[k + 1][0] for k in range(world - 1))
+    with pytest.raises(ValueError):
+        WL.shard_rows(100, 0, 8)
+
+
+def test_every_baseline_shape_shards_over_8():
+    import workload as WL
+    for p in WL.SWEEP + [WL.DRAFT]:
+        for world in (2, 4, 8):
+            WL.shard_rows(p.rows, 0, world)
+
+
+def _gpu_rank_main(rank: int, world: int, nid: bytes, out) -> None:
+    import sys
+    sys.path.insert(0, ORACLE)
+    sys.path.insert(0, PKG)
+    import oracle as O
+    import rtb200
+    import workload as WL
+    torch.cuda.set_device(rank)
+    rows, cols, t = 8192, 4096, 2
+    r0, n = WL.shard_rows(rows, rank, world)
+    w = torch.empty(rtb200.gemv_s_bytes(n, cols), dtype=torch.uint8, device="cuda")
+    rtb200.synth_q8_0(w.data_ptr(), r0, n, cols, 11, 5)
+    x = torch.from_numpy(np.stack([O.synth_f32(cols, 11, 6 + k) for k in range(t)])).cuda()
+    y = torch.full((t, rows), float("nan"), dtype=torch.float32, device="cuda")
+    y1 = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
+    with rtb200.Runtime() as rt:
+        rt.shard(rank, world, nid)
+        rt.gemm(w.data_ptr(), rows, cols, x.data_ptr(), t, y.data_ptr())
+        rt.gemv(w.data_ptr(), rows, cols, x.data_ptr(), y1.data_ptr())
+    out.put((rank, y.cpu().numpy(), y1.cpu().numpy()))
+
+
+@pytest.mark.gpu
+def test_nccl_row_shards_on_two_gpus(cuda, rtb, oracle):
+    """rt_b200_shard on 2 GPUs: each rank computes its rows, NCCL all-gathers y; every rank
+    ends with the whole product, bit for bit."""
+    if cuda.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 2
+    nid = rtb.nccl_id()
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    procs = [ctx.Process(target=_gpu_rank_main, args=(r, world, nid, out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [out.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    rows, cols, t = 8192, 4096, 2
+    q8 = oracle.synth_q8_0(rows, cols, 11, 5)
+    x = np.stack([oracle.synth_f32(cols, 11, 6 + k) for k in range(t)])
+    want = oracle.gemm(q8, rows, cols, x, t)
+    for _, y, y1 in res:
+        assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
+        assert np.array_equal(y1.view(np.uint32), want[0].view(np.uint32))
