@@ -34,7 +34,11 @@ constexpr int R = 8;               // rows per tile / stage
 constexpr int KC = 4096;           // columns per stage
 constexpr int NBK = KC / Q8_QK;    // blocks per stage: 128
 constexpr int STAGES = 4;
-constexpr int TBUF = 4;            // partial-sum buffers: compute may run this far ahead of the chain
+// Partial-sum buffers: compute may run this many stages ahead of the chain warps. Eight for one
+// token (they absorb the chain's jitter); four when the tokens' partial sums fill the space.
+template <int MT>
+constexpr int tbuf() { return MT == 1 ? 8 : 4; }
+constexpr int MAX_TBUF = 8;
 constexpr int NC = 256;            // compute threads: (block column, row half) each
 constexpr int NH = R / 2;          // rows per compute thread
 constexpr int NCHAIN = 2;          // chain warps: tile i of the CTA goes to chain warp i % NCHAIN
@@ -52,11 +56,12 @@ static_assert(ROWB % 16 == 0 && SLOT % 16 == 0, "bulk copy destinations are 16-b
 // s-STAGES-1, whose partial-sum wait means the chain finished stage s-STAGES-1-TBUF: a ring of
 // 16 entries is never overwritten while read.
 constexpr int FRING = 16;
-static_assert(FRING >= STAGES + TBUF + 2, "row-flag ring");
+static_assert(FRING >= STAGES + MAX_TBUF + 2, "row-flag ring");
 
 template <int MT>
 constexpr size_t smem_bytes() {
-    return size_t(STAGES) * SLOT + size_t(TBUF) * (MT + 1) * R * TPAD * 4 + (STAGES * 2 + TBUF * 2) * 8 + FRING * R;
+    return size_t(STAGES) * SLOT + size_t(tbuf<MT>()) * (MT + 1) * R * TPAD * 4 + (STAGES * 2 + tbuf<MT>() * 2) * 8 +
+           FRING * R;
 }
 
 // One job's fields, cached in registers by every role when its stage sequence enters the job:
@@ -177,6 +182,7 @@ __device__ __forceinline__ void block_chains(const uint32_t (&wq)[RG][8], const 
 
 template <int MT>
 __global__ void __launch_bounds__(NT, 1) gemv_exact_kernel(const __grid_constant__ GemvParams p) {
+    constexpr int TBUF = tbuf<MT>();
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t *slots = smem;
     float *T = reinterpret_cast<float *>(smem + size_t(STAGES) * SLOT); // [TBUF][MT][R][TPAD]
