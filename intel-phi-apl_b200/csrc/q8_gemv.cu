@@ -45,11 +45,15 @@ constexpr int NCHAIN = 2;          // chain warps: tile i of the CTA goes to cha
 constexpr int CHAIN_WARP = NC / 32; // the first chain warp; the copy warp follows the chain warps
 constexpr int COPY_WARP = CHAIN_WARP + NCHAIN;
 constexpr int NT = NC + 32 * NCHAIN + 32;
-constexpr int ROWB = KC + NBK * 2; // a row's slot: quants then scales, 4352 B
+// A row's slot: quants, scales, then 16 bytes of padding (4368 B). The padding puts neighbouring
+// rows 16 bytes apart in the bank space, so a warp reading two rows at once (lanes with b & 4 read
+// the other row of a pair) touches eight distinct 16-byte bank groups per quarter-warp.
+constexpr int ROWB = KC + NBK * 2 + 16;
 constexpr int SLOT = R * ROWB;
 constexpr int TPAD = NBK + 4;      // partial-sum row stride (floats): 16-byte rows, conflict-free per lane = row
 static_assert(NC == 2 * NBK, "two compute threads (row halves) per block column of a stage");
 static_assert(ROWB % 16 == 0 && SLOT % 16 == 0, "bulk copy destinations are 16-byte aligned");
+static_assert(ROWB % 128 == 16, "a row pair's two rows sit in different bank groups");
 
 // Per-stage row flags (row loaded or not), written by the copy warp, read by the chain warp. When
 // the copy warp fills stage s, compute has released stage s-STAGES, so it has finished stage
@@ -242,8 +246,13 @@ __global__ void __launch_bounds__(NT, 1) gemv_exact_kernel(const __grid_constant
                 }
             }
             constexpr int RG = row_group<MT>();
+            static_assert(RG % 2 == 0, "row pairs stay inside one row group");
             const uint8_t *qbase = slots + size_t(slot) * SLOT + b * Q8_QK; // row r's block b: + r*ROWB
             const uint8_t *dbase = slots + size_t(slot) * SLOT + KC + 2 * b; // row r's scale b: + r*ROWB
+            // Lanes with b & 4 take each row pair in the other order (register k holds row k ^ 1):
+            // their 32-byte blocks would otherwise share banks with lanes b - 4 of the same row.
+            const int rot = (b >> 2) & 1;
+            const uint8_t *qeven = qbase + rot * ROWB, *qodd = qbase - rot * ROWB;
             float *Tb = T + tb * MT * R * TPAD;
             float *TDb = TD + tb * R * TPAD;
             bool ok = true;
@@ -255,8 +264,9 @@ __global__ void __launch_bounds__(NT, 1) gemv_exact_kernel(const __grid_constant
 #pragma unroll
                     for (int k = 0; k < RG; ++k) {
                         const int r = half * NH + g * RG + k;
-                        const uint4 q0 = *reinterpret_cast<const uint4 *>(qbase + r * ROWB);
-                        const uint4 q1 = *reinterpret_cast<const uint4 *>(qbase + r * ROWB + 16);
+                        const uint8_t *qr = ((k & 1) ? qodd : qeven) + r * ROWB; // row r ^ rot
+                        const uint4 q0 = *reinterpret_cast<const uint4 *>(qr);
+                        const uint4 q1 = *reinterpret_cast<const uint4 *>(qr + 16);
                         wq[k][0] = q0.x ^ 0x80808080u;
                         wq[k][1] = q0.y ^ 0x80808080u;
                         wq[k][2] = q0.z ^ 0x80808080u;
@@ -283,7 +293,7 @@ __global__ void __launch_bounds__(NT, 1) gemv_exact_kernel(const __grid_constant
                         const int r = half * NH + g * RG + k;
 #pragma unroll
                         for (int mt = 0; mt < MT; ++mt)
-                            Tb[(mt * R + r) * TPAD + b] = t[mt][k];
+                            Tb[(mt * R + r) * TPAD + b] = rot ? t[mt][k ^ 1] : t[mt][k];
                         TDb[r * TPAD + b] = dv[k];
                     }
                 }
