@@ -133,10 +133,13 @@ struct StageIter {
 
 
 
-// Rows processed side by side by one compute thread: its 4 for one or two tokens; 2 at a time
-// for three or four (the x registers grow with the tokens).
+// Rows processed side by side by one compute thread. Two at a time for one token: the second
+// pair's shared-memory reads then overlap the first pair's chains in the other warps (all eight
+// compute warps wait on the same stage, so one load phase per stage would leave the ALUs idle
+// while shared memory serves every warp). All 4 for two tokens (the pair of tokens already
+// gives each quant two uses); 2 at a time for three or four (the x registers grow).
 template <int MT>
-constexpr int row_group() { return MT <= 2 ? NH : NH / 2; }
+constexpr int row_group() { return MT == 2 ? NH : NH / 2; }
 
 // The RG rows' 32-step chains of one block for MT tokens. MT == 1: rows in packed pairs
 // (fma.rn.f32x2 and add.rn.f32x2: two independent IEEE operations). MT > 1: scalar.
