@@ -13,12 +13,13 @@
 //   warps 0-7  compute: thread j owns 32-column block j % 128 and row half j / 128 of the stage;
 //              it keeps that block's x in registers, pulls its 4 rows' 32 quants and scales out
 //              of the slot (then frees the slot) and runs the 4 rows' 32-fma chains side by side
-//              (packed in row pairs); the t_b and fp32 scales go to a partial-sum buffer. Two
-//              warps per SM sub-partition, each on a ~5 KB loop body, keep the issue slots busy;
-//   warps 8-9  chain: one lane per (token, row) runs acc = fma(t_b, d_b, acc) in block order and
-//              writes y (for a SwiGLU pair: silu(gate) * up). The chain is serial per row, so
-//              the CTA's tiles alternate between the two chain warps (a tile's chunks stay on one);
-//   warp 10    copies: issues a stage's bulk copies as soon as its slot is free.
+//              (packed in row pairs); the t_b and fp32 scales go to a partial-sum buffer;
+//   chain      one or two warps (Cfg): one lane per (token, row) runs acc = fma(t_b, d_b, acc) in
+//              block order and writes y (for a SwiGLU pair: silu(gate) * up). The chain is serial
+//              per row, so the CTA's tiles alternate between the chain warps (a tile's chunks
+//              stay on one);
+//   last warp  copies: issues a stage's bulk copies as soon as its slot is free.
+// One token runs two CTAs per SM, more tokens one (Cfg).
 // Barriers: full (copies landed), empty (slot read), tfull/tempty (partial sums). Every wait is
 // bounded: a timeout sets a bit in the context's error word and the CTA leaves.
 #include <cuda_fp16.h>
@@ -33,18 +34,31 @@ namespace {
 constexpr int R = 8;               // rows per tile / stage
 constexpr int KC = 4096;           // columns per stage
 constexpr int NBK = KC / Q8_QK;    // blocks per stage: 128
-constexpr int STAGES = 4;
-// Partial-sum buffers: compute may run this many stages ahead of the chain warps. Eight for one
-// token (they absorb the chain's jitter); four when the tokens' partial sums fill the space.
-template <int MT>
-constexpr int tbuf() { return MT == 1 ? 8 : 4; }
-constexpr int MAX_TBUF = 8;
 constexpr int NC = 256;            // compute threads: (block column, row half) each
 constexpr int NH = R / 2;          // rows per compute thread
-constexpr int NCHAIN = 2;          // chain warps: tile i of the CTA goes to chain warp i % NCHAIN
 constexpr int CHAIN_WARP = NC / 32; // the first chain warp; the copy warp follows the chain warps
-constexpr int COPY_WARP = CHAIN_WARP + NCHAIN;
-constexpr int NT = NC + 32 * NCHAIN + 32;
+
+// The CTA's shape: CTAS CTAs per SM.
+//   CTAS = 2 (one token, long launches): 320 threads, <= 102 registers and ~104 KB of shared
+//   memory each, with a 2-stage ring, 4 partial-sum buffers and one chain warp. The SM holds 4
+//   stages in flight as with one CTA, and the two CTAs' load and chain phases interleave instead
+//   of every compute warp of the SM waiting on the same stage (the output head streams ~10%
+//   faster). A CTA that finishes frees half an SM for the next kernel on the stream.
+//   CTAS = 1: a 4-stage ring, two chain warps, and 8 partial-sum buffers for one token (they
+//   absorb the chain's jitter), 4 for more (their partial sums fill the space). Launches of a
+//   few stages per SM run faster so: each CTA has more stages in flight and chain warps.
+template <int MT, int CTAS_>
+struct Cfg {
+    static_assert(CTAS_ == 1 || (CTAS_ == 2 && MT == 1), "two CTAs per SM for one token only");
+    static constexpr int CTAS = CTAS_;
+    static constexpr int STAGES = CTAS == 2 ? 2 : 4;                  // weight slots
+    static constexpr int TBUF = CTAS == 2 ? 4 : (MT == 1 ? 8 : 4);    // partial-sum buffers
+    static constexpr int NCHAIN = CTAS == 2 ? 1 : 2;                  // tile i of the CTA -> chain warp i % NCHAIN
+    static constexpr int COPY_WARP = CHAIN_WARP + NCHAIN;
+    static constexpr int NT = NC + 32 * NCHAIN + 32;                  // threads
+};
+// One-token launches with at least this many stages per SM run two CTAs per SM.
+constexpr int TWO_CTA_MIN_STAGES_PER_SM = 12;
 // A row's slot: quants, scales, then 16 bytes of padding (4368 B). The padding puts neighbouring
 // rows 16 bytes apart in the bank space, so a warp reading two rows at once (lanes with b & 4 read
 // the other row of a pair) touches eight distinct 16-byte bank groups per quarter-warp.
@@ -60,11 +74,12 @@ static_assert(ROWB % 128 == 16, "a row pair's two rows sit in different bank gro
 // s-STAGES-1, whose partial-sum wait means the chain finished stage s-STAGES-1-TBUF: a ring of
 // 16 entries is never overwritten while read.
 constexpr int FRING = 16;
-static_assert(FRING >= STAGES + MAX_TBUF + 2, "row-flag ring");
 
-template <int MT>
+template <int MT, int CTAS>
 constexpr size_t smem_bytes() {
-    return size_t(STAGES) * SLOT + size_t(tbuf<MT>()) * (MT + 1) * R * TPAD * 4 + (STAGES * 2 + tbuf<MT>() * 2) * 8 +
+    using C = Cfg<MT, CTAS>;
+    static_assert(FRING >= C::STAGES + C::TBUF + 2, "row-flag ring");
+    return size_t(C::STAGES) * SLOT + size_t(C::TBUF) * (MT + 1) * R * TPAD * 4 + (C::STAGES * 2 + C::TBUF * 2) * 8 +
            FRING * R;
 }
 
@@ -187,9 +202,10 @@ __device__ __forceinline__ void block_chains(const uint32_t (&wq)[RG][8], const 
     }
 }
 
-template <int MT>
-__global__ void __launch_bounds__(NT, 1) gemv_exact_kernel(const __grid_constant__ GemvParams p) {
-    constexpr int TBUF = tbuf<MT>();
+template <int MT, int CTAS>
+__global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(const __grid_constant__ GemvParams p) {
+    using C = Cfg<MT, CTAS>;
+    constexpr int STAGES = C::STAGES, TBUF = C::TBUF, NCHAIN = C::NCHAIN, COPY_WARP = C::COPY_WARP;
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t *slots = smem;
     float *T = reinterpret_cast<float *>(smem + size_t(STAGES) * SLOT); // [TBUF][MT][R][TPAD]
@@ -443,19 +459,32 @@ __global__ void __launch_bounds__(NT, 1) gemv_exact_kernel(const __grid_constant
     }
 }
 
-template <int MT>
-cudaError_t launch_mt(const GemvParams &p, int grid, cudaStream_t stream, bool pdl) {
-    const size_t smem = smem_bytes<MT>();
-    static bool attr_set = false; // per process; the attribute is per function
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_exact_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+template <int MT, int CTAS>
+cudaError_t launch_mt(const GemvParams &p, int num_sms, int grid_limit, cudaStream_t stream, bool pdl) {
+    using C = Cfg<MT, CTAS>;
+    const size_t smem = smem_bytes<MT, CTAS>();
+    static int per_sm = 0; // CTAs that fit on one SM (per process; the attribute is per function)
+    if (per_sm == 0) {
+        cudaError_t e =
+            cudaFuncSetAttribute(gemv_exact_kernel<MT, CTAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
         if (e != cudaSuccess)
             return e;
-        attr_set = true;
+        int n = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_exact_kernel<MT, CTAS>, C::NT, smem);
+        if (e != cudaSuccess)
+            return e;
+        if (n < 1)
+            return cudaErrorInvalidConfiguration;
+        per_sm = n < CTAS ? n : CTAS;
     }
+    int grid = per_sm * (num_sms > 0 ? num_sms : 148);
+    if (grid_limit > 0 && grid > grid_limit)
+        grid = grid_limit;
+    if (grid > p.total_tiles)
+        grid = p.total_tiles;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(NT);
+    cfg.blockDim = dim3(C::NT);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -463,7 +492,7 @@ cudaError_t launch_mt(const GemvParams &p, int grid, cudaStream_t stream, bool p
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_exact_kernel<MT>, p);
+    return cudaLaunchKernelEx(&cfg, gemv_exact_kernel<MT, CTAS>, p);
 }
 
 } // namespace
@@ -473,6 +502,7 @@ cudaError_t launch_gemv(GemvParams &p, int num_sms, int grid_limit, cudaStream_t
         return cudaErrorInvalidValue;
     const int m = p.job[0].m;
     int tiles = 0;
+    long long stages = 0;
     for (int j = 0; j < p.njobs; ++j) {
         GemvJob &J = p.job[j];
         if (J.m != m || J.m < 1 || J.m > GEMV_MAX_T || J.cols < Q8_QK || J.cols % Q8_QK || J.rows < 1)
@@ -481,18 +511,17 @@ cudaError_t launch_gemv(GemvParams &p, int num_sms, int grid_limit, cudaStream_t
         J.tiles = int((J.rows + rpt - 1) / rpt);
         J.tile0 = tiles;
         tiles += J.tiles;
+        stages += (long long)J.tiles * ((J.cols + KC - 1) / KC);
     }
     p.total_tiles = tiles;
-    int grid = num_sms > 0 ? num_sms : 148;
-    if (grid_limit > 0 && grid > grid_limit)
-        grid = grid_limit;
-    if (grid > tiles)
-        grid = tiles;
+    const int sms = num_sms > 0 ? num_sms : 148;
     switch (m) {
-    case 1: return launch_mt<1>(p, grid, stream, pdl);
-    case 2: return launch_mt<2>(p, grid, stream, pdl);
-    case 3: return launch_mt<3>(p, grid, stream, pdl);
-    default: return launch_mt<4>(p, grid, stream, pdl);
+    case 1:
+        return stages >= (long long)TWO_CTA_MIN_STAGES_PER_SM * sms ? launch_mt<1, 2>(p, num_sms, grid_limit, stream, pdl)
+                                                                    : launch_mt<1, 1>(p, num_sms, grid_limit, stream, pdl);
+    case 2: return launch_mt<2, 1>(p, num_sms, grid_limit, stream, pdl);
+    case 3: return launch_mt<3, 1>(p, num_sms, grid_limit, stream, pdl);
+    default: return launch_mt<4, 1>(p, num_sms, grid_limit, stream, pdl);
     }
 }
 

@@ -132,6 +132,22 @@ def test_gemv_bit_exact(cuda, runtime, rtb, oracle, rows, cols):
     assert bits_equal(y.cpu().numpy(), oracle.gemv(m.q8, rows, cols, x[0]))
 
 
+@pytest.mark.parametrize("rows,cols", [
+    (14208, 4096),   # 1776 stages: the smallest one-token launch that runs two CTAs per SM
+    (12288, 8192),   # two CTAs per SM, rows longer than a stage (two chunks each)
+    (14200, 4096),   # 1775 stages: one CTA per SM, just under the switch
+])
+def test_gemv_two_ctas_per_sm(cuda, runtime, rtb, oracle, rows, cols):
+    """Launches long enough to run two CTAs per SM (12 stages per SM on 148 SMs), and the one
+    just under the switch, bit for bit."""
+    m = Mat(cuda, rtb, oracle, rows, cols, 15)
+    x = xs(oracle, 1, cols, 16)
+    xd = dev(cuda, x)
+    y = cuda.full((rows,), float("nan"), dtype=cuda.float32, device="cuda")
+    runtime.gemv(m.ptr, rows, cols, xd.data_ptr(), y.data_ptr())
+    assert bits_equal(y.cpu().numpy(), oracle.gemv(m.q8, rows, cols, x[0]))
+
+
 def test_gemv_output_head_full_size(cuda, runtime, rtb, oracle):
     """BASELINE config 2's output head, 151936 x 4096, every output bit for bit."""
     rows, cols = 151936, 4096
