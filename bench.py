@@ -18,9 +18,10 @@ divided by the step time (CUDA events on the launching stream, max over ranks). 
 
 Also reported (rank 0): the M = 2 verify step; e2e through the C ABI with host buffers (per
 round: pinned H2D of x, the product, D2H of y, as the reference engine crosses its link each
-phase); the config-2 per-shape sweep (N = 1); the roofline of the gemv kernel on the output head;
-the reference's own CPU implementation on a sample (oracle/_ref, N = 1); SM clocks sampled during
-the timed region.
+phase); the config-2 per-shape sweep (N = 1); the config-4 prompt products at M = 16, 40, 512 on the
+tensor-core path (N = 1; TFLOP/s and fraction of the measured bf16 peak; --no-prompt skips it); the
+roofline of the gemv kernel on the output head; the reference's own CPU implementation on a sample
+(oracle/_ref, N = 1); SM clocks sampled during the timed region.
 
 --impl reference: the reference's CPU implementation of the product (its host-model gemv_i_thread
 built from its sources, oracle/_ref) on all host cores, same metric and unit, each step a bounded
@@ -58,6 +59,15 @@ def peaks() -> tuple[float, str]:
             return float(json.load(f)["hbm_gbs"]), "measured"
     except (OSError, KeyError, ValueError):
         return 6650.0, "fallback"
+
+
+def tensor_peak() -> tuple[float, str]:
+    """Dense bf16 TFLOP/s: the burst cuBLAS figure (a kernel timed alone)."""
+    try:
+        with open(PEAKS_PATH) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback"
 
 
 # ---------------------------------------------------------------- the reference's CPU path
@@ -269,6 +279,8 @@ class Bench:
         res["e2e"] = self.e2e(max(3, min(args.steps, 10)), args.warmup)
         if self.world == 1 and self.rank == 0:
             res["sweep"] = self.sweep()
+            if not self.args.no_prompt:
+                res["prompt"] = self.prompt()
         return res
 
     def roofline(self, steps: int) -> dict:
@@ -356,9 +368,89 @@ class Bench:
                 "d2h_bytes_per_step": d2h // steps, "ms_per_step": round(dt * 1e3, 3),
                 "tok_s": round(1.0 / dt, 1), "path": "blocking rt_gemv / rt_gemm_silu per round, pinned host x and y"}
 
+    def _graph(self, fns):
+        """The calls captured as one CUDA graph on a side stream (the runtime follows the stream)."""
+        torch, rt = self.torch, self.rt
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                rt.set_stream(torch.cuda.current_stream().cuda_stream)
+                for f in fns:
+                    f()
+        torch.cuda.current_stream().wait_stream(s)
+        rt.set_stream(torch.cuda.current_stream().cuda_stream)
+        return g
+
+    def _time_graph(self, g, reps: int) -> float:
+        """ms per replay (CUDA events on the current stream), after one untimed replay."""
+        torch = self.torch
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    def prompt(self) -> dict:
+        """the prompt products at M = 16, 40 and 512 tokens on the config-2
+        shapes, through rt_gemm / rt_gemm_silu (the tensor-core path at M >= 16). The 32 layer
+        copies of a shape run back to back as one CUDA graph (weights larger than L2); the head
+        runs twice per graph. M = 512 is judged by TFLOP/s against the measured bf16 peak, M = 16
+        and 40 (HBM-bound) by GB/s against the measured copy bandwidth."""
+        torch, rt = self.torch, self.rt
+        rt.set_async(True)
+        rt.set_stream(torch.cuda.current_stream().cuda_stream)
+        tpeak, tkind = tensor_peak()
+        hpeak, hkind = peaks()
+        out = {"peaks": {"bf16_tflops": tpeak, "hbm_gbs": hpeak, "kind": tkind}}
+        for m in (16, 40, 512):
+            xd = torch.empty(m * WL.D, dtype=torch.float32, device="cuda")
+            xf = torch.empty(m * WL.FF, dtype=torch.float32, device="cuda")
+            self.rtb.synth_f32(xd.data_ptr(), m * WL.D, SEED, 91 + m)
+            self.rtb.synth_f32(xf.data_ptr(), m * WL.FF, SEED, 92 + m)
+            ys = {p.name: torch.empty(m * p.rows, dtype=torch.float32, device="cuda") for p in WL.SWEEP}
+            calls = {
+                "gate_up_silu": lambda L: rt.gemm_silu(L["gate"].data_ptr(), L["up"].data_ptr(), WL.FF, WL.D,
+                                                       xd.data_ptr(), m, ys["gate_up_silu"].data_ptr()),
+                "down": lambda L: rt.gemm(L["down"].data_ptr(), WL.D, WL.FF, xf.data_ptr(), m, ys["down"].data_ptr()),
+                "qkv": lambda L: rt.gemm(L["qkv"].data_ptr(), WL.QKV, WL.D, xd.data_ptr(), m, ys["qkv"].data_ptr()),
+                "out": lambda L: rt.gemm(L["out"].data_ptr(), WL.D, WL.D, xd.data_ptr(), m, ys["out"].data_ptr()),
+            }
+            row = {}
+            tot_f = tot_t = 0.0
+            for p in WL.SWEEP:
+                if p.name == "head":
+                    fns = [lambda: rt.gemm(self.head.data_ptr(), WL.VOCAB, WL.D, xd.data_ptr(), m,
+                                           ys["head"].data_ptr())] * 2
+                else:
+                    fns = [(lambda L=L, p=p: calls[p.name](L)) for L in self.w]
+                for f in fns[:2]:  # eager first: kernel attributes and scratch
+                    f()
+                torch.cuda.synchronize()
+                g = self._graph(fns)
+                us = self._time_graph(g, 2) * 1e3 / len(fns)
+                del g
+                fl, by = p.flops(m), p.bytes(m)
+                tot_f += fl * len(fns)
+                tot_t += us * len(fns)
+                row[p.name] = {"us": round(us, 2), "TFLOP_s": round(fl / us / 1e6, 1), "GB_s": round(by / us / 1e3, 1),
+                               "tensor_frac": round(fl / us / 1e6 / tpeak, 3), "hbm_frac": round(by / us / 1e3 / hpeak, 3)}
+            row["all_shapes"] = {"TFLOP_s": round(tot_f / tot_t / 1e6, 1),
+                                 "tensor_frac": round(tot_f / tot_t / 1e6 / tpeak, 3)}
+            out[f"m{m}"] = row
+            del xd, xf, ys
+        rt.sync()
+        return out
+
     def sweep(self) -> dict:
         """each decode shape alone, GB/s. The 32 layer copies of a shape run
-        back to back (1.1-3.4 GB: larger than L2); the head is one 661 MB matrix."""
+        back to back as one CUDA graph (1.1-3.4 GB: larger than L2); the head is one 661 MB matrix,
+        8 launches per graph."""
         torch, rt = self.torch, self.rt
         rt.set_async(True)
         rt.set_stream(torch.cuda.current_stream().cuda_stream)
@@ -376,16 +468,12 @@ class Bench:
                 fn = [lambda: rt.gemv(self.head.data_ptr(), WL.VOCAB, WL.D, xd, y[("head", 1)].data_ptr())] * 8
             else:
                 fn = [(lambda L=L: calls[p.name](L)) for L in self.w]
-            for f in fn:
+            for f in fn:  # eager once (kernel attributes), then the launches as one CUDA graph
                 f()
             torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for f in fn:
-                f()
-            e1.record()
-            torch.cuda.synchronize()
-            us = e0.elapsed_time(e1) * 1e3 / len(fn)
+            g = self._graph(fn)
+            us = self._time_graph(g, 3) * 1e3 / len(fn)
+            del g
             out[p.name] = {"shape": f"{p.rows}x{p.cols}" + (" x2 +silu" if p.kind == "silu" else ""),
                            "us": round(us, 2), "GB_s": round(p.bytes(1) / us / 1e3, 1)}
         rt.sync()
@@ -399,6 +487,7 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--layers", type=int, default=WL.LAYERS)
+    ap.add_argument("--no-prompt", action="store_true", help="skip the config-4 prompt gemm section")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank = int(os.environ.get("RANK", "0"))
@@ -457,6 +546,8 @@ def main() -> int:
             line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
         if "sweep" in res:
             line["sweep"] = res["sweep"]
+        if "prompt" in res:
+            line["prompt"] = res["prompt"]
         print(json.dumps(line), flush=True)
     b.rt.close()
     if world > 1:

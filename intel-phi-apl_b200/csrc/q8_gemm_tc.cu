@@ -11,13 +11,18 @@
 // stated 2e-3 (bf16 tiles measure ~1e-2 on the BASELINE shapes).
 //
 // A CTA (persistent, one per SM: it owns all 512 TMEM columns) runs 128-row x BN-token tiles:
-//   warp 8      TMA: per 64-column stage, the quant box (128 rows x 64 B, 64B swizzle), the scale
-//               box (128 rows x 8 scales) and the fp16 x box (BN rows x 128 B, 128B swizzle);
-//   warps 4-7   dequant: thread i turns row i's 64 quants and 2 scales into 64 fp16 weights,
-//               written into the A tile in the UMMA 128B-swizzled K-major layout;
-//   warp 9      MMA: 4 x tcgen05.mma (M=128, N=BN, K=16) per stage into one of two TMEM
-//               accumulators; tcgen05.commit frees the stage, and at a tile's end the accumulator;
+//   warp 12     TMA: per 64-column stage, the quant box (128 rows x 64 B, 64B swizzle), the scale
+//               box (128 rows x 8 scales) and the fp16 x box (BN rows x 128 B, 128B swizzle), into
+//               a ring of up to 8 shared-memory stages;
+//   warps 4-11  dequant: thread (i, h) turns row i's 32 quants of block h and its scale into 32
+//               fp16 weights and stores them (tcgen05.st) into TMEM lane i of an 8-stage A ring;
+//   warp 13     MMA: 4 x tcgen05.mma (M=128, N=BN, K=16, A from TMEM, B = the x box) per stage;
+//               tcgen05.commit frees the shared stage and the A stage, and at a tile's end the
+//               accumulator;
 //   warps 0-3   epilogue: tcgen05.ld of TMEM lanes 32*(warp%4).. -> y (or silu(g)*u for a pair).
+// A stays out of shared memory: the stage's traffic there is the bulk copies in, the dequant's
+// quant reads and the tensor core's reads of x (writing A to shared memory and reading it back
+// made the kernel shared-memory bound at ~1000 cycles per 64-column stage).
 // Every wait is bounded (error word on timeout); every TMA load is a plain single-CTA load.
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -36,21 +41,34 @@ namespace {
 
 constexpr int BM = 128;          // weight rows per tile (MMA M)
 constexpr int BK = 64;           // columns per stage
-constexpr int MAX_BN = 256;      // tokens per tile (MMA N)
-constexpr int MAX_STAGES = 6;
-constexpr int NT = 320;          // 10 warps
-constexpr int EPI_WARP0 = 0, DQ_WARP0 = 4, TMA_WARP = 8, MMA_WARP = 9;
-constexpr int TMEM_COLS = 512;   // two accumulators of up to 256 columns
-constexpr int OFF_Q = 0, OFF_D = 8192, OFF_A = 10240, OFF_X = 26624; // within a stage (1024-aligned)
-constexpr size_t SMEM_LIMIT = 200 * 1024;
+constexpr int MAX_BN = 256;      // tokens per tile (MMA N); 128 for SwiGLU pairs (two accumulators)
+constexpr int MAX_STAGES = 8;
+constexpr int NDQ = 8;           // dequant warps: two per SM sub-partition, each on half of a stage's columns
+constexpr int DQ_WARP0 = 4, TMA_WARP = DQ_WARP0 + NDQ, MMA_WARP = TMA_WARP + 1; // epilogue: warps 0-3
+constexpr int NT = 32 * (MMA_WARP + 1);
+// Tensor memory (512 columns x 128 lanes of 32 bits): the accumulators in columns [0, 256), two
+// of 128 columns when a tile has <= 128 tokens (double-buffered, or a SwiGLU pair's gate and up),
+// else one of 256; the dequantised A tiles in an 8-stage ring of 32 columns each at [256, 512)
+// (a 128 x 64 fp16 tile: lane = row, column j = k 2j and 2j+1).
+constexpr int TMEM_COLS = 512;
+constexpr int A_BASE = 256, A_COLS = BK / 2, NA = (TMEM_COLS - A_BASE) / A_COLS;
+// Shared memory per stage (1024-aligned): the quant box (128 rows x 64 B, 64B swizzle), the scale
+// box (128 rows x 8 fp16), the fp16 x box (bn rows x 128 B, 128B swizzle).
+constexpr int OFF_Q = 0, OFF_D = 8192, OFF_X = 10240;
+// Epilogue staging, after the stages: per epilogue warp two 1 KB buffers of 8 tokens x 32 rows.
+constexpr int STG_TOK = 8, STG_BYTES = STG_TOK * 32 * 4, STG_TOTAL = 4 * 2 * STG_BYTES;
+constexpr size_t SMEM_LIMIT = 224 * 1024; // stages + staging + barriers (the launch adds 1 KB of alignment)
 
 __host__ __device__ constexpr int stage_bytes(int bn) { return (OFF_X + bn * 128 + 1023) / 1024 * 1024; }
+__host__ __device__ constexpr int n_acc(int bn) { return bn <= 128 ? 2 : 1; }
 
 struct TcJobDev {
     CUtensorMap tq, td, tq2, td2; // quants and scales of W (and of the SwiGLU up matrix)
+    CUtensorMap ty;               // y as [t][ldy] fp32, boxes of 32 rows x 8 tokens (when tma_y)
     float *y;
     long long rows, ldy;
     int cols, t, pair, n_pass, tiles, unit0; // tiles: row tiles; units = tiles * n_pass
+    int tma_y;                               // y leaves through bulk tensor stores (else plain stores)
 };
 
 struct TcParams {
@@ -71,6 +89,16 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, in
         : "memory");
 }
 
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *tm, const void *src, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(tm), "r"(c0),
+                 "r"(c1), "r"(smem_u32(src))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// at most one bulk store group of this thread still reading its shared-memory source
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -79,12 +107,25 @@ __device__ __forceinline__ void tc_commit(uint64_t *bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+// D[tmem] (+)= A[tmem] * B[smem descriptor]: M = 128, N from idesc, K = 16.
+__device__ __forceinline__ void tc_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc, uint32_t acc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(da), "l"(db), "r"(idesc), "r"(acc));
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc));
 }
+
+// 16 consecutive 32-bit columns of this thread's TMEM lane (the warp's 32-lane quarter).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // UMMA shared-memory descriptor of a K-major tile in the 128B-swizzled canonical layout: rows of
 // 128 B, 8-row groups 1024 B apart (SBO), leading offset 1 (unused when swizzled), version 1.
@@ -135,12 +176,14 @@ __device__ __forceinline__ Unit unit_of(const TcParams &p, int u) {
 __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int S = p.stages, BN = p.bn, SB = stage_bytes(BN);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + size_t(S) * SB);
-    uint64_t *empty = full + MAX_STAGES;
-    uint64_t *afull = empty + MAX_STAGES;
-    uint64_t *accfull = afull + MAX_STAGES; // [2]
-    uint64_t *accempty = accfull + 2;       // [2]
+    const int S = p.stages, BN = p.bn, SB = stage_bytes(BN), NACC = n_acc(BN), ACC_STRIDE = 256 / NACC;
+    float *stg = reinterpret_cast<float *>(smem + size_t(S) * SB);             // epilogue staging
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + size_t(S) * SB + STG_TOTAL); // [S]: TMA landed
+    uint64_t *empty = full + MAX_STAGES;                                   // [S]: the stage's MMAs done
+    uint64_t *afull = empty + MAX_STAGES;                                  // [NA]: A tile in TMEM
+    uint64_t *aempty = afull + NA;                                         // [NA]: its MMAs done
+    uint64_t *accfull = aempty + NA;                                       // [2]
+    uint64_t *accempty = accfull + 2;                                      // [2]
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accempty + 2);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
@@ -148,7 +191,10 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
-            mbar_init(&afull[s], 128);
+        }
+        for (int a = 0; a < NA; ++a) {
+            mbar_init(&afull[a], 32 * NDQ);
+            mbar_init(&aempty[a], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&accfull[b], 1);
@@ -168,13 +214,11 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     grid_wait(); // x (fp16) and the y buffers belong to the kernels before this one
-    const int nk = 0; // per job (cols differ): computed in the loops
-    (void)nk;
 
     if (warp == TMA_WARP) {
         // ---------------------------------------------------------------- producer
         if (lane == 0) {
-            int s = 0, use = 0; // running stage counter
+            int s = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
                 const Unit w = unit_of(p, u);
@@ -183,8 +227,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
                 for (int ti = 0; ti < w.ntile && ok; ++ti) {
                     const CUtensorMap *tq = ti ? &J.tq2 : &J.tq, *td = ti ? &J.td2 : &J.td;
                     for (int kb = 0; kb < nks; ++kb, ++s) {
-                        const int slot = s % S;
-                        const int k = s / S;
+                        const int slot = s % S, k = s / S;
                         if (k > 0 && !mbar_wait(&empty[slot], (k - 1) & 1)) {
                             report(p.err, ERR_TIMEOUT_MMA);
                             ok = false;
@@ -196,7 +239,6 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
                         tma_load_2d(st + OFF_Q, tq, k0, w.rt * BM, &full[slot]);
                         tma_load_2d(st + OFF_D, td, (k0 / Q8_QK) & ~7, w.rt * BM, &full[slot]);
                         tma_load_2d(st + OFF_X, &p.tx[w.j], k0, w.np * BN, &full[slot]);
-                        ++use;
                     }
                 }
             }
@@ -205,9 +247,12 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
                 if (!mbar_wait(&full[q % S], (q / S) & 1))
                     report(p.err, ERR_TIMEOUT_DRAIN);
         }
-    } else if (warp >= DQ_WARP0 && warp < DQ_WARP0 + 4) {
-        // ---------------------------------------------------------------- dequant
-        const int i = threadIdx.x - DQ_WARP0 * 32; // tile row
+    } else if (warp >= DQ_WARP0 && warp < DQ_WARP0 + NDQ) {
+        // ---------------------------------------------------------------- dequant -> TMEM
+        const int i = (threadIdx.x - DQ_WARP0 * 32) % BM; // tile row = this thread's TMEM lane
+        const int h = (threadIdx.x - DQ_WARP0 * 32) / BM; // 32-column block of the stage
+        const uint32_t lane_base = uint32_t(32 * (warp % 4)) << 16;
+        const __half2 bias = __half2half2(__ushort_as_half(uint16_t(0x6480))); // 1152
         int s = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
@@ -216,53 +261,46 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
             const int nks = (J.cols + BK - 1) / BK;
             for (int ti = 0; ti < w.ntile && ok; ++ti) {
                 for (int kb = 0; kb < nks; ++kb, ++s) {
-                    const int slot = s % S, k = s / S;
-                    if (!mbar_wait(&full[slot], k & 1)) {
+                    const int slot = s % S, as = s % NA;
+                    if (!mbar_wait(&full[slot], (s / S) & 1)) {
                         report(p.err, ERR_TIMEOUT_FULL);
                         ok = false;
                         break;
                     }
-                    // the A tile of this slot is free once the MMAs of its previous use are done
-                    if (k > 0 && !mbar_wait(&empty[slot], (k - 1) & 1)) {
-                        report(p.err, ERR_TIMEOUT_MMA);
-                        ok = false;
-                        break;
-                    }
-                    uint8_t *st = smem + size_t(slot) * SB;
-                    // the two scales of this 64-column stage, from the 8 the scale box holds
-                    const int e0 = (kb * 2) & 7;
-                    const uint32_t dd = *reinterpret_cast<const uint32_t *>(st + OFF_D + i * 16 + e0 * 2);
-                    const __half2 d0 = __half2half2(__ushort_as_half(uint16_t(dd & 0xffff)));
-                    const __half2 d1 = __half2half2(__ushort_as_half(uint16_t(dd >> 16)));
-                    const __half2 bias = __half2half2(__ushort_as_half(uint16_t(0x6480))); // 1152
-                    uint8_t *arow = st + OFF_A + i * 128;
+                    const uint8_t *st = smem + size_t(slot) * SB;
+                    // this block's scale (one of the 8 the scale box holds) and its 32 quants
+                    const __half2 dd2 =
+                        __half2half2(*reinterpret_cast<const __half *>(st + OFF_D + i * 16 + ((kb * 2 + h) & 7) * 2));
+                    uint32_t outw[16];
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) { // 16 quants per chunk; chunks 0,1 block 0; 2,3 block 1
+                    for (int cc = 0; cc < 2; ++cc) { // 16 quants per chunk; chunks 2h, 2h+1
+                        const int c = 2 * h + cc;
                         const uint4 qv =
                             *reinterpret_cast<const uint4 *>(st + OFF_Q + i * 64 + ((c ^ ((i >> 1) & 3)) << 4));
                         const uint32_t wq[4] = {qv.x ^ 0x80808080u, qv.y ^ 0x80808080u, qv.z ^ 0x80808080u,
                                                 qv.w ^ 0x80808080u};
-                        const __half2 dd2 = c < 2 ? d0 : d1;
-                        uint32_t outw[8];
 #pragma unroll
                         for (int v = 0; v < 4; ++v) {
                             // (q+128) as the low byte of fp16 1024+(q+128): exact; minus 1152 -> q
                             const uint32_t lo = __byte_perm(wq[v], 0x64646464u, 0x4140u);
                             const uint32_t hi = __byte_perm(wq[v], 0x64646464u, 0x4342u);
-                            __half2 a = __hsub2(*reinterpret_cast<const __half2 *>(&lo), bias);
-                            __half2 b = __hsub2(*reinterpret_cast<const __half2 *>(&hi), bias);
-                            a = __hmul2(a, dd2);
-                            b = __hmul2(b, dd2);
-                            outw[2 * v] = *reinterpret_cast<uint32_t *>(&a);
-                            outw[2 * v + 1] = *reinterpret_cast<uint32_t *>(&b);
+                            __half2 a = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&lo), bias), dd2);
+                            __half2 b = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&hi), bias), dd2);
+                            outw[8 * cc + 2 * v] = *reinterpret_cast<uint32_t *>(&a);
+                            outw[8 * cc + 2 * v + 1] = *reinterpret_cast<uint32_t *>(&b);
                         }
-                        // 16 fp16 = two 16-byte chunks (2c, 2c+1) of the 128-byte row, swizzled
-                        const int c0 = (2 * c) ^ (i & 7), c1 = (2 * c + 1) ^ (i & 7);
-                        *reinterpret_cast<uint4 *>(arow + (c0 << 4)) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
-                        *reinterpret_cast<uint4 *>(arow + (c1 << 4)) = make_uint4(outw[4], outw[5], outw[6], outw[7]);
                     }
-                    fence_proxy_async_shared(); // generic-proxy writes -> visible to the tensor core
-                    mbar_arrive(&afull[slot]);
+                    // the TMEM A stage is free once the MMAs of its previous use completed
+                    if (s >= NA && !mbar_wait(&aempty[as], ((s / NA) - 1) & 1)) {
+                        report(p.err, ERR_TIMEOUT_MMA);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    tmem_st16(tmem + lane_base + uint32_t(A_BASE + as * A_COLS + 16 * h), outw);
+                    tmem_wait_st();
+                    tc_fence_before();
+                    mbar_arrive(&afull[as]);
                 }
             }
         }
@@ -277,28 +315,29 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
                 const TcJobDev &J = p.job[w.j];
                 const int nks = (J.cols + BK - 1) / BK;
                 for (int ti = 0; ti < w.ntile && ok; ++ti, ++tcount) {
-                    const int b = tcount & 1, bu = tcount >> 1;
+                    const int b = tcount % NACC, bu = tcount / NACC;
                     if (bu > 0 && !mbar_wait(&accempty[b], (bu - 1) & 1)) {
                         report(p.err, ERR_TIMEOUT_MMA);
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t tacc = tmem + uint32_t(b * 256);
+                    const uint32_t tacc = tmem + uint32_t(b * ACC_STRIDE);
                     for (int kb = 0; kb < nks; ++kb, ++s) {
-                        const int slot = s % S, k = s / S;
-                        if (!mbar_wait(&afull[slot], k & 1) || !mbar_wait(&full[slot], k & 1)) {
+                        const int slot = s % S, as = s % NA;
+                        if (!mbar_wait(&afull[as], (s / NA) & 1) || !mbar_wait(&full[slot], (s / S) & 1)) {
                             report(p.err, ERR_TIMEOUT_MMA);
                             ok = false;
                             break;
                         }
                         tc_fence_after();
-                        uint8_t *st = smem + size_t(slot) * SB;
-                        const uint64_t da = sw128_desc(st + OFF_A), db = sw128_desc(st + OFF_X);
+                        const uint64_t db = sw128_desc(smem + size_t(slot) * SB + OFF_X);
+                        const uint32_t ta = tmem + uint32_t(A_BASE + as * A_COLS);
 #pragma unroll
-                        for (int kk = 0; kk < BK / 16; ++kk) // +32 bytes along K per step
-                            tc_mma(tacc, da + uint64_t(2 * kk), db + uint64_t(2 * kk), idesc, (kb | kk) ? 1u : 0u);
+                        for (int kk = 0; kk < BK / 16; ++kk) // K = 16 per MMA: 8 TMEM columns of A, 32 B of B
+                            tc_mma_ts(tacc, ta + uint32_t(8 * kk), db + uint64_t(2 * kk), idesc, (kb | kk) ? 1u : 0u);
                         tc_commit(&empty[slot]);
+                        tc_commit(&aempty[as]);
                     }
                     if (ok)
                         tc_commit(&accfull[b]);
@@ -311,16 +350,20 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
         }
     } else {
         // ---------------------------------------------------------------- epilogue (warps 0-3)
-        const int e = warp & 3; // TMEM lanes 32e..32e+31 = tile rows
-        int tcount = 0;
+        // Warp e reads TMEM lanes 32e.. (rows 32e..32e+31 of the tile) 16 token columns at a time.
+        // With tma_y the values go through a double-buffered 1 KB staging box per warp and leave by
+        // bulk tensor stores (clipped at the matrix and token edges); the accumulator is released
+        // as soon as its last columns are in registers.
+        const int e = warp & 3;
+        float *mystg = stg + e * 2 * (STG_BYTES / 4);
+        int tcount = 0, nstore = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
             const Unit w = unit_of(p, u);
             const TcJobDev &J = p.job[w.j];
-            const int b0 = tcount & 1;
             bool got = true;
             for (int ti = 0; ti < w.ntile; ++ti) {
-                const int b = (tcount + ti) & 1, bu = (tcount + ti) >> 1;
+                const int b = (tcount + ti) % NACC, bu = (tcount + ti) / NACC;
                 got = got && mbar_wait(&accfull[b], bu & 1);
             }
             if (!got) {
@@ -329,34 +372,68 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
                 break;
             }
             tc_fence_after();
-            const long long row = (long long)w.rt * BM + 32 * e + lane;
+            const uint32_t c_gate = uint32_t((tcount % NACC) * ACC_STRIDE);
+            const uint32_t c_up = uint32_t(((tcount + 1) % NACC) * ACC_STRIDE);
+            const int row0 = w.rt * BM + 32 * e; // this warp's first row
+            const long long row = (long long)row0 + lane;
             const int n0 = w.np * BN;
+            const bool tma_y = J.tma_y != 0;
+            float *const ybase = J.y;
+            const long long ldy = J.ldy, nrows = J.rows;
+            const int ntok = J.t;
             for (int c0 = 0; c0 < BN; c0 += 16) {
                 uint32_t r[16], r2[16];
-                tmem_ld16(tmem + (uint32_t(32 * e) << 16) + uint32_t(b0 * 256 + c0), r);
+                tmem_ld16(tmem + (uint32_t(32 * e) << 16) + c_gate + uint32_t(c0), r);
                 if (w.ntile == 2)
-                    tmem_ld16(tmem + (uint32_t(32 * e) << 16) + uint32_t((b0 ^ 1) * 256 + c0), r2);
+                    tmem_ld16(tmem + (uint32_t(32 * e) << 16) + c_up + uint32_t(c0), r2);
                 tmem_wait_ld();
-                if (row < J.rows) {
+                if (c0 + 16 >= BN) { // the unit's accumulators are in registers: hand them back
+                    tc_fence_before();
+                    for (int ti = 0; ti < w.ntile; ++ti)
+                        mbar_arrive(&accempty[(tcount + ti) % NACC]);
+                }
+                float v[16];
 #pragma unroll
-                    for (int c = 0; c < 16; ++c) {
-                        const int tok = n0 + c0 + c;
-                        if (tok < J.t) {
-                            float v = __uint_as_float(r[c]);
-                            if (w.ntile == 2) {
-                                const float up = __uint_as_float(r2[c]);
-                                v = v / (1.0f + expf(-v)) * up;
-                            }
-                            J.y[(long long)tok * J.ldy + row] = v;
-                        }
+                for (int c = 0; c < 16; ++c) {
+                    v[c] = __uint_as_float(r[c]);
+                    if (w.ntile == 2) {
+                        const float up = __uint_as_float(r2[c]);
+                        v[c] = v[c] / (1.0f + expf(-v[c])) * up;
                     }
                 }
+                if (tma_y) {
+#pragma unroll
+                    for (int hh = 0; hh < 16 / STG_TOK; ++hh) {
+                        if (n0 + c0 + hh * STG_TOK >= ntok)
+                            break; // tokens past t: nothing to store
+                        float *buf = mystg + (nstore & 1) * (STG_BYTES / 4);
+                        if (lane == 0)
+                            bulk_wait_read1(); // the store two back (same buffer) has read it
+                        __syncwarp();
+#pragma unroll
+                        for (int c = 0; c < STG_TOK; ++c)
+                            buf[c * 32 + lane] = v[hh * STG_TOK + c];
+                        fence_proxy_async_shared(); // generic-proxy writes -> visible to the bulk store
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(&J.ty, buf, row0, n0 + c0 + hh * STG_TOK);
+                            bulk_commit();
+                        }
+                        ++nstore;
+                    }
+                } else if (row < nrows) {
+                    float *yp = ybase + (long long)(n0 + c0) * ldy + row;
+#pragma unroll
+                    for (int c = 0; c < 16; ++c)
+                        if (n0 + c0 + c < ntok)
+                            yp[(long long)c * ldy] = v[c];
+                }
             }
-            tc_fence_before();
-            for (int ti = 0; ti < w.ntile; ++ti)
-                mbar_arrive(&accempty[(tcount + ti) & 1]);
             tcount += w.ntile;
         }
+        if (lane == 0)
+            bulk_wait_all(); // the staging buffers stay valid until every bulk store has completed
+        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();
@@ -424,10 +501,13 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
     if (gemm_tc_scratch_bytes(jobs, n) > scratch_bytes || !scratch)
         return cudaErrorInvalidValue;
     // tokens per tile: the largest t split into passes of <= 256, rounded up to 16
-    int tmax = 0;
-    for (int j = 0; j < n; ++j)
+    int tmax = 0, maxbn = MAX_BN;
+    for (int j = 0; j < n; ++j) {
         tmax = jobs[j].t > tmax ? jobs[j].t : tmax;
-    const int npass_max = (tmax + MAX_BN - 1) / MAX_BN;
+        if (jobs[j].w2)
+            maxbn = 128; // a pair's gate and up accumulators share the 256 accumulator columns
+    }
+    const int npass_max = (tmax + maxbn - 1) / maxbn;
     int bn = ((tmax + npass_max - 1) / npass_max + 15) / 16 * 16;
     if (bn < 16)
         bn = 16;
@@ -437,7 +517,7 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
     p.bn = bn;
     p.err = err;
     const int sb = stage_bytes(bn);
-    p.stages = int(SMEM_LIMIT / size_t(sb));
+    p.stages = int((SMEM_LIMIT - STG_TOTAL - 512) / size_t(sb));
     if (p.stages > MAX_STAGES)
         p.stages = MAX_STAGES;
     if (p.stages < 2)
@@ -466,6 +546,12 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
         J.y = G.y;
         J.rows = G.rows;
         J.ldy = G.ldy;
+        // bulk tensor stores need a 16-byte aligned y and row stride
+        J.tma_y = (reinterpret_cast<uintptr_t>(G.y) % 16 == 0 && (G.ldy * 4) % 16 == 0 &&
+                   make_map(&J.ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, G.y, uint64_t(G.rows), uint64_t(G.t),
+                            uint64_t(G.ldy) * 4, 32, STG_TOK, CU_TENSOR_MAP_SWIZZLE_NONE))
+                      ? 1
+                      : 0;
         J.cols = G.cols;
         J.t = G.t;
         J.n_pass = (G.t + bn - 1) / bn;
@@ -474,11 +560,17 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
         units += J.tiles * J.n_pass;
     }
     p.total_units = units;
-    const size_t smem = size_t(p.stages) * sb + 6 * 8 * MAX_STAGES + 64 + 1024;
+    size_t smem = size_t(p.stages) * sb + STG_TOTAL + 8 * (2 * MAX_STAGES + 2 * NA + 4) + 64 + 1024;
+    if (smem > 227 * 1024)
+        return cudaErrorInvalidValue;
+    // One CTA per SM: it allocates all 512 TMEM columns, so a second CTA on the SM would only wait
+    // in its allocation. More than half the SM's shared memory keeps a second one off.
+    if (smem < 116 * 1024)
+        smem = 116 * 1024;
     static bool attr = false;
     if (!attr) {
         cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             int(SMEM_LIMIT + 4096));
+                                             227 * 1024); // the SM's limit per CTA
         if (e != cudaSuccess)
             return e;
         attr = true;
