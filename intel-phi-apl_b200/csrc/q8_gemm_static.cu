@@ -94,7 +94,7 @@ extern "C" RTB_API int rt_gemm_static(const void *w, long rows, long cols, const
     job.rows = rows;
     job.cols = int(cols);
     job.t = int(t);
-    if (q8::launch_gemm_tc(&job, 1, d->base + STATIC_HEADER, STATIC_X_BYTES, d->num_sms, err, s, false) !=
+    if (q8::launch_gemm_tc(&job, 1, d->base + STATIC_HEADER, STATIC_X_BYTES, d->num_sms, err, s, false, false) !=
         cudaSuccess)
         return RTB_ECUDA;
     unsigned h = 0;

@@ -65,10 +65,13 @@ __host__ __device__ constexpr int n_acc(int bn) { return bn <= 128 ? 2 : 1; }
 struct TcJobDev {
     CUtensorMap tq, td, tq2, td2; // quants and scales of W (and of the SwiGLU up matrix)
     CUtensorMap ty;               // y as [t][ldy] fp32, boxes of 32 rows x 8 tokens (when tma_y)
+    CUtensorMap tp;               // split-K partial sums as [plane][t][rows] fp32, same boxes (when tma_p)
     float *y;
+    float *part;                  // split-K partial sums: plane = (pair tile) * ks + K part
     long long rows, ldy;
-    int cols, t, pair, n_pass, tiles, unit0; // tiles: row tiles; units = tiles * n_pass
-    int tma_y;                               // y leaves through bulk tensor stores (else plain stores)
+    int cols, t, pair, n_pass, tiles, unit0; // tiles: row tiles; units = tiles * n_pass * ks
+    int ks;                                  // K parts (1: no split, the epilogue writes y)
+    int tma_y, tma_p;                        // bulk tensor stores usable for y / for the partials
 };
 
 struct TcParams {
@@ -92,6 +95,11 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, in
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *tm, const void *src, int c0, int c1) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(tm), "r"(c0),
                  "r"(c1), "r"(smem_u32(src))
+                 : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *tm, const void *src, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(tm),
+                 "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src))
                  : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
@@ -158,8 +166,9 @@ __device__ __forceinline__ int find_job(const TcParams &p, int u) {
 
 // A unit of work: row tile `rt` and token pass `np` of job `j`; a SwiGLU pair unit is two MMA
 // tiles (gate, then up) sharing the x tiles and the two accumulators.
+// A unit: row tile `rt`, token pass `np` and K part `kp` (64-column blocks kb0..kb1-1) of job `j`.
 struct Unit {
-    int j, rt, np, ntile; // ntile: MMA tiles in the unit (1 or 2)
+    int j, rt, np, kp, kb0, kb1, ntile; // ntile: MMA tiles in the unit (1 or 2)
 };
 
 __device__ __forceinline__ Unit unit_of(const TcParams &p, int u) {
@@ -167,8 +176,14 @@ __device__ __forceinline__ Unit unit_of(const TcParams &p, int u) {
     w.j = find_job(p, u);
     const TcJobDev &J = p.job[w.j];
     const int lu = u - J.unit0;
-    w.rt = lu / J.n_pass;
-    w.np = lu - w.rt * J.n_pass;
+    const int per_rt = J.n_pass * J.ks;
+    w.rt = lu / per_rt;
+    const int rem = lu - w.rt * per_rt;
+    w.np = rem / J.ks;
+    w.kp = rem - w.np * J.ks;
+    const int nks = (J.cols + BK - 1) / BK;
+    w.kb0 = int((long long)w.kp * nks / J.ks);
+    w.kb1 = int((long long)(w.kp + 1) * nks / J.ks);
     w.ntile = J.pair ? 2 : 1;
     return w;
 }
@@ -223,10 +238,9 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
             for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
                 const Unit w = unit_of(p, u);
                 const TcJobDev &J = p.job[w.j];
-                const int nks = (J.cols + BK - 1) / BK;
                 for (int ti = 0; ti < w.ntile && ok; ++ti) {
                     const CUtensorMap *tq = ti ? &J.tq2 : &J.tq, *td = ti ? &J.td2 : &J.td;
-                    for (int kb = 0; kb < nks; ++kb, ++s) {
+                    for (int kb = w.kb0; kb < w.kb1; ++kb, ++s) {
                         const int slot = s % S, k = s / S;
                         if (k > 0 && !mbar_wait(&empty[slot], (k - 1) & 1)) {
                             report(p.err, ERR_TIMEOUT_MMA);
@@ -258,9 +272,9 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
         for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
             const Unit w = unit_of(p, u);
             const TcJobDev &J = p.job[w.j];
-            const int nks = (J.cols + BK - 1) / BK;
+            (void)J;
             for (int ti = 0; ti < w.ntile && ok; ++ti) {
-                for (int kb = 0; kb < nks; ++kb, ++s) {
+                for (int kb = w.kb0; kb < w.kb1; ++kb, ++s) {
                     const int slot = s % S, as = s % NA;
                     if (!mbar_wait(&full[slot], (s / S) & 1)) {
                         report(p.err, ERR_TIMEOUT_FULL);
@@ -313,7 +327,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
             for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
                 const Unit w = unit_of(p, u);
                 const TcJobDev &J = p.job[w.j];
-                const int nks = (J.cols + BK - 1) / BK;
+                (void)J;
                 for (int ti = 0; ti < w.ntile && ok; ++ti, ++tcount) {
                     const int b = tcount % NACC, bu = tcount / NACC;
                     if (bu > 0 && !mbar_wait(&accempty[b], (bu - 1) & 1)) {
@@ -323,7 +337,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
                     }
                     tc_fence_after();
                     const uint32_t tacc = tmem + uint32_t(b * ACC_STRIDE);
-                    for (int kb = 0; kb < nks; ++kb, ++s) {
+                    for (int kb = w.kb0; kb < w.kb1; ++kb, ++s) {
                         const int slot = s % S, as = s % NA;
                         if (!mbar_wait(&afull[as], (s / NA) & 1) || !mbar_wait(&full[slot], (s / S) & 1)) {
                             report(p.err, ERR_TIMEOUT_MMA);
@@ -335,7 +349,8 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
                         const uint32_t ta = tmem + uint32_t(A_BASE + as * A_COLS);
 #pragma unroll
                         for (int kk = 0; kk < BK / 16; ++kk) // K = 16 per MMA: 8 TMEM columns of A, 32 B of B
-                            tc_mma_ts(tacc, ta + uint32_t(8 * kk), db + uint64_t(2 * kk), idesc, (kb | kk) ? 1u : 0u);
+                            tc_mma_ts(tacc, ta + uint32_t(8 * kk), db + uint64_t(2 * kk), idesc,
+                                      (kb != w.kb0 || kk) ? 1u : 0u);
                         tc_commit(&empty[slot]);
                         tc_commit(&aempty[as]);
                     }
@@ -377,10 +392,13 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
             const int row0 = w.rt * BM + 32 * e; // this warp's first row
             const long long row = (long long)row0 + lane;
             const int n0 = w.np * BN;
-            const bool tma_y = J.tma_y != 0;
-            float *const ybase = J.y;
-            const long long ldy = J.ldy, nrows = J.rows;
+            const long long nrows = J.rows;
             const int ntok = J.t;
+            const bool split = J.ks > 1; // partial sums to the split-K planes, reduced afterwards
+            // one or two outputs per unit: y (silu(g)*u for a pair), or the partial plane(s)
+            const int nout = split ? w.ntile : 1;
+            const bool use_tma = split ? J.tma_p != 0 : J.tma_y != 0;
+            const CUtensorMap *tmap = split ? &J.tp : &J.ty;
             for (int c0 = 0; c0 < BN; c0 += 16) {
                 uint32_t r[16], r2[16];
                 tmem_ld16(tmem + (uint32_t(32 * e) << 16) + c_gate + uint32_t(c0), r);
@@ -392,41 +410,57 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
                     for (int ti = 0; ti < w.ntile; ++ti)
                         mbar_arrive(&accempty[(tcount + ti) % NACC]);
                 }
-                float v[16];
+                for (int o = 0; o < nout; ++o) {
+                    float v[16];
 #pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    v[c] = __uint_as_float(r[c]);
-                    if (w.ntile == 2) {
-                        const float up = __uint_as_float(r2[c]);
-                        v[c] = v[c] / (1.0f + expf(-v[c])) * up;
-                    }
-                }
-                if (tma_y) {
-#pragma unroll
-                    for (int hh = 0; hh < 16 / STG_TOK; ++hh) {
-                        if (n0 + c0 + hh * STG_TOK >= ntok)
-                            break; // tokens past t: nothing to store
-                        float *buf = mystg + (nstore & 1) * (STG_BYTES / 4);
-                        if (lane == 0)
-                            bulk_wait_read1(); // the store two back (same buffer) has read it
-                        __syncwarp();
-#pragma unroll
-                        for (int c = 0; c < STG_TOK; ++c)
-                            buf[c * 32 + lane] = v[hh * STG_TOK + c];
-                        fence_proxy_async_shared(); // generic-proxy writes -> visible to the bulk store
-                        __syncwarp();
-                        if (lane == 0) {
-                            tma_store_2d(&J.ty, buf, row0, n0 + c0 + hh * STG_TOK);
-                            bulk_commit();
+                    for (int c = 0; c < 16; ++c) {
+                        const float g = __uint_as_float(o ? r2[c] : r[c]);
+                        if (!split && w.ntile == 2) {
+                            const float up = __uint_as_float(r2[c]);
+                            v[c] = g / (1.0f + expf(-g)) * up;
+                        } else {
+                            v[c] = g;
                         }
-                        ++nstore;
                     }
-                } else if (row < nrows) {
-                    float *yp = ybase + (long long)(n0 + c0) * ldy + row;
+                    const int plane = o * J.ks + w.kp; // split: the partial plane; else unused
+                    if (use_tma) {
 #pragma unroll
-                    for (int c = 0; c < 16; ++c)
-                        if (n0 + c0 + c < ntok)
-                            yp[(long long)c * ldy] = v[c];
+                        for (int hh = 0; hh < 16 / STG_TOK; ++hh) {
+                            if (n0 + c0 + hh * STG_TOK >= ntok)
+                                break; // tokens past t: nothing to store
+                            float *buf = mystg + (nstore & 1) * (STG_BYTES / 4);
+                            if (lane == 0)
+                                bulk_wait_read1(); // the store two back (same buffer) has read it
+                            __syncwarp();
+#pragma unroll
+                            for (int c = 0; c < STG_TOK; ++c)
+                                buf[c * 32 + lane] = v[hh * STG_TOK + c];
+                            fence_proxy_async_shared(); // generic-proxy writes -> visible to the bulk store
+                            __syncwarp();
+                            if (lane == 0) {
+                                if (split)
+                                    tma_store_3d(tmap, buf, row0, n0 + c0 + hh * STG_TOK, plane);
+                                else
+                                    tma_store_2d(tmap, buf, row0, n0 + c0 + hh * STG_TOK);
+                                bulk_commit();
+                            }
+                            ++nstore;
+                        }
+                    } else if (row < nrows) {
+                        float *yp;
+                        long long ld;
+                        if (split) {
+                            yp = J.part + ((long long)plane * ntok + n0 + c0) * nrows + row;
+                            ld = nrows;
+                        } else {
+                            yp = J.y + (long long)(n0 + c0) * J.ldy + row;
+                            ld = J.ldy;
+                        }
+#pragma unroll
+                        for (int c = 0; c < 16; ++c)
+                            if (n0 + c0 + c < ntok)
+                                yp[(long long)c * ld] = v[c];
+                    }
                 }
             }
             tcount += w.ntile;
@@ -447,6 +481,26 @@ __global__ void x_to_half_kernel(const float *x, long long ldx, int cols, int t,
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
         const long long r = i / cols, c = i - r * cols;
         xh[i] = __float2half_rn(x[r * ldx + c]);
+    }
+}
+
+// y[tok][row] = sum over K parts k (in order) of part[k][tok][row]; for a SwiGLU pair the gate
+// planes come first, then the up planes, and y = silu(gate sum) * (up sum).
+__global__ void splitk_reduce_kernel(const float *part, int ks, int pair, long long rows, int t, float *y,
+                                     long long ldy) {
+    const long long n = (long long)t * rows, plane = n;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const long long tok = i / rows, row = i - tok * rows;
+        float g = part[i];
+        for (int k = 1; k < ks; ++k)
+            g += part[k * plane + i];
+        if (pair) {
+            float u = part[ks * plane + i];
+            for (int k = 1; k < ks; ++k)
+                u += part[(ks + k) * plane + i];
+            g = g / (1.0f + expf(-g)) * u;
+        }
+        y[tok * ldy + row] = g;
     }
 }
 
@@ -475,6 +529,18 @@ bool make_map(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// fp32 [d2][d1][d0] array (dense), boxes of b0 x b1 x 1: the split-K partial planes.
+bool make_map3(CUtensorMap *m, const float *base, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t b0, uint32_t b1) {
+    auto fn = encode_fn();
+    if (!fn)
+        return false;
+    const cuuint64_t dims[3] = {d0, d1, d2}, strides[2] = {d0 * 4, d0 * d1 * 4};
+    const cuuint32_t box[3] = {b0, b1, 1}, es[3] = {1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // The quant and scale maps of a row-split matrix (rows x cols): quants are a 2-D uint8 array of
 // cols bytes per row, rows q8s_row_bytes apart; scales a uint16 array at +cols of the same rows.
 bool weight_maps(const uint8_t *w, long long rows, int cols, CUtensorMap *tq, CUtensorMap *td) {
@@ -487,20 +553,11 @@ bool weight_maps(const uint8_t *w, long long rows, int cols, CUtensorMap *tq, CU
 
 } // namespace
 
-size_t gemm_tc_scratch_bytes(const GemmJob *jobs, int n) {
-    size_t s = 0;
-    for (int j = 0; j < n; ++j)
-        s += (size_t(jobs[j].t) * jobs[j].cols * sizeof(__half) + 255) / 256 * 256;
-    return s;
-}
+namespace {
 
-cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scratch_bytes, int num_sms,
-                           unsigned *err, cudaStream_t stream, bool pdl) {
-    if (n < 1 || n > 8)
-        return cudaErrorInvalidValue;
-    if (gemm_tc_scratch_bytes(jobs, n) > scratch_bytes || !scratch)
-        return cudaErrorInvalidValue;
-    // tokens per tile: the largest t split into passes of <= 256, rounded up to 16
+// Tokens per tile: the largest t split into passes of <= MAX_BN (128 when a SwiGLU pair is in the
+// launch), rounded up to 16.
+int choose_bn(const GemmJob *jobs, int n) {
     int tmax = 0, maxbn = MAX_BN;
     for (int j = 0; j < n; ++j) {
         tmax = jobs[j].t > tmax ? jobs[j].t : tmax;
@@ -508,9 +565,60 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
             maxbn = 128; // a pair's gate and up accumulators share the 256 accumulator columns
     }
     const int npass_max = (tmax + maxbn - 1) / maxbn;
-    int bn = ((tmax + npass_max - 1) / npass_max + 15) / 16 * 16;
-    if (bn < 16)
-        bn = 16;
+    const int bn = ((tmax + npass_max - 1) / npass_max + 15) / 16 * 16;
+    return bn < 16 ? 16 : bn;
+}
+
+// K parts per job. A launch whose (row tile, token pass) units would leave more than half of the
+// SMs idle splits K so that there are about two units per SM, each part at least 32 64-column
+// blocks long (shorter parts measure slower: every unit pays its pipeline fill and epilogue); the
+// parts' fp32 partial sums are then added in order by a reduce pass.
+void choose_splits(const GemmJob *jobs, int n, int bn, int num_sms, bool allow, int *ks) {
+    long long base = 0;
+    for (int j = 0; j < n; ++j)
+        base += ((jobs[j].rows + BM - 1) / BM) * ((jobs[j].t + bn - 1) / bn);
+    const int sms = num_sms > 0 ? num_sms : 148;
+    for (int j = 0; j < n; ++j) {
+        int k = 1;
+        if (allow && 2 * base <= sms) {
+            k = int((2 * sms + base - 1) / base);
+            const int nks = (jobs[j].cols + BK - 1) / BK;
+            const int kmax = nks / 32 > 1 ? nks / 32 : 1;
+            k = k < kmax ? k : kmax;
+            k = k < 16 ? k : 16;
+        }
+        ks[j] = k;
+    }
+}
+
+size_t part_bytes(const GemmJob &G, int ks) {
+    return ks > 1 ? (size_t(G.w2 ? 2 : 1) * ks * G.t * G.rows * sizeof(float) + 255) / 256 * 256 : 0;
+}
+
+size_t x_bytes(const GemmJob &G) { return (size_t(G.t) * G.cols * sizeof(__half) + 255) / 256 * 256; }
+
+} // namespace
+
+size_t gemm_tc_scratch_bytes(const GemmJob *jobs, int n, int num_sms, bool split_k) {
+    if (n < 1 || n > 8)
+        return 0;
+    int ks[8];
+    choose_splits(jobs, n, choose_bn(jobs, n), num_sms, split_k, ks);
+    size_t s = 0;
+    for (int j = 0; j < n; ++j)
+        s += x_bytes(jobs[j]) + part_bytes(jobs[j], ks[j]);
+    return s;
+}
+
+cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scratch_bytes, int num_sms,
+                           unsigned *err, cudaStream_t stream, bool pdl, bool split_k) {
+    if (n < 1 || n > 8)
+        return cudaErrorInvalidValue;
+    if (gemm_tc_scratch_bytes(jobs, n, num_sms, split_k) > scratch_bytes || !scratch)
+        return cudaErrorInvalidValue;
+    const int bn = choose_bn(jobs, n);
+    int ks[8];
+    choose_splits(jobs, n, bn, num_sms, split_k, ks);
     TcParams p;
     memset(&p, 0, sizeof p);
     p.njobs = n;
@@ -529,7 +637,7 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
         if (G.cols < Q8_QK || G.cols % Q8_QK || G.t < 1 || G.rows < 1)
             return cudaErrorInvalidValue;
         __half *xh = reinterpret_cast<__half *>(sc);
-        sc += (size_t(G.t) * G.cols * sizeof(__half) + 255) / 256 * 256;
+        sc += x_bytes(G);
         const long long nconv = (long long)G.t * G.cols;
         int grid = int((nconv + 255) / 256);
         grid = grid > 4096 ? 4096 : grid;
@@ -546,18 +654,30 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
         J.y = G.y;
         J.rows = G.rows;
         J.ldy = G.ldy;
-        // bulk tensor stores need a 16-byte aligned y and row stride
+        J.ks = ks[j];
+        // bulk tensor stores need a 16-byte aligned base and row stride
         J.tma_y = (reinterpret_cast<uintptr_t>(G.y) % 16 == 0 && (G.ldy * 4) % 16 == 0 &&
                    make_map(&J.ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, G.y, uint64_t(G.rows), uint64_t(G.t),
                             uint64_t(G.ldy) * 4, 32, STG_TOK, CU_TENSOR_MAP_SWIZZLE_NONE))
                       ? 1
                       : 0;
+        J.part = nullptr;
+        J.tma_p = 0;
+        if (J.ks > 1) {
+            J.part = reinterpret_cast<float *>(sc);
+            sc += part_bytes(G, J.ks);
+            J.tma_p = (G.rows * 4) % 16 == 0 &&
+                              make_map3(&J.tp, J.part, uint64_t(G.rows), uint64_t(G.t), uint64_t((J.pair ? 2 : 1) * J.ks),
+                                        32, STG_TOK)
+                          ? 1
+                          : 0;
+        }
         J.cols = G.cols;
         J.t = G.t;
         J.n_pass = (G.t + bn - 1) / bn;
         J.tiles = int((G.rows + BM - 1) / BM);
         J.unit0 = units;
-        units += J.tiles * J.n_pass;
+        units += J.tiles * J.n_pass * J.ks;
     }
     p.total_units = units;
     size_t smem = size_t(p.stages) * sb + STG_TOTAL + 8 * (2 * MAX_STAGES + 2 * NA + 4) + 64 + 1024;
@@ -588,7 +708,22 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
     lattr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = lattr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel, p);
+    if (e != cudaSuccess)
+        return e;
+    // the split jobs' partial sums, added in K order (stream order after the product)
+    for (int j = 0; j < n; ++j) {
+        const TcJobDev &J = p.job[j];
+        if (J.ks < 2)
+            continue;
+        const long long outs = (long long)J.t * J.rows;
+        int g = int((outs + 255) / 256);
+        g = g > 8192 ? 8192 : g;
+        splitk_reduce_kernel<<<g, 256, 0, stream>>>(J.part, J.ks, J.pair, J.rows, J.t, J.y, J.ldy);
+        if ((e = cudaGetLastError()) != cudaSuccess)
+            return e;
+    }
+    return cudaSuccess;
 }
 
 } // namespace q8

@@ -53,11 +53,13 @@ struct GemmJob {
     int t;
 };
 
-// Scratch (device bytes) launch_gemm_tc needs for these jobs: their x in fp16.
-size_t gemm_tc_scratch_bytes(const GemmJob *jobs, int n);
-// Up to 8 jobs in one persistent launch (plus one fp16 conversion of each x).
+// Scratch (device bytes) launch_gemm_tc needs for these jobs: their x in fp16, and with split_k
+// the fp32 partial sums of jobs whose K is split (launches with fewer row-tile units than SMs).
+size_t gemm_tc_scratch_bytes(const GemmJob *jobs, int n, int num_sms, bool split_k);
+// Up to 8 jobs in one persistent launch (plus one fp16 conversion of each x, and with split_k one
+// reduce pass per split job).
 cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scratch_bytes, int num_sms,
-                           unsigned *err, cudaStream_t stream, bool pdl);
+                           unsigned *err, cudaStream_t stream, bool pdl, bool split_k);
 
 // ---- utilities
 cudaError_t launch_repack(const uint8_t *gguf, long long rows, int cols, uint8_t *out, cudaStream_t stream);

@@ -176,11 +176,11 @@ bool ensure_scratch(Ctx *c, size_t bytes) {
 bool flush_tc(Ctx *c, std::vector<q8::GemmJob> &jobs) {
     for (size_t i = 0; i < jobs.size(); i += 8) {
         const int n = int(jobs.size() - i < 8 ? jobs.size() - i : 8);
-        const size_t need = q8::gemm_tc_scratch_bytes(&jobs[i], n);
+        const size_t need = q8::gemm_tc_scratch_bytes(&jobs[i], n, c->num_sms, true);
         if (!ensure_scratch(c, need))
             return false;
         if (!cuda_ok(c, q8::launch_gemm_tc(&jobs[i], n, c->scratch, c->scratch_bytes, c->num_sms, c->d_err, c->stream,
-                                           c->overlap),
+                                           c->overlap, true),
                      "tensor-core gemm launch"))
             return false;
     }
