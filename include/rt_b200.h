@@ -163,11 +163,19 @@ RTB_API void rt_b200_free(struct rt *R);
 /* ---------------------------------------------------------------- row sharding over GPUs
  * One process per GPU. With world > 1, every product's w is this rank's row shard (rows/world
  * consecutive rows, rank-major, rows % world == 0) while rows, y and t keep the whole product's
- * meaning: each rank computes its rows and an NCCL all-gather over NVLink fills y on every rank.
- * nccl_id is the 128-byte ncclUniqueId from rt_b200_nccl_id on rank 0, passed to every rank by
- * the caller. 0 or an RTB_E* code. */
+ * meaning: each rank computes its rows and y is filled on every rank over NVLink.
+ * - A single product of <= 4 tokens (rt_gemv, rt_gemm, rt_gemm_silu) gathers y in its own kernel:
+ *   every output is also stored into each peer's staging buffer (CUDA IPC mappings set up by
+ *   rt_b200_shard), the last CTA raises a flag on every peer, and a small kernel on each rank waits
+ *   for the peers' flags and copies their rows into y.
+ * - Queued rounds, t > 4 and the tensor-core path all-gather y with NCCL.
+ * All ranks must issue the same products in the same order. nccl_id is the 128-byte ncclUniqueId
+ * from rt_b200_nccl_id on rank 0, passed to every rank by the caller. 0 or an RTB_E* code.
+ * The environment variable RTB_NO_PEER_GATHER (set before rt_b200_shard) keeps every round on
+ * NCCL. rt_b200_peer_gather: 1 when the in-kernel gather is set up, else 0. */
 RTB_API int rt_b200_nccl_id(void *out128);
 RTB_API int rt_b200_shard(struct rt *R, int rank, int world, const void *nccl_id);
+RTB_API int rt_b200_peer_gather(struct rt *R);
 
 /* ---------------------------------------------------------------- synthetic inputs (benchmarks, tests)
  * Rows [row0, row0+rows) of a seeded Q8_0 matrix with w ~ sigma*N(0,1), written in the row-split

@@ -325,6 +325,27 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
         // ---------------------------------------------------------------- chain warps
         const int mt = lane / R, r = lane % R, cw = warp - CHAIN_WARP;
         float acc = 0.0f;
+        // A row-sharded launch also stores each output into every peer's staging image of this
+        // round ([t][rows_total], parity of the round being produced).
+        const PeerOut &po = p.peer;
+        unsigned long long stage_off = 0;
+        if (po.on) {
+            // the previous launch on the stream (the last round's gather) has completed: under
+            // programmatic launch this kernel may start before it does
+            grid_wait();
+            const unsigned long long round0 =
+                *reinterpret_cast<const volatile unsigned long long *>(po.region[po.rank] + 72);
+            stage_off = PEER_HDR + ((round0 + 1) & 1) * PEER_STAGE_BYTES;
+        }
+        auto put = [&](float *y, long long ldy, long long o, float v) {
+            y[mt * ldy + o] = v;
+            if (po.on) {
+                const long long gi = mt * po.rows_total + po.row0 + o;
+                for (int w = 0; w < po.world; ++w)
+                    if (w != po.rank)
+                        reinterpret_cast<float *>(po.region[w] + stage_off)[gi] = v;
+            }
+        };
         StageIter it;
         it.start(p);
         for (int s = 0, tile = 0; it.valid(p); ++s) {
@@ -373,12 +394,12 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
                         const float up = __shfl_down_sync(0xffffffffu, acc, R / 2);
                         if (mine && r < R / 2) {
                             const float silu = acc / (1.0f + expf(-acc));
-                            it.J.y[mt * it.J.ldy + o] = silu * up;
+                            put(it.J.y, it.J.ldy, o, silu * up);
                         }
                     } else if (mine) {
-                        it.J.y[mt * it.J.ldy + o] = acc;
+                        put(it.J.y, it.J.ldy, o, acc);
                     } else if (mt < it.J.m && valid) { // a gather index outside the matrix
-                        it.J.y[mt * it.J.ldy + o] = __int_as_float(0x7fc00000);
+                        put(it.J.y, it.J.ldy, o, __int_as_float(0x7fc00000));
                         report(p.err, ERR_BAD_JOB);
                     }
                 }
@@ -456,6 +477,29 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
             for (int k = max(0, s - STAGES); k < s; ++k)
                 if (!mbar_wait(&full[k % STAGES], (k / STAGES) & 1))
                     report(p.err, ERR_TIMEOUT_DRAIN);
+    }
+
+    if (p.peer.on) {
+        // The last CTA to finish publishes the round: the CTA's peer stores are ordered (barrier,
+        // then one system-scope fence) before its count, the last count before the flags.
+        __syncthreads();
+        if (tid == 0) {
+            unsigned char *mine = p.peer.region[p.peer.rank];
+            unsigned *done = reinterpret_cast<unsigned *>(mine + 64);
+            __threadfence_system();
+            if (atomicAdd(done, 1u) == gridDim.x - 1) {
+                __threadfence_system();
+                volatile unsigned long long *round = reinterpret_cast<volatile unsigned long long *>(mine + 72);
+                const unsigned long long e = *round + 1;
+                *round = e;
+                *done = 0;
+                for (int w = 0; w < p.peer.world; ++w)
+                    if (w != p.peer.rank) {
+                        unsigned long long *flag = reinterpret_cast<unsigned long long *>(p.peer.region[w]) + p.peer.rank;
+                        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(flag), "l"(e) : "memory");
+                    }
+            }
+        }
     }
 }
 

@@ -28,13 +28,41 @@ struct GemvJob {
     int tile0;          // its first tile in the launch (filled by the launcher)
 };
 
+// ---- the fused all-gather of a row-sharded product over NVLink (one job per launch)
+// Each rank owns a peer region, mapped by every other rank (CUDA IPC):
+//   [0, 64)            flags: uint64 per writer rank, the last round that rank published here
+//   [64, 68)           uint32 completion counter of the product kernel's CTAs (local use)
+//   [72, 80)           uint64 round: products completed by this rank (advanced on the device, so
+//                      CUDA-graph replays keep counting)
+//   [PEER_HDR, +2*PEER_STAGE_BYTES)  two staging images of y, [t][rows] fp32, by round parity.
+// The product kernel stores every output into its local y and into the current staging image of
+// every peer; its last CTA advances `round` and raises its flag on every peer. launch_peer_finish
+// then waits (bounded) for all peers' flags and copies their rows from staging into y.
+constexpr int MAX_PEERS = 8;
+constexpr size_t PEER_HDR = 256;
+constexpr size_t PEER_STAGE_BYTES = size_t(16) << 20;
+constexpr size_t PEER_REGION_BYTES = PEER_HDR + 2 * PEER_STAGE_BYTES;
+
+struct PeerOut {
+    unsigned char *region[MAX_PEERS]; // every rank's region as mapped on this GPU (own: local)
+    long long row0, rows_total;       // this rank's first output row; the product's rows
+    int rank, world, on;              // on = 0: an unsharded launch
+};
+
 struct GemvParams {
     GemvJob job[MAX_JOBS];
     int njobs;
     int total_tiles;
     int early;     // 1: weights may stream in before the previous kernel on the stream completes
     unsigned *err; // the context's device error word
+    PeerOut peer;  // peer.on: one job, row-sharded; y is gathered through the peers' staging
 };
+
+// After a peer-gathered launch: wait for every peer's flag of this round, then copy their rows
+// of y ([t][ldy], ldy = rows_total) from the staging image.
+// pdl: launch with programmatic stream serialization (overlaps the product's tail).
+cudaError_t launch_peer_finish(const PeerOut &po, float *y, long long ldy, int t, unsigned *err, cudaStream_t stream,
+                               bool pdl);
 
 // Launches the exact CUDA-core product over p.job[0..njobs) (all with the same m). Fills the
 // tile fields. grid_limit 0 = one CTA per SM. pdl: launch with programmatic stream serialization

@@ -7,6 +7,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <vector>
@@ -42,6 +43,11 @@ struct Ctx {
     std::vector<Item> queue;
     int rank = 0, world = 1;
     ncclComm_t comm = nullptr;
+    // the fused all-gather (q8_kernels.h, PeerOut): this rank's peer region and every rank's
+    // mapping of it here; peer_ok false means rounds all-gather through NCCL instead
+    unsigned char *peer_local = nullptr;
+    unsigned char *peer_map[q8::MAX_PEERS] = {};
+    bool peer_ok = false;
     void *scratch = nullptr; // grows on demand (the tensor-core path's fp16 x)
     size_t scratch_bytes = 0;
 };
@@ -190,7 +196,52 @@ bool flush_tc(Ctx *c, std::vector<q8::GemmJob> &jobs) {
 
 // Splits the items into kernel jobs (t >= 16: one tensor-core job; else passes of <= 4 tokens on
 // CUDA cores), launches them, then all-gathers the sharded outputs.
+// One row-sharded product of <= 4 tokens on CUDA cores, its y gathered through the peers' staging
+// images in the same launch (plus the receiving kernel), instead of an NCCL all-gather.
+bool peer_gatherable(const Ctx *c, const std::vector<Item> &items) {
+    if (c->world < 2 || !c->peer_ok || items.size() != 1)
+        return false;
+    const Item &it = items[0];
+    return it.kind != K_ROWS && it.t <= q8::GEMV_MAX_T &&
+           size_t(it.t) * size_t(it.rows) * sizeof(float) <= q8::PEER_STAGE_BYTES;
+}
+
+bool run_peer_gathered(Ctx *c, const Item &it) {
+    long long lr, r0;
+    shard_rows(c, it.rows, &lr, &r0);
+    q8::GemvParams p;
+    memset(&p, 0, sizeof p);
+    p.err = c->d_err;
+    p.early = c->overlap ? 1 : 0;
+    p.njobs = 1;
+    q8::GemvJob &j = p.job[0];
+    j.w = it.w;
+    j.w2 = it.kind == K_SILU ? it.w2 : nullptr;
+    j.x = it.x;
+    j.ldx = it.cols;
+    j.ldy = it.rows;
+    j.y = it.y + r0;
+    j.rows = lr;
+    j.src_rows = lr;
+    j.cols = int(it.cols);
+    j.m = int(it.t);
+    q8::PeerOut &po = p.peer;
+    for (int w = 0; w < c->world; ++w)
+        po.region[w] = c->peer_map[w];
+    po.row0 = r0;
+    po.rows_total = it.rows;
+    po.rank = c->rank;
+    po.world = c->world;
+    po.on = 1;
+    if (!cuda_ok(c, q8::launch_gemv(p, c->num_sms, 0, c->stream, c->overlap), "gemv launch"))
+        return false;
+    return cuda_ok(c, q8::launch_peer_finish(po, it.y, it.rows, int(it.t), c->d_err, c->stream, c->overlap),
+                   "peer gather");
+}
+
 bool run_items(Ctx *c, const std::vector<Item> &items) {
+    if (peer_gatherable(c, items))
+        return run_peer_gathered(c, items[0]);
     std::vector<q8::GemvJob> jobs;
     std::vector<q8::GemmJob> tc;
     for (const Item &it : items) {
@@ -292,6 +343,75 @@ Item make_item(Kind k, const void *w, const void *w2, const int32_t *idx, long l
 
 } // namespace
 
+namespace {
+
+void drop_peers(Ctx *c) {
+    for (int w = 0; w < q8::MAX_PEERS; ++w) {
+        if (c->peer_map[w] && c->peer_map[w] != c->peer_local)
+            cudaIpcCloseMemHandle(c->peer_map[w]);
+        c->peer_map[w] = nullptr;
+    }
+    cudaFree(c->peer_local);
+    c->peer_local = nullptr;
+    c->peer_ok = false;
+}
+
+// Maps every rank's peer region on this GPU: each rank allocates and zeroes its own, the CUDA IPC
+// handles travel through one NCCL all-gather, and each rank opens the others'. Any failure leaves
+// the fused gather off (rounds then all-gather through NCCL).
+void setup_peers(Ctx *c) {
+    drop_peers(c);
+    if (c->world < 2 || c->world > q8::MAX_PEERS)
+        return;
+    if (cudaMalloc(&c->peer_local, q8::PEER_REGION_BYTES) != cudaSuccess) {
+        c->peer_local = nullptr;
+        return;
+    }
+    cudaIpcMemHandle_t mine;
+    void *d_handles = nullptr;
+    std::vector<cudaIpcMemHandle_t> all(size_t(c->world));
+    bool ok = cudaMemset(c->peer_local, 0, q8::PEER_HDR) == cudaSuccess &&
+              cudaIpcGetMemHandle(&mine, c->peer_local) == cudaSuccess &&
+              cudaMalloc(&d_handles, sizeof(cudaIpcMemHandle_t) * size_t(c->world)) == cudaSuccess;
+    if (ok) {
+        unsigned char *slot = static_cast<unsigned char *>(d_handles) + sizeof mine * size_t(c->rank);
+        ok = cudaMemcpyAsync(slot, &mine, sizeof mine, cudaMemcpyHostToDevice, c->stream) == cudaSuccess &&
+             ncclAllGather(slot, d_handles, sizeof mine, ncclUint8, c->comm, c->stream) == ncclSuccess &&
+             cudaMemcpyAsync(all.data(), d_handles, sizeof mine * size_t(c->world), cudaMemcpyDeviceToHost, c->stream) ==
+                 cudaSuccess &&
+             cudaStreamSynchronize(c->stream) == cudaSuccess;
+    }
+    cudaFree(d_handles);
+    for (int w = 0; ok && w < c->world; ++w) {
+        if (w == c->rank) {
+            c->peer_map[w] = c->peer_local;
+            continue;
+        }
+        void *p = nullptr;
+        ok = cudaIpcOpenMemHandle(&p, all[size_t(w)], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+        c->peer_map[w] = static_cast<unsigned char *>(p);
+    }
+    // every rank's region is zeroed and mapped before any rank's first product can write to it
+    int flag = ok ? 1 : 0, *d_flag = nullptr;
+    if (cudaMalloc(&d_flag, sizeof(int)) == cudaSuccess) {
+        if (cudaMemcpyAsync(d_flag, &flag, sizeof flag, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+            ncclAllReduce(d_flag, d_flag, 1, ncclInt32, ncclMin, c->comm, c->stream) != ncclSuccess ||
+            cudaMemcpyAsync(&flag, d_flag, sizeof flag, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess ||
+            cudaStreamSynchronize(c->stream) != cudaSuccess)
+            flag = 0;
+        cudaFree(d_flag);
+    } else {
+        flag = 0;
+    }
+    cudaGetLastError(); // a failed IPC open is not the caller's error: the NCCL path stands in
+    if (flag)
+        c->peer_ok = true;
+    else
+        drop_peers(c);
+}
+
+} // namespace
+
 extern "C" {
 
 int rt_init(struct rt *R, int threads) {
@@ -325,6 +445,7 @@ void rt_b200_free(struct rt *R) {
         return;
     Ctx *c = static_cast<Ctx *>(R->chain);
     cudaStreamSynchronize(c->stream);
+    drop_peers(c);
     if (c->comm)
         ncclCommDestroy(c->comm);
     cudaFree(c->scratch);
@@ -561,6 +682,8 @@ int rt_b200_shard(struct rt *R, int rank, int world, const void *nccl_id) {
         ctx_err(c, RTB_EINVAL, "rt_b200_shard: rank %d world %d", rank, world);
         return RTB_EINVAL;
     }
+    cudaStreamSynchronize(c->stream);
+    drop_peers(c);
     if (c->comm) {
         ncclCommDestroy(c->comm);
         c->comm = nullptr;
@@ -579,7 +702,14 @@ int rt_b200_shard(struct rt *R, int rank, int world, const void *nccl_id) {
         ctx_err(c, RTB_ENCCL, "ncclCommInitRank: %s", ncclGetErrorString(e));
         return RTB_ENCCL;
     }
+    if (!getenv("RTB_NO_PEER_GATHER"))
+        setup_peers(c);
     return RTB_OK;
+}
+
+int rt_b200_peer_gather(struct rt *R) {
+    Ctx *c = ctx_of(R);
+    return c && c->peer_ok ? 1 : 0;
 }
 
 int rtb_synth_q8_0(void *dst, long row0, long rows, long cols, uint64_t seed, uint64_t stream, float sigma) {

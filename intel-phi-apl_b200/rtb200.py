@@ -26,7 +26,8 @@ ERRORS = {1: "RTB_EINVAL", 2: "RTB_ECUDA", 3: "RTB_EKERNEL", 4: "RTB_ENOMEM", 5:
 EXPORTS = ("rt_init", "rt_gemv", "rt_gemv_q", "rt_gemv_open", "rt_gemv_go", "rt_gemm", "rt_gemm_q", "rt_q8_row",
            "gemv_s_bytes", "gemv_s_repack", "rt_gemm_silu_q", "rt_gemm_silu", "rt_gemv_rows_q", "rt_gemv_rows",
            "rt_b200_last_error", "rt_b200_set_overlap", "rt_b200_set_async", "rt_b200_sync", "rt_b200_stream", "rt_b200_set_stream",
-           "rt_b200_free", "rt_b200_nccl_id", "rt_b200_shard", "rtb_synth_q8_0", "rtb_synth_f32", "rt_gemm_static")
+           "rt_b200_free", "rt_b200_nccl_id", "rt_b200_shard", "rt_b200_peer_gather", "rtb_synth_q8_0", "rtb_synth_f32",
+           "rt_gemm_static")
 
 
 class RtError(RuntimeError):
@@ -79,6 +80,7 @@ def load() -> C.CDLL:
         "rt_b200_free": ([R], None),
         "rt_b200_nccl_id": ([_P], C.c_int),
         "rt_b200_shard": ([R, C.c_int, C.c_int, _P], C.c_int),
+        "rt_b200_peer_gather": ([R], C.c_int),
         "rtb_synth_q8_0": ([_P, _L, _L, _L, C.c_uint64, C.c_uint64, C.c_float], C.c_int),
         "rtb_synth_f32": ([_P, _L, C.c_uint64, C.c_uint64, C.c_float], C.c_int),
         "rt_gemm_static": ([_P, _L, _L, _P, _L, _P, _P], C.c_int),
@@ -232,3 +234,7 @@ class Runtime:
         if code:
             _check(self)
             raise RtError(code, "rt_b200_shard")
+
+    def peer_gather(self) -> bool:
+        """True when single products gather y in their own kernel (else through NCCL)."""
+        return bool(self.lib.rt_b200_peer_gather(self._ref))

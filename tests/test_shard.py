@@ -98,20 +98,54 @@ def _gpu_rank_main(rank: int, world: int, nid: bytes, out) -> None:
     r0, n = WL.shard_rows(rows, rank, world)
     w = torch.empty(rtb200.gemv_s_bytes(n, cols), dtype=torch.uint8, device="cuda")
     rtb200.synth_q8_0(w.data_ptr(), r0, n, cols, 11, 5)
-    x = torch.from_numpy(np.stack([O.synth_f32(cols, 11, 6 + k) for k in range(t)])).cuda()
+    w2 = torch.empty_like(w)
+    rtb200.synth_q8_0(w2.data_ptr(), r0, n, cols, 11, 7)
+    x = torch.from_numpy(np.stack([O.synth_f32(cols, 11, 6 + k) for k in range(16)])).cuda()
     y = torch.full((t, rows), float("nan"), dtype=torch.float32, device="cuda")
     y1 = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
+    ys = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
+    y16 = torch.full((16, rows), float("nan"), dtype=torch.float32, device="cuda")
+    rounds = []
     with rtb200.Runtime() as rt:
         rt.shard(rank, world, nid)
+        peer = rt.peer_gather()
         rt.gemm(w.data_ptr(), rows, cols, x.data_ptr(), t, y.data_ptr())
         rt.gemv(w.data_ptr(), rows, cols, x.data_ptr(), y1.data_ptr())
-    out.put((rank, y.cpu().numpy(), y1.cpu().numpy()))
+        rt.gemm_silu(w.data_ptr(), w2.data_ptr(), rows, cols, x.data_ptr(), 1, ys.data_ptr())
+        rt.gemm(w.data_ptr(), rows, cols, x.data_ptr(), 16, y16.data_ptr())  # tensor cores, NCCL gather
+        # rounds back to back (alternating staging images), each on its own x row
+        for k in range(5):
+            yk = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
+            rt.gemv(w.data_ptr(), rows, cols, x[k].data_ptr(), yk.data_ptr())
+            rounds.append(yk)
+        # one round captured as a CUDA graph and replayed twice: the round count lives on the GPU
+        yg = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
+        rt.set_async(True)
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                rt.set_stream(torch.cuda.current_stream().cuda_stream)
+                rt.gemv(w.data_ptr(), rows, cols, x[6].data_ptr(), yg.data_ptr())
+        torch.cuda.current_stream().wait_stream(s)
+        rt.set_stream(torch.cuda.current_stream().cuda_stream)
+        for _ in range(2):
+            yg.fill_(float("nan"))
+            g.replay()
+            torch.cuda.synchronize()
+        rt.sync()
+        del g
+    out.put((rank, peer, y.cpu().numpy(), y1.cpu().numpy(), ys.cpu().numpy(), y16.cpu().numpy(),
+             [r.cpu().numpy() for r in rounds], yg.cpu().numpy()))
 
 
 @pytest.mark.gpu
-def test_nccl_row_shards_on_two_gpus(cuda, rtb, oracle):
-    """rt_b200_shard on 2 GPUs: each rank computes its rows, NCCL all-gathers y; every rank
-    ends with the whole product, bit for bit."""
+def test_row_shards_on_two_gpus(cuda, rtb, oracle):
+    """rt_b200_shard on 2 GPUs: each rank computes its rows and y is gathered over NVLink, in
+    the product's own kernel for single products of <= 4 tokens (peer stores + flags), through
+    NCCL for the tensor-core path. Every rank ends with the whole product, bit for bit (the
+    tensor-core one within its tolerance), over repeated rounds and CUDA-graph replays."""
     if cuda.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     world = 2
@@ -127,8 +161,20 @@ def test_nccl_row_shards_on_two_gpus(cuda, rtb, oracle):
         assert p.exitcode == 0
     rows, cols, t = 8192, 4096, 2
     q8 = oracle.synth_q8_0(rows, cols, 11, 5)
-    x = np.stack([oracle.synth_f32(cols, 11, 6 + k) for k in range(t)])
-    want = oracle.gemm(q8, rows, cols, x, t)
-    for _, y, y1 in res:
+    q8u = oracle.synth_q8_0(rows, cols, 11, 7)
+    x = np.stack([oracle.synth_f32(cols, 11, 6 + k) for k in range(16)])
+    want = oracle.gemm(q8, rows, cols, x[:t], t)
+    g = oracle.gemv(q8, rows, cols, x[0])
+    u = oracle.gemv(q8u, rows, cols, x[0])
+    want_silu = (g / (1.0 + np.exp(-g.astype(np.float64))) * u).astype(np.float32)
+    want16 = oracle.gemm_f64(q8, rows, cols, x, 16)
+    for _, peer, y, y1, ys, y16, rounds, yg in res:
+        assert peer, "the in-kernel gather was not set up"
         assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
         assert np.array_equal(y1.view(np.uint32), want[0].view(np.uint32))
+        assert np.max(np.abs(ys - want_silu) / np.maximum(np.abs(want_silu), 1e-3)) < 1e-4
+        rms = np.sqrt(np.mean(want16 ** 2))
+        assert np.max(np.abs(y16 - want16)) / rms < 2e-3
+        for k, yk in enumerate(rounds):
+            assert np.array_equal(yk.view(np.uint32), oracle.gemv(q8, rows, cols, x[k]).view(np.uint32))
+        assert np.array_equal(yg.view(np.uint32), oracle.gemv(q8, rows, cols, x[6]).view(np.uint32))
