@@ -177,6 +177,19 @@ RTB_API int rt_b200_nccl_id(void *out128);
 RTB_API int rt_b200_shard(struct rt *R, int rank, int world, const void *nccl_id);
 RTB_API int rt_b200_peer_gather(struct rt *R);
 
+/* ---------------------------------------------------------------- chains: rounds in one launch
+ * Between rt_b200_chain_begin and rt_b200_chain_end, products (rt_gemv, rt_gemm, rt_gemm_silu,
+ * rt_gemv_rows) and queued rounds (rt_gemv_go) are recorded, not run: each call or go is one round.
+ * rt_b200_chain_end runs them in order as ONE persistent launch per 160 products (one decode step
+ * is 129 rounds): weights stream across round boundaries with no launch in between, and a round
+ * that reads an earlier round's y waits for that round on the GPU before reading x. serial != 0
+ * makes every round wait for the one before (a decode step's dependency chain); serial == 0
+ * derives the waits from overlapping x and y ranges. Rounds that cannot chain (t > 4, the
+ * tensor-core path, several GPUs) run as separate launches in the same order. Blocking mode
+ * waits at rt_b200_chain_end. 0 or an RTB_E* code. */
+RTB_API int rt_b200_chain_begin(struct rt *R);
+RTB_API int rt_b200_chain_end(struct rt *R, int serial);
+
 /* ---------------------------------------------------------------- synthetic inputs (benchmarks, tests)
  * Rows [row0, row0+rows) of a seeded Q8_0 matrix with w ~ sigma*N(0,1), written in the row-split
  * layout to dst (device); and n seeded fp32 values ~ sigma*N(0,1). The values are the same bits

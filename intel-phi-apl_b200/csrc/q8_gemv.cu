@@ -79,8 +79,8 @@ template <int MT, int CTAS>
 constexpr size_t smem_bytes() {
     using C = Cfg<MT, CTAS>;
     static_assert(FRING >= C::STAGES + C::TBUF + 2, "row-flag ring");
-    return size_t(C::STAGES) * SLOT + size_t(C::TBUF) * (MT + 1) * R * TPAD * 4 + (C::STAGES * 2 + C::TBUF * 2) * 8 +
-           FRING * R;
+    return size_t(C::STAGES) * SLOT + size_t(C::TBUF) * (MT + 1) * R * TPAD * 4 +
+           (C::STAGES * 2 + C::TBUF * 2 + 1) * 8 + FRING * R;
 }
 
 // One job's fields, cached in registers by every role when its stage sequence enters the job:
@@ -90,9 +90,17 @@ struct JobView {
     const int32_t *idx;
     const float *x;
     float *y;
+    unsigned *done_ctr;
+    const unsigned *wait_ctr;
+    unsigned wait_target;
+    int x_written;
     long long rows, src_rows, ldx, ldy, rb;
     int cols, m, tile0, rpt, nchunk;
     __device__ __forceinline__ void load(const GemvJob &J) {
+        done_ctr = J.done_ctr;
+        wait_ctr = J.wait_ctr;
+        wait_target = J.wait_target;
+        x_written = J.x_written;
         w = J.w;
         w2 = J.w2;
         idx = J.idx;
@@ -116,14 +124,16 @@ struct JobView {
 struct StageIter {
     int g, c, job;
     JobView J;
-    __device__ __forceinline__ void start(const GemvParams &p) {
+    template <class P>
+    __device__ __forceinline__ void start(const P &p) {
         g = blockIdx.x;
         c = 0;
         job = -1;
         if (g < p.total_tiles)
             set(p);
     }
-    __device__ __forceinline__ void set(const GemvParams &p) {
+    template <class P>
+    __device__ __forceinline__ void set(const P &p) {
         int j = job < 0 ? 0 : job;
         while (j + 1 < p.njobs && g >= p.job[j + 1].tile0)
             ++j;
@@ -132,8 +142,10 @@ struct StageIter {
             J.load(p.job[j]);
         }
     }
-    __device__ __forceinline__ bool valid(const GemvParams &p) const { return g < p.total_tiles; }
-    __device__ __forceinline__ void next(const GemvParams &p) {
+    template <class P>
+    __device__ __forceinline__ bool valid(const P &p) const { return g < p.total_tiles; }
+    template <class P>
+    __device__ __forceinline__ void next(const P &p) {
         if (++c == J.nchunk) {
             c = 0;
             g += gridDim.x;
@@ -202,8 +214,24 @@ __device__ __forceinline__ void block_chains(const uint32_t (&wq)[RG][8], const 
     }
 }
 
-template <int MT, int CTAS>
-__global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(const __grid_constant__ GemvParams p) {
+// Waits until *ctr >= target (an acquire at GPU scope), bounded like every wait here.
+__device__ __noinline__ bool wait_count(const unsigned *ctr, unsigned target) {
+    const long long t0 = clock64();
+    for (;;) {
+        unsigned v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+        if (v >= target)
+            return true;
+        const long long dt = clock64() - t0;
+        if (dt > WAIT_LIMIT_CYCLES)
+            return false;
+        if (dt > 20000) // past ~10 us, poll less often
+            __nanosleep(200);
+    }
+}
+
+template <int MT, int CTAS, class P>
+__global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(const __grid_constant__ P p) {
     using C = Cfg<MT, CTAS>;
     constexpr int STAGES = C::STAGES, TBUF = C::TBUF, NCHAIN = C::NCHAIN, COPY_WARP = C::COPY_WARP;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -214,7 +242,8 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
     uint64_t *empty = full + STAGES;                                      // [STAGES]
     uint64_t *tfull = empty + STAGES;                                     // [TBUF]
     uint64_t *tempty = tfull + TBUF;                                      // [TBUF]
-    uint8_t *rowflag = reinterpret_cast<uint8_t *>(tempty + TBUF);        // [FRING][R]: row was loaded
+    uint64_t *depbar = tempty + TBUF;                                     // a chained round's dependency met
+    uint8_t *rowflag = reinterpret_cast<uint8_t *>(depbar + 1);           // [FRING][R]: row was loaded
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
 
     if (tid == 0) {
@@ -226,6 +255,7 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
             mbar_init(&tfull[b], NC);
             mbar_init(&tempty[b], 1);
         }
+        mbar_init(depbar, 1);
         fence_barrier_init();
         grid_launch_dependents();
     }
@@ -234,7 +264,7 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
     if (warp < CHAIN_WARP) {
         // ---------------------------------------------------------------- compute threads
         float xr[MT][Q8_QK];
-        int xjob = -1, xc = -1;
+        int xjob = -1, xc = -1, wjob = -1, ndep = 0;
         const int b = tid % NBK, half = tid / NBK;
         grid_wait(); // x comes from the previous kernel on the stream
         StageIter it;
@@ -248,15 +278,34 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
             const int c0 = it.c * KC;
             const int nbk = min(KC, it.J.cols - c0) / Q8_QK;
             const bool active = b < nbk;
+            if (it.job != wjob) {
+                // A chained job that depends on an earlier round: its x is that round's output,
+                // written during this launch. Compute thread 0 alone polls the round's counter
+                // (bounded, an acquire at GPU scope) and passes it on through a CTA barrier that
+                // the other compute warps wait on, bounded like every wait here.
+                wjob = it.job;
+                if (it.J.wait_ctr) {
+                    if (tid == 0) {
+                        if (!wait_count(it.J.wait_ctr, it.J.wait_target))
+                            report(p.err, ERR_TIMEOUT_ROUND);
+                        mbar_arrive(depbar);
+                    } else if (lane == 0 && !mbar_wait(depbar, ndep & 1)) {
+                        report(p.err, ERR_TIMEOUT_ROUND);
+                    }
+                    ++ndep;
+                    __syncwarp();
+                }
+            }
             if (active && (it.c != xc || it.job != xjob)) {
                 xc = it.c;
                 xjob = it.job;
+                const bool coherent = it.J.x_written != 0; // x written earlier in this launch: not via L1
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt) {
                     const float4 *xp = reinterpret_cast<const float4 *>(it.J.x + mt * it.J.ldx + c0 + b * Q8_QK);
 #pragma unroll
                     for (int v = 0; v < 8; ++v) {
-                        const float4 f = __ldg(xp + v);
+                        const float4 f = coherent ? __ldcg(xp + v) : __ldg(xp + v);
                         xr[mt][4 * v + 0] = f.x;
                         xr[mt][4 * v + 1] = f.y;
                         xr[mt][4 * v + 2] = f.z;
@@ -402,6 +451,12 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
                         put(it.J.y, it.J.ldy, o, __int_as_float(0x7fc00000));
                         report(p.err, ERR_BAD_JOB);
                     }
+                    if (it.J.done_ctr) { // chained: the tile's outputs, then its count (release)
+                        __threadfence();
+                        __syncwarp();
+                        if (lane == 0)
+                            atomicAdd(it.J.done_ctr, 1u);
+                    }
                 }
             }
             if (last_chunk)
@@ -503,18 +558,18 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
     }
 }
 
-template <int MT, int CTAS>
-cudaError_t launch_mt(const GemvParams &p, int num_sms, int grid_limit, cudaStream_t stream, bool pdl) {
+template <int MT, int CTAS, class P = GemvParams>
+cudaError_t launch_mt(const P &p, int num_sms, int grid_limit, cudaStream_t stream, bool pdl, bool coop = false) {
     using C = Cfg<MT, CTAS>;
     const size_t smem = smem_bytes<MT, CTAS>();
     static int per_sm = 0; // CTAs that fit on one SM (per process; the attribute is per function)
     if (per_sm == 0) {
-        cudaError_t e =
-            cudaFuncSetAttribute(gemv_exact_kernel<MT, CTAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        cudaError_t e = cudaFuncSetAttribute(gemv_exact_kernel<MT, CTAS, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             int(smem));
         if (e != cudaSuccess)
             return e;
         int n = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_exact_kernel<MT, CTAS>, C::NT, smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_exact_kernel<MT, CTAS, P>, C::NT, smem);
         if (e != cudaSuccess)
             return e;
         if (n < 1)
@@ -524,7 +579,7 @@ cudaError_t launch_mt(const GemvParams &p, int num_sms, int grid_limit, cudaStre
     int grid = per_sm * (num_sms > 0 ? num_sms : 148);
     if (grid_limit > 0 && grid > grid_limit)
         grid = grid_limit;
-    if (grid > p.total_tiles)
+    if (grid > p.total_tiles && !coop)
         grid = p.total_tiles;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -532,25 +587,34 @@ cudaError_t launch_mt(const GemvParams &p, int num_sms, int grid_limit, cudaStre
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    if (coop) {
+        // every CTA resident at once: a chained round waits on other CTAs' tiles
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+    } else {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_exact_kernel<MT, CTAS>, p);
+    cfg.numAttrs = (pdl || coop) ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemv_exact_kernel<MT, CTAS, P>, p);
 }
 
 } // namespace
 
-cudaError_t launch_gemv(GemvParams &p, int num_sms, int grid_limit, cudaStream_t stream, bool pdl) {
-    if (p.njobs < 1 || p.njobs > MAX_JOBS)
-        return cudaErrorInvalidValue;
+// Tile bookkeeping shared by both launchers: checks the jobs, fills tiles / tile0 / total_tiles,
+// and returns the stages (tile x chunk) of the launch (-1 for an invalid job list).
+template <class P>
+long long plan_tiles(P &p, int max_jobs) {
+    if (p.njobs < 1 || p.njobs > max_jobs)
+        return -1;
     const int m = p.job[0].m;
     int tiles = 0;
     long long stages = 0;
     for (int j = 0; j < p.njobs; ++j) {
         GemvJob &J = p.job[j];
         if (J.m != m || J.m < 1 || J.m > GEMV_MAX_T || J.cols < Q8_QK || J.cols % Q8_QK || J.rows < 1)
-            return cudaErrorInvalidValue;
+            return -1;
         const long long rpt = J.w2 ? R / 2 : R;
         J.tiles = int((J.rows + rpt - 1) / rpt);
         J.tile0 = tiles;
@@ -558,14 +622,32 @@ cudaError_t launch_gemv(GemvParams &p, int num_sms, int grid_limit, cudaStream_t
         stages += (long long)J.tiles * ((J.cols + KC - 1) / KC);
     }
     p.total_tiles = tiles;
+    return stages;
+}
+
+cudaError_t launch_gemv(GemvParams &p, int num_sms, int grid_limit, cudaStream_t stream, bool pdl) {
+    const long long stages = plan_tiles(p, MAX_JOBS);
+    if (stages < 0)
+        return cudaErrorInvalidValue;
     const int sms = num_sms > 0 ? num_sms : 148;
-    switch (m) {
+    switch (p.job[0].m) {
     case 1:
         return stages >= (long long)TWO_CTA_MIN_STAGES_PER_SM * sms ? launch_mt<1, 2>(p, num_sms, grid_limit, stream, pdl)
                                                                     : launch_mt<1, 1>(p, num_sms, grid_limit, stream, pdl);
     case 2: return launch_mt<2, 1>(p, num_sms, grid_limit, stream, pdl);
     case 3: return launch_mt<3, 1>(p, num_sms, grid_limit, stream, pdl);
     default: return launch_mt<4, 1>(p, num_sms, grid_limit, stream, pdl);
+    }
+}
+
+cudaError_t launch_gemv_chain(ChainParams &p, int num_sms, cudaStream_t stream) {
+    if (plan_tiles(p, MAX_CHAIN_JOBS) < 0)
+        return cudaErrorInvalidValue;
+    switch (p.job[0].m) {
+    case 1: return launch_mt<1, 1, ChainParams>(p, num_sms, 0, stream, false, true);
+    case 2: return launch_mt<2, 1, ChainParams>(p, num_sms, 0, stream, false, true);
+    case 3: return launch_mt<3, 1, ChainParams>(p, num_sms, 0, stream, false, true);
+    default: return launch_mt<4, 1, ChainParams>(p, num_sms, 0, stream, false, true);
     }
 }
 

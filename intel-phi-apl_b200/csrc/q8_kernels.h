@@ -26,7 +26,17 @@ struct GemvJob {
     int m;              // tokens, 1..GEMV_MAX_T
     int tiles;          // row tiles of this job (filled by the launcher)
     int tile0;          // its first tile in the launch (filled by the launcher)
+    // Chained launches (launch_gemv_chain): the job's round counts its finished row tiles into
+    // done_ctr; with wait_ctr set, the job reads x only once *wait_ctr >= wait_target (the tiles
+    // of the round it depends on). Null in plain launches.
+    unsigned *done_ctr;
+    const unsigned *wait_ctr;
+    unsigned wait_target;
+    int x_written;      // chained: x overlaps a y written earlier in the launch (read it past L1)
 };
+// Chained launches' round counters sit one per 128-byte line (pollers and the tile counts of
+// other rounds do not share it).
+constexpr int ROUND_CTR_STRIDE = 32;
 
 // ---- the fused all-gather of a row-sharded product over NVLink (one job per launch)
 // Each rank owns a peer region, mapped by every other rank (CUDA IPC):
@@ -49,14 +59,25 @@ struct PeerOut {
     int rank, world, on;              // on = 0: an unsharded launch
 };
 
-struct GemvParams {
-    GemvJob job[MAX_JOBS];
+template <int NJ>
+struct GemvParamsT {
+    GemvJob job[NJ];
     int njobs;
     int total_tiles;
     int early;     // 1: weights may stream in before the previous kernel on the stream completes
     unsigned *err; // the context's device error word
     PeerOut peer;  // peer.on: one job, row-sharded; y is gathered through the peers' staging
 };
+using GemvParams = GemvParamsT<MAX_JOBS>;
+
+// A chain: a sequence of rounds (each one or more jobs, all with the same m) in ONE persistent,
+// cooperative launch. Weights stream across round boundaries without a launch in between; a
+// round that depends on an earlier one waits on the device for that round's tiles (bounded)
+// before it reads x. 160 jobs fit the kernel parameters (one decode step is 129 rounds).
+constexpr int MAX_CHAIN_JOBS = 160;
+using ChainParams = GemvParamsT<MAX_CHAIN_JOBS>;
+// Fills the tile fields (the done/wait fields are the caller's). One CTA shape for the chain.
+cudaError_t launch_gemv_chain(ChainParams &p, int num_sms, cudaStream_t stream);
 
 // After a peer-gathered launch: wait for every peer's flag of this round, then copy their rows
 // of y ([t][ldy], ldy = rows_total) from the staging image.

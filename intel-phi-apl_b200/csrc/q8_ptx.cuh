@@ -15,6 +15,7 @@ enum : unsigned {
     ERR_TIMEOUT_DRAIN = 1u << 4,  // copies in flight at exit never completed
     ERR_BAD_JOB = 1u << 5,        // a job the kernel cannot run (host checks missed it)
     ERR_TIMEOUT_PEER = 1u << 6,   // a peer GPU's flag never arrived
+    ERR_TIMEOUT_ROUND = 1u << 7,  // a chained round's dependency never completed
 };
 
 // A spin of about this many SM clocks (~1 s at 2 GHz) is a hang, not a slow GPU.

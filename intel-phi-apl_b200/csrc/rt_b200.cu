@@ -50,6 +50,11 @@ struct Ctx {
     bool peer_ok = false;
     void *scratch = nullptr; // grows on demand (the tensor-core path's fp16 x)
     size_t scratch_bytes = 0;
+    // chains (rt_b200_chain_begin .. rt_b200_chain_end): recorded rounds, and the device counters
+    // of their finished tiles (one per round of a launch)
+    bool chaining = false;
+    std::vector<std::vector<Item>> chain;
+    unsigned *d_round = nullptr;
 };
 
 // Errors of the calls that take no struct rt.
@@ -313,7 +318,100 @@ bool run_items(Ctx *c, const std::vector<Item> &items) {
 
 bool run_now(Ctx *c, const Item &it) {
     std::vector<Item> one(1, it);
+    if (c->chaining) {
+        c->chain.push_back(one);
+        return true;
+    }
     return run_items(c, one) && finish(c);
+}
+
+// ---------------------------------------------------------------- chains
+
+bool overlaps(const void *a, size_t na, const void *b, size_t nb) {
+    const uintptr_t a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
+    return a0 < b0 + nb && b0 < a0 + na;
+}
+
+// Whether the recorded rounds can run as chained launches: every product on CUDA cores with the
+// same number of tokens (<= 4), one GPU, and no gather list written inside the chain.
+bool chainable(const Ctx *c) {
+    if (c->world > 1 || c->chain.empty())
+        return false;
+    const long long t = c->chain[0][0].t;
+    for (size_t r = 0; r < c->chain.size(); ++r)
+        for (const Item &it : c->chain[r]) {
+            if (it.t != t || it.t > q8::GEMV_MAX_T)
+                return false;
+            if (it.idx)
+                for (size_t q = 0; q < c->chain.size(); ++q)
+                    for (const Item &o : c->chain[q])
+                        if (overlaps(it.idx, size_t(it.rows) * 4, o.y, size_t(o.rows * o.t) * 4))
+                            return false;
+        }
+    return true;
+}
+
+long long item_tiles(const Item &it) { return (it.rows + (it.kind == K_SILU ? 3 : 7)) / (it.kind == K_SILU ? 4 : 8); }
+
+// One chained launch per <= MAX_CHAIN_JOBS jobs. Round r's jobs count their tiles into d_round[r];
+// a round waits for the latest earlier round of the same launch whose y its x (or, with serial,
+// simply the previous round) overlaps. Rounds in different launches are ordered by the stream.
+bool run_chain(Ctx *c, bool serial) {
+    const size_t nr = c->chain.size();
+    size_t r = 0;
+    while (r < nr) {
+        q8::ChainParams p;
+        memset(&p, 0, sizeof p);
+        p.err = c->d_err;
+        const size_t r0 = r;
+        std::vector<long long> round_tiles;
+        for (; r < nr && p.njobs + int(c->chain[r].size()) <= q8::MAX_CHAIN_JOBS; ++r) {
+            const size_t lr = r - r0; // round index inside this launch
+            long long tiles = 0;
+            int wait = -1;
+            for (const Item &it : c->chain[r]) {
+                tiles += item_tiles(it);
+                if (serial && lr > 0)
+                    wait = int(lr) - 1;
+                for (size_t q = r0; !serial && q < r; ++q)
+                    for (const Item &o : c->chain[q])
+                        if (overlaps(it.x, size_t(it.t * it.cols) * 4, o.y, size_t(o.t * o.rows) * 4) && int(q - r0) > wait)
+                            wait = int(q - r0);
+            }
+            for (const Item &it : c->chain[r]) {
+                q8::GemvJob &j = p.job[p.njobs++];
+                j.w = it.w;
+                j.w2 = it.kind == K_SILU ? it.w2 : nullptr;
+                j.idx = it.kind == K_ROWS ? it.idx : nullptr;
+                j.x = it.x;
+                j.ldx = it.cols;
+                j.ldy = it.rows;
+                j.y = it.y;
+                j.rows = it.rows;
+                j.src_rows = it.kind == K_ROWS ? it.src_rows : it.rows;
+                j.cols = int(it.cols);
+                j.m = int(it.t);
+                j.done_ctr = c->d_round + q8::ROUND_CTR_STRIDE * lr;
+                j.wait_ctr = wait >= 0 ? c->d_round + q8::ROUND_CTR_STRIDE * wait : nullptr;
+                j.wait_target = wait >= 0 ? unsigned(round_tiles[size_t(wait)]) : 0u;
+                j.x_written = 0;
+                for (size_t q = 0; q < r && !j.x_written; ++q) // any earlier round of the chain
+                    for (const Item &o : c->chain[q])
+                        if (overlaps(it.x, size_t(it.t * it.cols) * 4, o.y, size_t(o.t * o.rows) * 4))
+                            j.x_written = 1;
+            }
+            round_tiles.push_back(tiles);
+        }
+        if (r == r0) {
+            ctx_err(c, RTB_EINVAL, "chain: a round of more than %d products", q8::MAX_CHAIN_JOBS);
+            return false;
+        }
+        if (!cuda_ok(c, cudaMemsetAsync(c->d_round, 0, sizeof(unsigned) * q8::ROUND_CTR_STRIDE * (r - r0), c->stream),
+                     "round counters") ||
+            !cuda_ok(c, q8::launch_gemv_chain(p, c->num_sms, c->stream), "chained launch"))
+            return false;
+    }
+    return true;
 }
 
 bool enqueue(Ctx *c, const Item &it) {
@@ -427,7 +525,10 @@ int rt_init(struct rt *R, int threads) {
         return -1;
     }
     c->stream = c->own_stream;
-    if (cudaMalloc(&c->d_err, sizeof(unsigned)) != cudaSuccess || cudaMemset(c->d_err, 0, sizeof(unsigned)) != cudaSuccess) {
+    if (cudaMalloc(&c->d_err, sizeof(unsigned)) != cudaSuccess || cudaMemset(c->d_err, 0, sizeof(unsigned)) != cudaSuccess ||
+        cudaMalloc(&c->d_round, sizeof(unsigned) * q8::ROUND_CTR_STRIDE * q8::MAX_CHAIN_JOBS) != cudaSuccess) {
+        // (the chains' round counters: allocated here, so a chain can be captured in a graph)
+        cudaFree(c->d_err);
         cudaStreamDestroy(c->own_stream);
         delete c;
         return -1;
@@ -448,6 +549,7 @@ void rt_b200_free(struct rt *R) {
     drop_peers(c);
     if (c->comm)
         ncclCommDestroy(c->comm);
+    cudaFree(c->d_round);
     cudaFree(c->scratch);
     cudaFree(c->d_err);
     cudaStreamDestroy(c->own_stream);
@@ -487,7 +589,13 @@ void rt_gemv_go(struct rt *R) {
         return;
     std::vector<Item> items;
     items.swap(c->queue);
-    if (!items.empty() && run_items(c, items))
+    if (items.empty())
+        return;
+    if (c->chaining) {
+        c->chain.push_back(items);
+        return;
+    }
+    if (run_items(c, items))
         finish(c);
 }
 
@@ -705,6 +813,48 @@ int rt_b200_shard(struct rt *R, int rank, int world, const void *nccl_id) {
     if (!getenv("RTB_NO_PEER_GATHER"))
         setup_peers(c);
     return RTB_OK;
+}
+
+int rt_b200_chain_begin(struct rt *R) {
+    Ctx *c = ctx_of(R);
+    if (!c)
+        return RTB_ENOTINIT;
+    if (c->chaining || !c->queue.empty()) {
+        ctx_err(c, RTB_EINVAL, "rt_b200_chain_begin: a chain or a queued round is open");
+        return RTB_EINVAL;
+    }
+    c->chaining = true;
+    c->chain.clear();
+    return RTB_OK;
+}
+
+int rt_b200_chain_end(struct rt *R, int serial) {
+    Ctx *c = ctx_of(R);
+    if (!c)
+        return RTB_ENOTINIT;
+    if (!c->chaining) {
+        ctx_err(c, RTB_EINVAL, "rt_b200_chain_end without rt_b200_chain_begin");
+        return RTB_EINVAL;
+    }
+    c->chaining = false;
+    std::vector<std::vector<Item>> rounds;
+    rounds.swap(c->chain);
+    if (rounds.empty())
+        return RTB_OK;
+    bool ok;
+    c->chain.swap(rounds);
+    if (chainable(c)) {
+        ok = run_chain(c, serial != 0);
+        c->chain.clear();
+    } else { // not chainable: the rounds run one launch (and gather) each, in order
+        rounds.swap(c->chain);
+        ok = true;
+        for (size_t r = 0; ok && r < rounds.size(); ++r)
+            ok = run_items(c, rounds[r]);
+    }
+    if (ok)
+        ok = finish(c);
+    return ok ? RTB_OK : (c->status != RTB_OK ? c->status : RTB_ECUDA);
 }
 
 int rt_b200_peer_gather(struct rt *R) {

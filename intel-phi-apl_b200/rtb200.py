@@ -26,8 +26,8 @@ ERRORS = {1: "RTB_EINVAL", 2: "RTB_ECUDA", 3: "RTB_EKERNEL", 4: "RTB_ENOMEM", 5:
 EXPORTS = ("rt_init", "rt_gemv", "rt_gemv_q", "rt_gemv_open", "rt_gemv_go", "rt_gemm", "rt_gemm_q", "rt_q8_row",
            "gemv_s_bytes", "gemv_s_repack", "rt_gemm_silu_q", "rt_gemm_silu", "rt_gemv_rows_q", "rt_gemv_rows",
            "rt_b200_last_error", "rt_b200_set_overlap", "rt_b200_set_async", "rt_b200_sync", "rt_b200_stream", "rt_b200_set_stream",
-           "rt_b200_free", "rt_b200_nccl_id", "rt_b200_shard", "rt_b200_peer_gather", "rtb_synth_q8_0", "rtb_synth_f32",
-           "rt_gemm_static")
+           "rt_b200_free", "rt_b200_nccl_id", "rt_b200_shard", "rt_b200_peer_gather", "rt_b200_chain_begin",
+           "rt_b200_chain_end", "rtb_synth_q8_0", "rtb_synth_f32", "rt_gemm_static")
 
 
 class RtError(RuntimeError):
@@ -81,6 +81,8 @@ def load() -> C.CDLL:
         "rt_b200_nccl_id": ([_P], C.c_int),
         "rt_b200_shard": ([R, C.c_int, C.c_int, _P], C.c_int),
         "rt_b200_peer_gather": ([R], C.c_int),
+        "rt_b200_chain_begin": ([R], C.c_int),
+        "rt_b200_chain_end": ([R, C.c_int], C.c_int),
         "rtb_synth_q8_0": ([_P, _L, _L, _L, C.c_uint64, C.c_uint64, C.c_float], C.c_int),
         "rtb_synth_f32": ([_P, _L, C.c_uint64, C.c_uint64, C.c_float], C.c_int),
         "rt_gemm_static": ([_P, _L, _L, _P, _L, _P, _P], C.c_int),
@@ -234,6 +236,18 @@ class Runtime:
         if code:
             _check(self)
             raise RtError(code, "rt_b200_shard")
+
+    def chain_begin(self) -> None:
+        code = self.lib.rt_b200_chain_begin(self._ref)
+        if code:
+            _check(self)
+            raise RtError(code, "rt_b200_chain_begin")
+
+    def chain_end(self, serial: bool = True) -> None:
+        code = self.lib.rt_b200_chain_end(self._ref, 1 if serial else 0)
+        if code:
+            _check(self)
+            raise RtError(code, "rt_b200_chain_end")
 
     def peer_gather(self) -> bool:
         """True when single products gather y in their own kernel (else through NCCL)."""
