@@ -190,6 +190,44 @@ RTB_API int rt_b200_peer_gather(struct rt *R);
 RTB_API int rt_b200_chain_begin(struct rt *R);
 RTB_API int rt_b200_chain_end(struct rt *R, int serial);
 
+/* ---------------------------------------------------------------- the weight loader
+ * A GGUF file into device memory, its Q8_0 matrices repacked in place into the row-split layout
+ * (the engine's load step: src/card/engine.c:268-330, src/card/stream.c:77-104).
+ * rtb_gguf_info parses the header only (host): the tensor table and the file size.
+ * rt_b200_load_gguf reads the whole file into `arena` (device, >= the file size rounded up to 8,
+ * 256-byte aligned) through page-aligned O_DIRECT reads into pinned buffers (buffered reads where
+ * the file system refuses O_DIRECT), each slot's copy to the GPU overlapping the next read; then
+ * computes the file's position-weighted sum (sum of word_i * (2i+1) mod 2^64 over 8-byte words,
+ * src/bench/arena.h:26-44) on the GPU, and repacks every Q8_0 matrix whose rows keep their length
+ * (cols % 256 == 0) in place, each distinct offset once. Tensor i is at arena + out[i].offset
+ * (out[i].dev). Other types are left as they are in the file. 0 or an RTB_E* code;
+ * rtb_load_error() tells what failed. */
+typedef struct rtb_tensor {
+    char name[96];
+    int type;                  /* GGML type: 0 F32, 1 F16, 8 Q8_0, 30 BF16 */
+    int n_dims;
+    long long dim[4];          /* dim[0]: the fastest (columns) */
+    unsigned long long offset; /* from the start of the file */
+    unsigned long long bytes;
+    void *dev;                 /* rt_b200_load_gguf: the tensor in the arena */
+    int repacked;              /* 1: a Q8_0 matrix now in the row-split layout */
+    int pad_;
+} rtb_tensor;
+
+typedef struct rtb_load_stats {
+    unsigned long long file_bytes;
+    unsigned long long file_sum; /* the position-weighted sum of the file */
+    double seconds;              /* open to the end of the repack */
+    double seconds_repack;       /* the sum and the repacks on the GPU, after the last copy */
+    int direct;                  /* 1: the reads bypassed the page cache (O_DIRECT) */
+    int q8_matrices;             /* Q8_0 matrices repacked */
+} rtb_load_stats;
+
+RTB_API int rtb_gguf_info(const char *path, rtb_tensor *out, int cap, int *n, unsigned long long *file_bytes);
+RTB_API int rt_b200_load_gguf(struct rt *R, const char *path, void *arena, unsigned long long arena_bytes,
+                              rtb_tensor *out, int cap, int *n, rtb_load_stats *stats);
+RTB_API const char *rtb_load_error(void);
+
 /* ---------------------------------------------------------------- synthetic inputs (benchmarks, tests)
  * Rows [row0, row0+rows) of a seeded Q8_0 matrix with w ~ sigma*N(0,1), written in the row-split
  * layout to dst (device); and n seeded fp32 values ~ sigma*N(0,1). The values are the same bits

@@ -26,7 +26,7 @@ FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", 
          "--expt-relaxed-constexpr", "-I", os.path.join(ROOT, "include"), "-I", CSRC]
 # The exact products depend on IEEE fp32 fma and division: no fast-math, no flush-to-zero.
 FLAGS += ["-fmad=true", "-ftz=false", "-prec-div=true", "-prec-sqrt=true"]
-LIBS = ["-lcudart", "-lnccl"]
+LIBS = ["-lcudart", "-ldl"]  # NCCL is opened at run time, on first use
 
 
 def _newer(target: str, deps: list[str]) -> bool:

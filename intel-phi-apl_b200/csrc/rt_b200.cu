@@ -3,18 +3,60 @@
 // error state. The reference's counterparts are src/card/rt.c:179-285 (products) and 484-501
 // (rt_q8_row); there the work runs on a thread team, here on the GPU.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
 #include <nccl.h>
 
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <vector>
 
 #include "../../include/rt_b200.h"
 #include "q8_kernels.h"
 #include "q8_layout.h"
+
+// NCCL is resolved at run time, on first use (rt_b200_shard, rt_b200_nccl_id): loading this library
+// loads no NCCL, and a process that already holds one (PyTorch bundles its own) shares it.
+namespace {
+struct Nccl {
+    bool tried = false, ok = false;
+    decltype(&ncclGetUniqueId) GetUniqueId = nullptr;
+    decltype(&ncclCommInitRank) CommInitRank = nullptr;
+    decltype(&ncclCommDestroy) CommDestroy = nullptr;
+    decltype(&ncclAllGather) AllGather = nullptr;
+    decltype(&ncclAllReduce) AllReduce = nullptr;
+    decltype(&ncclGroupStart) GroupStart = nullptr;
+    decltype(&ncclGroupEnd) GroupEnd = nullptr;
+    decltype(&ncclGetErrorString) GetErrorString = nullptr;
+};
+
+Nccl &nccl() {
+    static Nccl n;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        n.tried = true;
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h)
+            h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h)
+            return;
+        n.GetUniqueId = reinterpret_cast<decltype(n.GetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
+        n.CommInitRank = reinterpret_cast<decltype(n.CommInitRank)>(dlsym(h, "ncclCommInitRank"));
+        n.CommDestroy = reinterpret_cast<decltype(n.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
+        n.AllGather = reinterpret_cast<decltype(n.AllGather)>(dlsym(h, "ncclAllGather"));
+        n.AllReduce = reinterpret_cast<decltype(n.AllReduce)>(dlsym(h, "ncclAllReduce"));
+        n.GroupStart = reinterpret_cast<decltype(n.GroupStart)>(dlsym(h, "ncclGroupStart"));
+        n.GroupEnd = reinterpret_cast<decltype(n.GroupEnd)>(dlsym(h, "ncclGroupEnd"));
+        n.GetErrorString = reinterpret_cast<decltype(n.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
+        n.ok = n.GetUniqueId && n.CommInitRank && n.CommDestroy && n.AllGather && n.AllReduce && n.GroupStart &&
+               n.GroupEnd && n.GetErrorString;
+    });
+    return n;
+}
+} // namespace
 
 namespace {
 
@@ -288,7 +330,7 @@ bool run_items(Ctx *c, const std::vector<Item> &items) {
     if (!flush_gemv(c, jobs) || !flush_tc(c, tc))
         return false;
     if (c->world > 1) {
-        if (ncclGroupStart() != ncclSuccess) {
+        if (nccl().GroupStart() != ncclSuccess) {
             ctx_err(c, RTB_ENCCL, "ncclGroupStart");
             return false;
         }
@@ -299,17 +341,17 @@ bool run_items(Ctx *c, const std::vector<Item> &items) {
             shard_rows(c, it.rows, &lr, &r0);
             for (long long k = 0; k < it.t; ++k) {
                 float *yt = it.y + k * it.rows;
-                ncclResult_t e = ncclAllGather(yt + r0, yt, size_t(lr), ncclFloat32, c->comm, c->stream);
+                ncclResult_t e = nccl().AllGather(yt + r0, yt, size_t(lr), ncclFloat32, c->comm, c->stream);
                 if (e != ncclSuccess) {
-                    ncclGroupEnd();
-                    ctx_err(c, RTB_ENCCL, "ncclAllGather: %s", ncclGetErrorString(e));
+                    nccl().GroupEnd();
+                    ctx_err(c, RTB_ENCCL, "ncclAllGather: %s", nccl().GetErrorString(e));
                     return false;
                 }
             }
         }
-        ncclResult_t e = ncclGroupEnd();
+        ncclResult_t e = nccl().GroupEnd();
         if (e != ncclSuccess) {
-            ctx_err(c, RTB_ENCCL, "ncclGroupEnd: %s", ncclGetErrorString(e));
+            ctx_err(c, RTB_ENCCL, "ncclGroupEnd: %s", nccl().GetErrorString(e));
             return false;
         }
     }
@@ -474,7 +516,7 @@ void setup_peers(Ctx *c) {
     if (ok) {
         unsigned char *slot = static_cast<unsigned char *>(d_handles) + sizeof mine * size_t(c->rank);
         ok = cudaMemcpyAsync(slot, &mine, sizeof mine, cudaMemcpyHostToDevice, c->stream) == cudaSuccess &&
-             ncclAllGather(slot, d_handles, sizeof mine, ncclUint8, c->comm, c->stream) == ncclSuccess &&
+             nccl().AllGather(slot, d_handles, sizeof mine, ncclUint8, c->comm, c->stream) == ncclSuccess &&
              cudaMemcpyAsync(all.data(), d_handles, sizeof mine * size_t(c->world), cudaMemcpyDeviceToHost, c->stream) ==
                  cudaSuccess &&
              cudaStreamSynchronize(c->stream) == cudaSuccess;
@@ -493,7 +535,7 @@ void setup_peers(Ctx *c) {
     int flag = ok ? 1 : 0, *d_flag = nullptr;
     if (cudaMalloc(&d_flag, sizeof(int)) == cudaSuccess) {
         if (cudaMemcpyAsync(d_flag, &flag, sizeof flag, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
-            ncclAllReduce(d_flag, d_flag, 1, ncclInt32, ncclMin, c->comm, c->stream) != ncclSuccess ||
+            nccl().AllReduce(d_flag, d_flag, 1, ncclInt32, ncclMin, c->comm, c->stream) != ncclSuccess ||
             cudaMemcpyAsync(&flag, d_flag, sizeof flag, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess ||
             cudaStreamSynchronize(c->stream) != cudaSuccess)
             flag = 0;
@@ -548,7 +590,7 @@ void rt_b200_free(struct rt *R) {
     cudaStreamSynchronize(c->stream);
     drop_peers(c);
     if (c->comm)
-        ncclCommDestroy(c->comm);
+        nccl().CommDestroy(c->comm);
     cudaFree(c->d_round);
     cudaFree(c->scratch);
     cudaFree(c->d_err);
@@ -775,7 +817,7 @@ int rt_b200_nccl_id(void *out128) {
     if (!out128)
         return RTB_EINVAL;
     ncclUniqueId id;
-    if (ncclGetUniqueId(&id) != ncclSuccess)
+    if (!nccl().ok || nccl().GetUniqueId(&id) != ncclSuccess)
         return RTB_ENCCL;
     static_assert(sizeof(id) == 128, "ncclUniqueId is 128 bytes");
     memcpy(out128, &id, sizeof id);
@@ -793,21 +835,27 @@ int rt_b200_shard(struct rt *R, int rank, int world, const void *nccl_id) {
     cudaStreamSynchronize(c->stream);
     drop_peers(c);
     if (c->comm) {
-        ncclCommDestroy(c->comm);
+        nccl().CommDestroy(c->comm);
         c->comm = nullptr;
     }
     c->rank = rank;
     c->world = world;
     if (world == 1)
         return RTB_OK;
+    if (!nccl().ok) {
+        c->world = 1;
+        c->rank = 0;
+        ctx_err(c, RTB_ENCCL, "rt_b200_shard: libnccl.so.2 not found");
+        return RTB_ENCCL;
+    }
     ncclUniqueId id;
     memcpy(&id, nccl_id, sizeof id);
-    ncclResult_t e = ncclCommInitRank(&c->comm, world, id, rank);
+    ncclResult_t e = nccl().CommInitRank(&c->comm, world, id, rank);
     if (e != ncclSuccess) {
         c->comm = nullptr;
         c->world = 1;
         c->rank = 0;
-        ctx_err(c, RTB_ENCCL, "ncclCommInitRank: %s", ncclGetErrorString(e));
+        ctx_err(c, RTB_ENCCL, "ncclCommInitRank: %s", nccl().GetErrorString(e));
         return RTB_ENCCL;
     }
     if (!getenv("RTB_NO_PEER_GATHER"))

@@ -27,7 +27,8 @@ EXPORTS = ("rt_init", "rt_gemv", "rt_gemv_q", "rt_gemv_open", "rt_gemv_go", "rt_
            "gemv_s_bytes", "gemv_s_repack", "rt_gemm_silu_q", "rt_gemm_silu", "rt_gemv_rows_q", "rt_gemv_rows",
            "rt_b200_last_error", "rt_b200_set_overlap", "rt_b200_set_async", "rt_b200_sync", "rt_b200_stream", "rt_b200_set_stream",
            "rt_b200_free", "rt_b200_nccl_id", "rt_b200_shard", "rt_b200_peer_gather", "rt_b200_chain_begin",
-           "rt_b200_chain_end", "rtb_synth_q8_0", "rtb_synth_f32", "rt_gemm_static")
+           "rt_b200_chain_end", "rtb_gguf_info", "rt_b200_load_gguf", "rtb_load_error", "rtb_synth_q8_0",
+           "rtb_synth_f32", "rt_gemm_static")
 
 
 class RtError(RuntimeError):
@@ -45,6 +46,19 @@ class StructRt(C.Structure):
 _lib = None
 _L = C.c_long
 _P = C.c_void_p
+
+
+class Tensor(C.Structure):
+    """rtb_tensor of include/rt_b200.h: one GGUF tensor's table entry."""
+    _fields_ = [("name", C.c_char * 96), ("type", C.c_int), ("n_dims", C.c_int), ("dim", C.c_longlong * 4),
+                ("offset", C.c_ulonglong), ("bytes", C.c_ulonglong), ("dev", C.c_void_p), ("repacked", C.c_int),
+                ("pad_", C.c_int)]
+
+
+class LoadStats(C.Structure):
+    """rtb_load_stats of include/rt_b200.h."""
+    _fields_ = [("file_bytes", C.c_ulonglong), ("file_sum", C.c_ulonglong), ("seconds", C.c_double),
+                ("seconds_repack", C.c_double), ("direct", C.c_int), ("q8_matrices", C.c_int)]
 
 
 def load() -> C.CDLL:
@@ -83,6 +97,11 @@ def load() -> C.CDLL:
         "rt_b200_peer_gather": ([R], C.c_int),
         "rt_b200_chain_begin": ([R], C.c_int),
         "rt_b200_chain_end": ([R, C.c_int], C.c_int),
+        "rtb_gguf_info": ([C.c_char_p, C.POINTER(Tensor), C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_ulonglong)],
+                          C.c_int),
+        "rt_b200_load_gguf": ([R, C.c_char_p, _P, C.c_ulonglong, C.POINTER(Tensor), C.c_int, C.POINTER(C.c_int),
+                               C.POINTER(LoadStats)], C.c_int),
+        "rtb_load_error": ([], C.c_char_p),
         "rtb_synth_q8_0": ([_P, _L, _L, _L, C.c_uint64, C.c_uint64, C.c_float], C.c_int),
         "rtb_synth_f32": ([_P, _L, C.c_uint64, C.c_uint64, C.c_float], C.c_int),
         "rt_gemm_static": ([_P, _L, _L, _P, _L, _P, _P], C.c_int),
@@ -105,6 +124,25 @@ def _check(rt: "Runtime | None") -> None:
     code, msg = last_error(rt)
     if code != RTB_OK:
         raise RtError(code, msg)
+
+
+def gguf_info(path: str) -> tuple[list[dict], int]:
+    """The tensor table of a GGUF file (host only) and the file's size."""
+    lib = load()
+    n, fb = C.c_int(0), C.c_ulonglong(0)
+    code = lib.rtb_gguf_info(path.encode(), None, 0, C.byref(n), C.byref(fb))
+    if code:
+        raise RtError(code, lib.rtb_load_error().decode(errors="replace"))
+    arr = (Tensor * max(1, n.value))()
+    code = lib.rtb_gguf_info(path.encode(), arr, n.value, C.byref(n), C.byref(fb))
+    if code:
+        raise RtError(code, lib.rtb_load_error().decode(errors="replace"))
+    return [_tensor_dict(arr[i]) for i in range(n.value)], fb.value
+
+
+def _tensor_dict(t: Tensor) -> dict:
+    return {"name": t.name.decode(), "type": t.type, "dims": [t.dim[d] for d in range(t.n_dims)],
+            "offset": t.offset, "bytes": t.bytes, "dev": t.dev or 0, "repacked": bool(t.repacked)}
 
 
 def gemv_s_bytes(rows: int, cols: int) -> int:
@@ -248,6 +286,18 @@ class Runtime:
         if code:
             _check(self)
             raise RtError(code, "rt_b200_chain_end")
+
+    def load_gguf(self, path: str, arena: int, arena_bytes: int) -> tuple[list[dict], dict]:
+        """rt_b200_load_gguf: the file into the device arena, Q8_0 matrices repacked in place."""
+        tensors, _ = gguf_info(path)
+        arr = (Tensor * max(1, len(tensors)))()
+        n, st = C.c_int(0), LoadStats()
+        code = self.lib.rt_b200_load_gguf(self._ref, path.encode(), arena, arena_bytes, arr, len(tensors), C.byref(n),
+                                          C.byref(st))
+        if code:
+            raise RtError(code, self.lib.rtb_load_error().decode(errors="replace"))
+        stats = {k: getattr(st, k) for k, _ in LoadStats._fields_}
+        return [_tensor_dict(arr[i]) for i in range(n.value)], stats
 
     def peer_gather(self) -> bool:
         """True when single products gather y in their own kernel (else through NCCL)."""
