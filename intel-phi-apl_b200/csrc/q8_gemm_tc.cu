@@ -13,16 +13,24 @@
 // A CTA (persistent, one per SM: it owns all 512 TMEM columns) runs 128-row x BN-token tiles:
 //   warp 12     TMA: per 64-column stage, the quant box (128 rows x 64 B, 64B swizzle), the scale
 //               box (128 rows x 8 scales) and the fp16 x box (BN rows x 128 B, 128B swizzle), into
-//               a ring of up to 8 shared-memory stages;
+//               a ring of S <= 8 shared-memory stages;
 //   warps 4-11  dequant: thread (i, h) turns row i's 32 quants of block h and its scale into 32
-//               fp16 weights and stores them (tcgen05.st) into TMEM lane i of an 8-stage A ring;
+//               fp16 weights and stores them (tcgen05.st) into TMEM lane i of the A ring, one A
+//               slot per shared stage;
 //   warp 13     MMA: 4 x tcgen05.mma (M=128, N=BN, K=16, A from TMEM, B = the x box) per stage;
-//               tcgen05.commit frees the shared stage and the A stage, and at a tile's end the
-//               accumulator;
-//   warps 0-3   epilogue: tcgen05.ld of TMEM lanes 32*(warp%4).. -> y (or silu(g)*u for a pair).
+//               one tcgen05.commit per stage frees the shared stage and with it the A slot, and at
+//               a tile's end another frees the accumulator;
+//   warps 0-3,  epilogue: tcgen05.ld of TMEM lanes 32*(warp%4).. -> y (or silu(g)*u for a pair);
+//   14-17       two warps per lane quarter, each on half of the tile's token columns.
 // A stays out of shared memory: the stage's traffic there is the bulk copies in, the dequant's
 // quant reads and the tensor core's reads of x (writing A to shared memory and reading it back
 // made the kernel shared-memory bound at ~1000 cycles per 64-column stage).
+// The MMA thread is the critical issuer: every barrier wait or commit it adds costs tensor-pipe
+// time (a shared-memory wait ~30 cycles per MMA, measured). So it waits once per stage, on the A
+// slot's barrier only: the dequant threads arrive there after waiting for the stage's copies, so
+// the stage's x box has landed too; and the A slot needs no barrier of its own, because the
+// producer refills a shared stage only after its MMAs completed, and the dequant writes the slot
+// only after that refill landed.
 // Every wait is bounded (error word on timeout); every TMA load is a plain single-CTA load.
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -44,34 +52,31 @@ constexpr int BK = 64;           // columns per stage
 constexpr int MAX_BN = 256;      // tokens per tile (MMA N); 128 for SwiGLU pairs (two accumulators)
 constexpr int MAX_STAGES = 8;
 constexpr int NDQ = 8;           // dequant warps: two per SM sub-partition, each on half of a stage's columns
-constexpr int DQ_WARP0 = 4, TMA_WARP = DQ_WARP0 + NDQ, MMA_WARP = TMA_WARP + 1; // epilogue: warps 0-3
-constexpr int NT = 32 * (MMA_WARP + 1);
+constexpr int DQ_WARP0 = 4, TMA_WARP = DQ_WARP0 + NDQ, MMA_WARP = TMA_WARP + 1;
+constexpr int EPI_WARPS = 8;     // warps 0-3 and MMA_WARP+1.. +4: two per TMEM lane quarter
+constexpr int NT = 32 * (MMA_WARP + 1 + EPI_WARPS - 4);
 // Tensor memory (512 columns x 128 lanes of 32 bits): the accumulators in columns [0, 256), two
 // of 128 columns when a tile has <= 128 tokens (double-buffered, or a SwiGLU pair's gate and up),
-// else one of 256; the dequantised A tiles in an 8-stage ring of 32 columns each at [256, 512)
-// (a 128 x 64 fp16 tile: lane = row, column j = k 2j and 2j+1).
+// else one of 256; the dequantised A tiles in a ring of one 32-column slot per shared stage from
+// column 256 (a 128 x 64 fp16 tile: lane = row, column j = k 2j and 2j+1; 8 slots fill [256, 512)).
 constexpr int TMEM_COLS = 512;
-constexpr int A_BASE = 256, A_COLS = BK / 2, NA = (TMEM_COLS - A_BASE) / A_COLS;
+constexpr int A_BASE = 256, A_COLS = BK / 2;
+static_assert(A_BASE + MAX_STAGES * A_COLS <= TMEM_COLS, "one A slot per shared stage");
 // Shared memory per stage (1024-aligned): the quant box (128 rows x 64 B, 64B swizzle), the scale
 // box (128 rows x 8 fp16), the fp16 x box (bn rows x 128 B, 128B swizzle).
 constexpr int OFF_Q = 0, OFF_D = 8192, OFF_X = 10240;
-// Epilogue staging, after the stages: per epilogue warp two 1 KB buffers of 8 tokens x 32 rows.
-constexpr int STG_TOK = 8, STG_BYTES = STG_TOK * 32 * 4, STG_TOTAL = 4 * 2 * STG_BYTES;
-constexpr size_t SMEM_LIMIT = 224 * 1024; // stages + staging + barriers (the launch adds 1 KB of alignment)
+constexpr size_t SMEM_LIMIT = 224 * 1024; // stages + barriers (the launch adds 1 KB of alignment)
 
 __host__ __device__ constexpr int stage_bytes(int bn) { return (OFF_X + bn * 128 + 1023) / 1024 * 1024; }
 __host__ __device__ constexpr int n_acc(int bn) { return bn <= 128 ? 2 : 1; }
 
 struct TcJobDev {
     CUtensorMap tq, td, tq2, td2; // quants and scales of W (and of the SwiGLU up matrix)
-    CUtensorMap ty;               // y as [t][ldy] fp32, boxes of 32 rows x 8 tokens (when tma_y)
-    CUtensorMap tp;               // split-K partial sums as [plane][t][rows] fp32, same boxes (when tma_p)
     float *y;
-    float *part;                  // split-K partial sums: plane = (pair tile) * ks + K part
+    float *part;                  // split-K partial sums as [plane][t][rows]: plane = (pair tile) * ks + K part
     long long rows, ldy;
     int cols, t, pair, n_pass, tiles, unit0; // tiles: row tiles; units = tiles * n_pass * ks
     int ks;                                  // K parts (1: no split, the epilogue writes y)
-    int tma_y, tma_p;                        // bulk tensor stores usable for y / for the partials
 };
 
 struct TcParams {
@@ -91,21 +96,6 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, in
         "l"(tm), "r"(c0), "r"(c1), "r"(smem_u32(bar))
         : "memory");
 }
-
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap *tm, const void *src, int c0, int c1) {
-    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(tm), "r"(c0),
-                 "r"(c1), "r"(smem_u32(src))
-                 : "memory");
-}
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap *tm, const void *src, int c0, int c1, int c2) {
-    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(tm),
-                 "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src))
-                 : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// at most one bulk store group of this thread still reading its shared-memory source
-__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -192,12 +182,10 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int S = p.stages, BN = p.bn, SB = stage_bytes(BN), NACC = n_acc(BN), ACC_STRIDE = 256 / NACC;
-    float *stg = reinterpret_cast<float *>(smem + size_t(S) * SB);             // epilogue staging
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + size_t(S) * SB + STG_TOTAL); // [S]: TMA landed
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + size_t(S) * SB); // [S]: TMA landed
     uint64_t *empty = full + MAX_STAGES;                                   // [S]: the stage's MMAs done
-    uint64_t *afull = empty + MAX_STAGES;                                  // [NA]: A tile in TMEM
-    uint64_t *aempty = afull + NA;                                         // [NA]: its MMAs done
-    uint64_t *accfull = aempty + NA;                                       // [2]
+    uint64_t *afull = empty + MAX_STAGES;                                  // [S]: the stage's A slot in TMEM
+    uint64_t *accfull = afull + MAX_STAGES;                                // [2]
     uint64_t *accempty = accfull + 2;                                      // [2]
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accempty + 2);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -206,14 +194,11 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
-        }
-        for (int a = 0; a < NA; ++a) {
-            mbar_init(&afull[a], 32 * NDQ);
-            mbar_init(&aempty[a], 1);
+            mbar_init(&afull[s], 32 * NDQ);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&accfull[b], 1);
-            mbar_init(&accempty[b], 128);
+            mbar_init(&accempty[b], 32 * EPI_WARPS);
         }
         fence_barrier_init();
     }
@@ -275,7 +260,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
             (void)J;
             for (int ti = 0; ti < w.ntile && ok; ++ti) {
                 for (int kb = w.kb0; kb < w.kb1; ++kb, ++s) {
-                    const int slot = s % S, as = s % NA;
+                    const int slot = s % S; // also the A slot
                     if (!mbar_wait(&full[slot], (s / S) & 1)) {
                         report(p.err, ERR_TIMEOUT_FULL);
                         ok = false;
@@ -304,17 +289,13 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
                             outw[8 * cc + 2 * v + 1] = *reinterpret_cast<uint32_t *>(&b);
                         }
                     }
-                    // the TMEM A stage is free once the MMAs of its previous use completed
-                    if (s >= NA && !mbar_wait(&aempty[as], ((s / NA) - 1) & 1)) {
-                        report(p.err, ERR_TIMEOUT_MMA);
-                        ok = false;
-                        break;
-                    }
+                    // the A slot is free: the MMAs of its previous use completed before the
+                    // producer refilled this shared stage, whose copies have landed
                     tc_fence_after();
-                    tmem_st16(tmem + lane_base + uint32_t(A_BASE + as * A_COLS + 16 * h), outw);
+                    tmem_st16(tmem + lane_base + uint32_t(A_BASE + slot * A_COLS + 16 * h), outw);
                     tmem_wait_st();
                     tc_fence_before();
-                    mbar_arrive(&afull[as]);
+                    mbar_arrive(&afull[slot]);
                 }
             }
         }
@@ -338,21 +319,22 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
                     tc_fence_after();
                     const uint32_t tacc = tmem + uint32_t(b * ACC_STRIDE);
                     for (int kb = w.kb0; kb < w.kb1; ++kb, ++s) {
-                        const int slot = s % S, as = s % NA;
-                        if (!mbar_wait(&afull[as], (s / NA) & 1) || !mbar_wait(&full[slot], (s / S) & 1)) {
+                        const int slot = s % S;
+                        // the dequant threads arrive after waiting for the stage's copies: the x box
+                        // has landed too
+                        if (!mbar_wait(&afull[slot], (s / S) & 1)) {
                             report(p.err, ERR_TIMEOUT_MMA);
                             ok = false;
                             break;
                         }
                         tc_fence_after();
                         const uint64_t db = sw128_desc(smem + size_t(slot) * SB + OFF_X);
-                        const uint32_t ta = tmem + uint32_t(A_BASE + as * A_COLS);
+                        const uint32_t ta = tmem + uint32_t(A_BASE + slot * A_COLS);
 #pragma unroll
                         for (int kk = 0; kk < BK / 16; ++kk) // K = 16 per MMA: 8 TMEM columns of A, 32 B of B
                             tc_mma_ts(tacc, ta + uint32_t(8 * kk), db + uint64_t(2 * kk), idesc,
                                       (kb != w.kb0 || kk) ? 1u : 0u);
-                        tc_commit(&empty[slot]);
-                        tc_commit(&aempty[as]);
+                        tc_commit(&empty[slot]); // frees the shared stage and its A slot
                     }
                     if (ok)
                         tc_commit(&accfull[b]);
@@ -364,14 +346,15 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
                     report(p.err, ERR_TIMEOUT_DRAIN);
         }
     } else {
-        // ---------------------------------------------------------------- epilogue (warps 0-3)
-        // Warp e reads TMEM lanes 32e.. (rows 32e..32e+31 of the tile) 16 token columns at a time.
-        // With tma_y the values go through a double-buffered 1 KB staging box per warp and leave by
-        // bulk tensor stores (clipped at the matrix and token edges); the accumulator is released
-        // as soon as its last columns are in registers.
-        const int e = warp & 3;
-        float *mystg = stg + e * 2 * (STG_BYTES / 4);
-        int tcount = 0, nstore = 0;
+        // ---------------------------------------------------------------- epilogue (8 warps)
+        // Warp e (e = warp % 4) reads TMEM lanes 32e.. (rows 32e..32e+31 of the tile), 16 token
+        // columns at a time: warps 0-3 the first half of the tile's columns, the other four the
+        // rest. Each lane stores its row's values with plain stores (for each token the warp
+        // writes 32 consecutive floats, one 128-byte segment); this measured faster here than
+        // bulk tensor stores through shared-memory staging boxes, which queue behind the loads.
+        // The accumulator is handed back as soon as a warp's last columns are in registers.
+        const int e = warp & 3, eh = warp > MMA_WARP ? 1 : 0;
+        int tcount = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
             const Unit w = unit_of(p, u);
@@ -387,87 +370,58 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
                 break;
             }
             tc_fence_after();
+            // this warp's columns: [cbeg, cend), halves rounded to 16 (the second half is empty
+            // when BN == 16: the warp only hands the accumulator back)
+            const int chalf = BN >= 32 ? (BN / 2 + 15) / 16 * 16 : BN;
+            const int cbeg = eh ? chalf : 0, cend = eh ? BN : chalf;
+            if (cbeg >= cend) {
+                tc_fence_before();
+                for (int ti = 0; ti < w.ntile; ++ti)
+                    mbar_arrive(&accempty[(tcount + ti) % NACC]);
+            }
             const uint32_t c_gate = uint32_t((tcount % NACC) * ACC_STRIDE);
             const uint32_t c_up = uint32_t(((tcount + 1) % NACC) * ACC_STRIDE);
-            const int row0 = w.rt * BM + 32 * e; // this warp's first row
-            const long long row = (long long)row0 + lane;
+            const long long row = (long long)w.rt * BM + 32 * e + lane; // this lane's row
             const int n0 = w.np * BN;
             const long long nrows = J.rows;
             const int ntok = J.t;
             const bool split = J.ks > 1; // partial sums to the split-K planes, reduced afterwards
             // one or two outputs per unit: y (silu(g)*u for a pair), or the partial plane(s)
             const int nout = split ? w.ntile : 1;
-            const bool use_tma = split ? J.tma_p != 0 : J.tma_y != 0;
-            const CUtensorMap *tmap = split ? &J.tp : &J.ty;
-            for (int c0 = 0; c0 < BN; c0 += 16) {
+            for (int c0 = cbeg; c0 < cend; c0 += 16) {
                 uint32_t r[16], r2[16];
                 tmem_ld16(tmem + (uint32_t(32 * e) << 16) + c_gate + uint32_t(c0), r);
                 if (w.ntile == 2)
                     tmem_ld16(tmem + (uint32_t(32 * e) << 16) + c_up + uint32_t(c0), r2);
                 tmem_wait_ld();
-                if (c0 + 16 >= BN) { // the unit's accumulators are in registers: hand them back
+                if (c0 + 16 >= cend) { // this warp's share of the accumulators is in registers
                     tc_fence_before();
                     for (int ti = 0; ti < w.ntile; ++ti)
                         mbar_arrive(&accempty[(tcount + ti) % NACC]);
                 }
-                for (int o = 0; o < nout; ++o) {
-                    float v[16];
+                for (int o = 0; o < nout && row < nrows; ++o) {
+                    float *yp;
+                    long long ld;
+                    if (split) {
+                        const int plane = o * J.ks + w.kp;
+                        yp = J.part + ((long long)plane * ntok + n0 + c0) * nrows + row;
+                        ld = nrows;
+                    } else {
+                        yp = J.y + (long long)(n0 + c0) * J.ldy + row;
+                        ld = J.ldy;
+                    }
+                    const bool swiglu = !split && w.ntile == 2;
 #pragma unroll
                     for (int c = 0; c < 16; ++c) {
                         const float g = __uint_as_float(o ? r2[c] : r[c]);
-                        if (!split && w.ntile == 2) {
-                            const float up = __uint_as_float(r2[c]);
-                            v[c] = g / (1.0f + expf(-g)) * up;
-                        } else {
-                            v[c] = g;
-                        }
-                    }
-                    const int plane = o * J.ks + w.kp; // split: the partial plane; else unused
-                    if (use_tma) {
-#pragma unroll
-                        for (int hh = 0; hh < 16 / STG_TOK; ++hh) {
-                            if (n0 + c0 + hh * STG_TOK >= ntok)
-                                break; // tokens past t: nothing to store
-                            float *buf = mystg + (nstore & 1) * (STG_BYTES / 4);
-                            if (lane == 0)
-                                bulk_wait_read1(); // the store two back (same buffer) has read it
-                            __syncwarp();
-#pragma unroll
-                            for (int c = 0; c < STG_TOK; ++c)
-                                buf[c * 32 + lane] = v[hh * STG_TOK + c];
-                            fence_proxy_async_shared(); // generic-proxy writes -> visible to the bulk store
-                            __syncwarp();
-                            if (lane == 0) {
-                                if (split)
-                                    tma_store_3d(tmap, buf, row0, n0 + c0 + hh * STG_TOK, plane);
-                                else
-                                    tma_store_2d(tmap, buf, row0, n0 + c0 + hh * STG_TOK);
-                                bulk_commit();
-                            }
-                            ++nstore;
-                        }
-                    } else if (row < nrows) {
-                        float *yp;
-                        long long ld;
-                        if (split) {
-                            yp = J.part + ((long long)plane * ntok + n0 + c0) * nrows + row;
-                            ld = nrows;
-                        } else {
-                            yp = J.y + (long long)(n0 + c0) * J.ldy + row;
-                            ld = J.ldy;
-                        }
-#pragma unroll
-                        for (int c = 0; c < 16; ++c)
-                            if (n0 + c0 + c < ntok)
-                                yp[(long long)c * ld] = v[c];
+                        const float v = swiglu ? g / (1.0f + expf(-g)) * __uint_as_float(r2[c]) : g;
+                        if (n0 + c0 + c < ntok)
+                            yp[(long long)c * ld] = v;
                     }
                 }
             }
             tcount += w.ntile;
         }
-        if (lane == 0)
-            bulk_wait_all(); // the staging buffers stay valid until every bulk store has completed
-        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();
@@ -527,18 +481,6 @@ bool make_map(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t
     const cuuint32_t box[2] = {b0, b1}, es[2] = {1, 1};
     return fn(m, dt, 2, const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// fp32 [d2][d1][d0] array (dense), boxes of b0 x b1 x 1: the split-K partial planes.
-bool make_map3(CUtensorMap *m, const float *base, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t b0, uint32_t b1) {
-    auto fn = encode_fn();
-    if (!fn)
-        return false;
-    const cuuint64_t dims[3] = {d0, d1, d2}, strides[2] = {d0 * 4, d0 * d1 * 4};
-    const cuuint32_t box[3] = {b0, b1, 1}, es[3] = {1, 1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box, es,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // The quant and scale maps of a row-split matrix (rows x cols): quants are a 2-D uint8 array of
@@ -625,7 +567,7 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
     p.bn = bn;
     p.err = err;
     const int sb = stage_bytes(bn);
-    p.stages = int((SMEM_LIMIT - STG_TOTAL - 512) / size_t(sb));
+    p.stages = int((SMEM_LIMIT - 512) / size_t(sb));
     if (p.stages > MAX_STAGES)
         p.stages = MAX_STAGES;
     if (p.stages < 2)
@@ -655,22 +597,10 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
         J.rows = G.rows;
         J.ldy = G.ldy;
         J.ks = ks[j];
-        // bulk tensor stores need a 16-byte aligned base and row stride
-        J.tma_y = (reinterpret_cast<uintptr_t>(G.y) % 16 == 0 && (G.ldy * 4) % 16 == 0 &&
-                   make_map(&J.ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, G.y, uint64_t(G.rows), uint64_t(G.t),
-                            uint64_t(G.ldy) * 4, 32, STG_TOK, CU_TENSOR_MAP_SWIZZLE_NONE))
-                      ? 1
-                      : 0;
         J.part = nullptr;
-        J.tma_p = 0;
         if (J.ks > 1) {
             J.part = reinterpret_cast<float *>(sc);
             sc += part_bytes(G, J.ks);
-            J.tma_p = (G.rows * 4) % 16 == 0 &&
-                              make_map3(&J.tp, J.part, uint64_t(G.rows), uint64_t(G.t), uint64_t((J.pair ? 2 : 1) * J.ks),
-                                        32, STG_TOK)
-                          ? 1
-                          : 0;
         }
         J.cols = G.cols;
         J.t = G.t;
@@ -680,7 +610,7 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
         units += J.tiles * J.n_pass * J.ks;
     }
     p.total_units = units;
-    size_t smem = size_t(p.stages) * sb + STG_TOTAL + 8 * (2 * MAX_STAGES + 2 * NA + 4) + 64 + 1024;
+    size_t smem = size_t(p.stages) * sb + 8 * (3 * MAX_STAGES + 4) + 64 + 1024;
     if (smem > 227 * 1024)
         return cudaErrorInvalidValue;
     // One CTA per SM: it allocates all 512 TMEM columns, so a second CTA on the SM would only wait
