@@ -10,7 +10,8 @@
 // tcgen05 kind::f16 rate with 3 more mantissa bits, which is what holds the product within the
 // stated 2e-3 (bf16 tiles measure ~1e-2 on the BASELINE shapes).
 //
-// A CTA (persistent, one per SM: it owns all 512 TMEM columns) runs 128-row x BN-token tiles:
+// A CTA (persistent, one per SM: it owns all 512 TMEM columns) runs 128-row x BN-token tiles (a
+// SwiGLU pair's tile: 64 rows of the gate matrix and the same 64 rows of the up matrix):
 //   warp 12     TMA: per 64-column stage, the quant box (128 rows x 64 B, 64B swizzle), the scale
 //               box (128 rows x 8 scales) and the fp16 x box (BN rows x 128 B, 128B swizzle), into
 //               a ring of S <= 8 shared-memory stages;
@@ -22,6 +23,9 @@
 //               a tile's end another frees the accumulator;
 //   warps 0-3,  epilogue: tcgen05.ld of TMEM lanes 32*(warp%4).. -> y (or silu(g)*u for a pair);
 //   14-17       two warps per lane quarter, each on half of the tile's token columns.
+// A pair's tile interleaves its two matrices by TMEM lane: lanes 32e..32e+15 hold gate rows
+// 16e..16e+15 and lanes 32e+16..32e+31 the same up rows, so one warp holds both factors of its
+// 16 output rows and combines them with a lane exchange (shfl.xor 16).
 // A stays out of shared memory: the stage's traffic there is the bulk copies in, the dequant's
 // quant reads and the tensor core's reads of x (writing A to shared memory and reading it back
 // made the kernel shared-memory bound at ~1000 cycles per 64-column stage).
@@ -49,15 +53,15 @@ namespace {
 
 constexpr int BM = 128;          // weight rows per tile (MMA M)
 constexpr int BK = 64;           // columns per stage
-constexpr int MAX_BN = 256;      // tokens per tile (MMA N); 128 for SwiGLU pairs (two accumulators)
+constexpr int MAX_BN = 256;      // tokens per tile (MMA N)
+constexpr int PAIR_ROWS = BM / 2; // output rows per tile of a SwiGLU pair
 constexpr int MAX_STAGES = 8;
 constexpr int NDQ = 8;           // dequant warps: two per SM sub-partition, each on half of a stage's columns
 constexpr int DQ_WARP0 = 4, TMA_WARP = DQ_WARP0 + NDQ, MMA_WARP = TMA_WARP + 1;
 constexpr int EPI_WARPS = 8;     // warps 0-3 and MMA_WARP+1.. +4: two per TMEM lane quarter
 constexpr int NT = 32 * (MMA_WARP + 1 + EPI_WARPS - 4);
 // Tensor memory (512 columns x 128 lanes of 32 bits): the accumulators in columns [0, 256), two
-// of 128 columns when a tile has <= 128 tokens (double-buffered, or a SwiGLU pair's gate and up),
-// else one of 256; the dequantised A tiles in a ring of one 32-column slot per shared stage from
+// of 128 columns when a tile has <= 128 tokens (double-buffered), else one of 256; the dequantised A tiles in a ring of one 32-column slot per shared stage from
 // column 256 (a 128 x 64 fp16 tile: lane = row, column j = k 2j and 2j+1; 8 slots fill [256, 512)).
 constexpr int TMEM_COLS = 512;
 constexpr int A_BASE = 256, A_COLS = BK / 2;
@@ -73,9 +77,9 @@ __host__ __device__ constexpr int n_acc(int bn) { return bn <= 128 ? 2 : 1; }
 struct TcJobDev {
     CUtensorMap tq, td, tq2, td2; // quants and scales of W (and of the SwiGLU up matrix)
     float *y;
-    float *part;                  // split-K partial sums as [plane][t][rows]: plane = (pair tile) * ks + K part
+    float *part;                  // split-K partial sums as [plane][t][rows]: plane = (up ? ks : 0) + K part
     long long rows, ldy;
-    int cols, t, pair, n_pass, tiles, unit0; // tiles: row tiles; units = tiles * n_pass * ks
+    int cols, t, pair, n_pass, tiles, unit0; // tiles: row tiles (of BM rows, PAIR_ROWS for a pair); units = tiles * n_pass * ks
     int ks;                                  // K parts (1: no split, the epilogue writes y)
 };
 
@@ -154,11 +158,10 @@ __device__ __forceinline__ int find_job(const TcParams &p, int u) {
     return j;
 }
 
-// A unit of work: row tile `rt` and token pass `np` of job `j`; a SwiGLU pair unit is two MMA
-// tiles (gate, then up) sharing the x tiles and the two accumulators.
-// A unit: row tile `rt`, token pass `np` and K part `kp` (64-column blocks kb0..kb1-1) of job `j`.
+// A unit: row tile `rt`, token pass `np` and K part `kp` (64-column blocks kb0..kb1-1) of job `j`:
+// one MMA tile.
 struct Unit {
-    int j, rt, np, kp, kb0, kb1, ntile; // ntile: MMA tiles in the unit (1 or 2)
+    int j, rt, np, kp, kb0, kb1;
 };
 
 __device__ __forceinline__ Unit unit_of(const TcParams &p, int u) {
@@ -174,7 +177,6 @@ __device__ __forceinline__ Unit unit_of(const TcParams &p, int u) {
     const int nks = (J.cols + BK - 1) / BK;
     w.kb0 = int((long long)w.kp * nks / J.ks);
     w.kb1 = int((long long)(w.kp + 1) * nks / J.ks);
-    w.ntile = J.pair ? 2 : 1;
     return w;
 }
 
@@ -223,22 +225,26 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
             for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
                 const Unit w = unit_of(p, u);
                 const TcJobDev &J = p.job[w.j];
-                for (int ti = 0; ti < w.ntile && ok; ++ti) {
-                    const CUtensorMap *tq = ti ? &J.tq2 : &J.tq, *td = ti ? &J.td2 : &J.td;
-                    for (int kb = w.kb0; kb < w.kb1; ++kb, ++s) {
-                        const int slot = s % S, k = s / S;
-                        if (k > 0 && !mbar_wait(&empty[slot], (k - 1) & 1)) {
-                            report(p.err, ERR_TIMEOUT_MMA);
-                            ok = false;
-                            break;
-                        }
-                        uint8_t *st = smem + size_t(slot) * SB;
-                        mbar_arrive_expect_tx(&full[slot], uint32_t(BM * 64 + BM * 16 + BN * 128));
-                        const int k0 = kb * BK;
-                        tma_load_2d(st + OFF_Q, tq, k0, w.rt * BM, &full[slot]);
-                        tma_load_2d(st + OFF_D, td, (k0 / Q8_QK) & ~7, w.rt * BM, &full[slot]);
-                        tma_load_2d(st + OFF_X, &p.tx[w.j], k0, w.np * BN, &full[slot]);
+                for (int kb = w.kb0; kb < w.kb1; ++kb, ++s) {
+                    const int slot = s % S, k = s / S;
+                    if (k > 0 && !mbar_wait(&empty[slot], (k - 1) & 1)) {
+                        report(p.err, ERR_TIMEOUT_MMA);
+                        ok = false;
+                        break;
                     }
+                    uint8_t *st = smem + size_t(slot) * SB;
+                    mbar_arrive_expect_tx(&full[slot], uint32_t(BM * 64 + BM * 16 + BN * 128));
+                    const int k0 = kb * BK, ks0 = (k0 / Q8_QK) & ~7;
+                    if (J.pair) { // 64 gate rows, then the same 64 up rows (maps of 64-row boxes)
+                        tma_load_2d(st + OFF_Q, &J.tq, k0, w.rt * PAIR_ROWS, &full[slot]);
+                        tma_load_2d(st + OFF_Q + PAIR_ROWS * 64, &J.tq2, k0, w.rt * PAIR_ROWS, &full[slot]);
+                        tma_load_2d(st + OFF_D, &J.td, ks0, w.rt * PAIR_ROWS, &full[slot]);
+                        tma_load_2d(st + OFF_D + PAIR_ROWS * 16, &J.td2, ks0, w.rt * PAIR_ROWS, &full[slot]);
+                    } else {
+                        tma_load_2d(st + OFF_Q, &J.tq, k0, w.rt * BM, &full[slot]);
+                        tma_load_2d(st + OFF_D, &J.td, ks0, w.rt * BM, &full[slot]);
+                    }
+                    tma_load_2d(st + OFF_X, &p.tx[w.j], k0, w.np * BN, &full[slot]);
                 }
             }
             // leave no copy in flight: wait for the most recent fill of every slot
@@ -254,49 +260,48 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
         const __half2 bias = __half2half2(__ushort_as_half(uint16_t(0x6480))); // 1152
         int s = 0;
         bool ok = true;
+        // a pair's tile: lane 32e+l reads shared row 16e+l (gate, l < 16) or 64+16e+l-16 (up)
+        const int ipair = (i & 16) ? PAIR_ROWS + 16 * (i >> 5) + (i & 15) : 16 * (i >> 5) + (i & 15);
         for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
             const Unit w = unit_of(p, u);
-            const TcJobDev &J = p.job[w.j];
-            (void)J;
-            for (int ti = 0; ti < w.ntile && ok; ++ti) {
-                for (int kb = w.kb0; kb < w.kb1; ++kb, ++s) {
-                    const int slot = s % S; // also the A slot
-                    if (!mbar_wait(&full[slot], (s / S) & 1)) {
-                        report(p.err, ERR_TIMEOUT_FULL);
-                        ok = false;
-                        break;
-                    }
-                    const uint8_t *st = smem + size_t(slot) * SB;
-                    // this block's scale (one of the 8 the scale box holds) and its 32 quants
-                    const __half2 dd2 =
-                        __half2half2(*reinterpret_cast<const __half *>(st + OFF_D + i * 16 + ((kb * 2 + h) & 7) * 2));
-                    uint32_t outw[16];
-#pragma unroll
-                    for (int cc = 0; cc < 2; ++cc) { // 16 quants per chunk; chunks 2h, 2h+1
-                        const int c = 2 * h + cc;
-                        const uint4 qv =
-                            *reinterpret_cast<const uint4 *>(st + OFF_Q + i * 64 + ((c ^ ((i >> 1) & 3)) << 4));
-                        const uint32_t wq[4] = {qv.x ^ 0x80808080u, qv.y ^ 0x80808080u, qv.z ^ 0x80808080u,
-                                                qv.w ^ 0x80808080u};
-#pragma unroll
-                        for (int v = 0; v < 4; ++v) {
-                            // (q+128) as the low byte of fp16 1024+(q+128): exact; minus 1152 -> q
-                            const uint32_t lo = __byte_perm(wq[v], 0x64646464u, 0x4140u);
-                            const uint32_t hi = __byte_perm(wq[v], 0x64646464u, 0x4342u);
-                            __half2 a = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&lo), bias), dd2);
-                            __half2 b = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&hi), bias), dd2);
-                            outw[8 * cc + 2 * v] = *reinterpret_cast<uint32_t *>(&a);
-                            outw[8 * cc + 2 * v + 1] = *reinterpret_cast<uint32_t *>(&b);
-                        }
-                    }
-                    // the A slot is free: the MMAs of its previous use completed before the
-                    // producer refilled this shared stage, whose copies have landed
-                    tc_fence_after();
-                    tmem_st16(tmem + lane_base + uint32_t(A_BASE + slot * A_COLS + 16 * h), outw);
-                    tmem_wait_st();
-                    tc_fence_before();
-                    mbar_arrive(&afull[slot]);
+            const int r = p.job[w.j].pair ? ipair : i; // the shared-memory row behind this lane
+            for (int kb = w.kb0; kb < w.kb1; ++kb, ++s) {
+                const int slot = s % S; // also the A slot
+                if (!mbar_wait(&full[slot], (s / S) & 1)) {
+                    report(p.err, ERR_TIMEOUT_FULL);
+                    ok = false;
+                    break;
                 }
+                const uint8_t *st = smem + size_t(slot) * SB;
+                // this block's scale (one of the 8 the scale box holds) and its 32 quants
+                const __half2 dd2 =
+                    __half2half2(*reinterpret_cast<const __half *>(st + OFF_D + r * 16 + ((kb * 2 + h) & 7) * 2));
+                uint32_t outw[16];
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) { // 16 quants per chunk; chunks 2h, 2h+1
+                    const int c = 2 * h + cc;
+                    const uint4 qv =
+                        *reinterpret_cast<const uint4 *>(st + OFF_Q + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+                    const uint32_t wq[4] = {qv.x ^ 0x80808080u, qv.y ^ 0x80808080u, qv.z ^ 0x80808080u,
+                                            qv.w ^ 0x80808080u};
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) {
+                        // (q+128) as the low byte of fp16 1024+(q+128): exact; minus 1152 -> q
+                        const uint32_t lo = __byte_perm(wq[v], 0x64646464u, 0x4140u);
+                        const uint32_t hi = __byte_perm(wq[v], 0x64646464u, 0x4342u);
+                        __half2 a = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&lo), bias), dd2);
+                        __half2 b = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&hi), bias), dd2);
+                        outw[8 * cc + 2 * v] = *reinterpret_cast<uint32_t *>(&a);
+                        outw[8 * cc + 2 * v + 1] = *reinterpret_cast<uint32_t *>(&b);
+                    }
+                }
+                // the A slot is free: the MMAs of its previous use completed before the producer
+                // refilled this shared stage, whose copies have landed
+                tc_fence_after();
+                tmem_st16(tmem + lane_base + uint32_t(A_BASE + slot * A_COLS + 16 * h), outw);
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(&afull[slot]);
             }
         }
     } else if (warp == MMA_WARP) {
@@ -305,40 +310,36 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
             const uint32_t idesc = idesc_f16(BN);
             int s = 0, tcount = 0;
             bool ok = true;
-            for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
+            for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x, ++tcount) {
                 const Unit w = unit_of(p, u);
-                const TcJobDev &J = p.job[w.j];
-                (void)J;
-                for (int ti = 0; ti < w.ntile && ok; ++ti, ++tcount) {
-                    const int b = tcount % NACC, bu = tcount / NACC;
-                    if (bu > 0 && !mbar_wait(&accempty[b], (bu - 1) & 1)) {
+                const int b = tcount % NACC, bu = tcount / NACC;
+                if (bu > 0 && !mbar_wait(&accempty[b], (bu - 1) & 1)) {
+                    report(p.err, ERR_TIMEOUT_MMA);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t tacc = tmem + uint32_t(b * ACC_STRIDE);
+                for (int kb = w.kb0; kb < w.kb1; ++kb, ++s) {
+                    const int slot = s % S;
+                    // the dequant threads arrive after waiting for the stage's copies: the x box has
+                    // landed too
+                    if (!mbar_wait(&afull[slot], (s / S) & 1)) {
                         report(p.err, ERR_TIMEOUT_MMA);
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t tacc = tmem + uint32_t(b * ACC_STRIDE);
-                    for (int kb = w.kb0; kb < w.kb1; ++kb, ++s) {
-                        const int slot = s % S;
-                        // the dequant threads arrive after waiting for the stage's copies: the x box
-                        // has landed too
-                        if (!mbar_wait(&afull[slot], (s / S) & 1)) {
-                            report(p.err, ERR_TIMEOUT_MMA);
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                        const uint64_t db = sw128_desc(smem + size_t(slot) * SB + OFF_X);
-                        const uint32_t ta = tmem + uint32_t(A_BASE + slot * A_COLS);
+                    const uint64_t db = sw128_desc(smem + size_t(slot) * SB + OFF_X);
+                    const uint32_t ta = tmem + uint32_t(A_BASE + slot * A_COLS);
 #pragma unroll
-                        for (int kk = 0; kk < BK / 16; ++kk) // K = 16 per MMA: 8 TMEM columns of A, 32 B of B
-                            tc_mma_ts(tacc, ta + uint32_t(8 * kk), db + uint64_t(2 * kk), idesc,
-                                      (kb != w.kb0 || kk) ? 1u : 0u);
-                        tc_commit(&empty[slot]); // frees the shared stage and its A slot
-                    }
-                    if (ok)
-                        tc_commit(&accfull[b]);
+                    for (int kk = 0; kk < BK / 16; ++kk) // K = 16 per MMA: 8 TMEM columns of A, 32 B of B
+                        tc_mma_ts(tacc, ta + uint32_t(8 * kk), db + uint64_t(2 * kk), idesc,
+                                  (kb != w.kb0 || kk) ? 1u : 0u);
+                    tc_commit(&empty[slot]); // frees the shared stage and its A slot
                 }
+                if (ok)
+                    tc_commit(&accfull[b]);
             }
             // drain: the MMAs of the last use of every slot
             for (int q = max(0, s - S); q < s; ++q)
@@ -356,15 +357,11 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
         const int e = warp & 3, eh = warp > MMA_WARP ? 1 : 0;
         int tcount = 0;
         bool ok = true;
-        for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
+        for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x, ++tcount) {
             const Unit w = unit_of(p, u);
             const TcJobDev &J = p.job[w.j];
-            bool got = true;
-            for (int ti = 0; ti < w.ntile; ++ti) {
-                const int b = (tcount + ti) % NACC, bu = (tcount + ti) / NACC;
-                got = got && mbar_wait(&accfull[b], bu & 1);
-            }
-            if (!got) {
+            const int b = tcount % NACC;
+            if (!mbar_wait(&accfull[b], (tcount / NACC) & 1)) {
                 report(p.err, ERR_TIMEOUT_MMA);
                 ok = false;
                 break;
@@ -376,51 +373,61 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
             const int cbeg = eh ? chalf : 0, cend = eh ? BN : chalf;
             if (cbeg >= cend) {
                 tc_fence_before();
-                for (int ti = 0; ti < w.ntile; ++ti)
-                    mbar_arrive(&accempty[(tcount + ti) % NACC]);
+                mbar_arrive(&accempty[b]);
             }
-            const uint32_t c_gate = uint32_t((tcount % NACC) * ACC_STRIDE);
-            const uint32_t c_up = uint32_t(((tcount + 1) % NACC) * ACC_STRIDE);
-            const long long row = (long long)w.rt * BM + 32 * e + lane; // this lane's row
+            const uint32_t tacc = tmem + (uint32_t(32 * e) << 16) + uint32_t(b * ACC_STRIDE);
             const int n0 = w.np * BN;
             const long long nrows = J.rows;
             const int ntok = J.t;
             const bool split = J.ks > 1; // partial sums to the split-K planes, reduced afterwards
-            // one or two outputs per unit: y (silu(g)*u for a pair), or the partial plane(s)
-            const int nout = split ? w.ntile : 1;
+            // this lane's output row (for a pair: lanes l and l+16 hold gate and up of one row)
+            const bool up = J.pair && (lane & 16);
+            const long long row = J.pair ? (long long)w.rt * PAIR_ROWS + 16 * e + (lane & 15)
+                                         : (long long)w.rt * BM + 32 * e + lane;
             for (int c0 = cbeg; c0 < cend; c0 += 16) {
-                uint32_t r[16], r2[16];
-                tmem_ld16(tmem + (uint32_t(32 * e) << 16) + c_gate + uint32_t(c0), r);
-                if (w.ntile == 2)
-                    tmem_ld16(tmem + (uint32_t(32 * e) << 16) + c_up + uint32_t(c0), r2);
+                uint32_t r[16];
+                tmem_ld16(tacc + uint32_t(c0), r);
                 tmem_wait_ld();
-                if (c0 + 16 >= cend) { // this warp's share of the accumulators is in registers
+                if (c0 + 16 >= cend) { // this warp's share of the accumulator is in registers
                     tc_fence_before();
-                    for (int ti = 0; ti < w.ntile; ++ti)
-                        mbar_arrive(&accempty[(tcount + ti) % NACC]);
+                    mbar_arrive(&accempty[b]);
                 }
-                for (int o = 0; o < nout && row < nrows; ++o) {
+                if (J.pair && !split) {
+                    // y = silu(g) * u: the gate lane finishes tokens c0..c0+7 of its row, the up
+                    // lane tokens c0+8..c0+15, each taking the other factor from its partner
+                    float g[8], uv[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const float give = __uint_as_float(up ? r[k] : r[8 + k]);
+                        const float got = __shfl_xor_sync(0xffffffffu, give, 16);
+                        g[k] = up ? got : __uint_as_float(r[k]);
+                        uv[k] = up ? __uint_as_float(r[8 + k]) : got;
+                    }
+                    const int tk0 = n0 + c0 + (up ? 8 : 0);
+                    if (row < nrows) {
+                        float *yp = J.y + (long long)tk0 * J.ldy + row;
+#pragma unroll
+                        for (int k = 0; k < 8; ++k)
+                            if (tk0 + k < ntok)
+                                yp[(long long)k * J.ldy] = g[k] / (1.0f + expf(-g[k])) * uv[k];
+                    }
+                } else if (row < nrows) {
                     float *yp;
                     long long ld;
-                    if (split) {
-                        const int plane = o * J.ks + w.kp;
+                    if (split) { // a pair's gate lanes to the gate planes, its up lanes to the up planes
+                        const int plane = (up ? J.ks : 0) + w.kp;
                         yp = J.part + ((long long)plane * ntok + n0 + c0) * nrows + row;
                         ld = nrows;
                     } else {
                         yp = J.y + (long long)(n0 + c0) * J.ldy + row;
                         ld = J.ldy;
                     }
-                    const bool swiglu = !split && w.ntile == 2;
 #pragma unroll
-                    for (int c = 0; c < 16; ++c) {
-                        const float g = __uint_as_float(o ? r2[c] : r[c]);
-                        const float v = swiglu ? g / (1.0f + expf(-g)) * __uint_as_float(r2[c]) : g;
+                    for (int c = 0; c < 16; ++c)
                         if (n0 + c0 + c < ntok)
-                            yp[(long long)c * ld] = v;
-                    }
+                            yp[(long long)c * ld] = __uint_as_float(r[c]);
                 }
             }
-            tcount += w.ntile;
         }
     }
     tc_fence_before();
@@ -485,28 +492,31 @@ bool make_map(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t
 
 // The quant and scale maps of a row-split matrix (rows x cols): quants are a 2-D uint8 array of
 // cols bytes per row, rows q8s_row_bytes apart; scales a uint16 array at +cols of the same rows.
-bool weight_maps(const uint8_t *w, long long rows, int cols, CUtensorMap *tq, CUtensorMap *td) {
+// Boxes of box_rows rows (BM, or PAIR_ROWS for the two matrices of a SwiGLU pair).
+bool weight_maps(const uint8_t *w, long long rows, int cols, uint32_t box_rows, CUtensorMap *tq, CUtensorMap *td) {
     const uint64_t rb = uint64_t(q8s_row_bytes(cols));
-    return make_map(tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, uint64_t(cols), uint64_t(rows), rb, 64, BM,
+    return make_map(tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, uint64_t(cols), uint64_t(rows), rb, 64, box_rows,
                     CU_TENSOR_MAP_SWIZZLE_64B) &&
            make_map(td, CU_TENSOR_MAP_DATA_TYPE_UINT16, w + cols, uint64_t(q8s_scale_stride(cols)), uint64_t(rows), rb, 8,
-                    BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+                    box_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+// Row tiles of a job: BM rows, or PAIR_ROWS output rows for a SwiGLU pair.
+long long row_tiles(const GemmJob &G) {
+    const long long tr = G.w2 ? PAIR_ROWS : BM;
+    return (G.rows + tr - 1) / tr;
 }
 
 } // namespace
 
 namespace {
 
-// Tokens per tile: the largest t split into passes of <= MAX_BN (128 when a SwiGLU pair is in the
-// launch), rounded up to 16.
+// Tokens per tile: the largest t split into passes of <= MAX_BN, rounded up to 16.
 int choose_bn(const GemmJob *jobs, int n) {
-    int tmax = 0, maxbn = MAX_BN;
-    for (int j = 0; j < n; ++j) {
+    int tmax = 0;
+    for (int j = 0; j < n; ++j)
         tmax = jobs[j].t > tmax ? jobs[j].t : tmax;
-        if (jobs[j].w2)
-            maxbn = 128; // a pair's gate and up accumulators share the 256 accumulator columns
-    }
-    const int npass_max = (tmax + maxbn - 1) / maxbn;
+    const int npass_max = (tmax + MAX_BN - 1) / MAX_BN;
     const int bn = ((tmax + npass_max - 1) / npass_max + 15) / 16 * 16;
     return bn < 16 ? 16 : bn;
 }
@@ -518,7 +528,7 @@ int choose_bn(const GemmJob *jobs, int n) {
 void choose_splits(const GemmJob *jobs, int n, int bn, int num_sms, bool allow, int *ks) {
     long long base = 0;
     for (int j = 0; j < n; ++j)
-        base += ((jobs[j].rows + BM - 1) / BM) * ((jobs[j].t + bn - 1) / bn);
+        base += row_tiles(jobs[j]) * ((jobs[j].t + bn - 1) / bn);
     const int sms = num_sms > 0 ? num_sms : 148;
     for (int j = 0; j < n; ++j) {
         int k = 1;
@@ -588,10 +598,11 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
                       uint64_t(G.cols) * 2, 64, uint32_t(bn), CU_TENSOR_MAP_SWIZZLE_128B))
             return cudaErrorInvalidValue;
         TcJobDev &J = p.job[j];
-        if (!weight_maps(G.w, G.rows, G.cols, &J.tq, &J.td))
-            return cudaErrorInvalidValue;
         J.pair = G.w2 != nullptr;
-        if (J.pair && !weight_maps(G.w2, G.rows, G.cols, &J.tq2, &J.td2))
+        const uint32_t box_rows = J.pair ? PAIR_ROWS : BM;
+        if (!weight_maps(G.w, G.rows, G.cols, box_rows, &J.tq, &J.td))
+            return cudaErrorInvalidValue;
+        if (J.pair && !weight_maps(G.w2, G.rows, G.cols, box_rows, &J.tq2, &J.td2))
             return cudaErrorInvalidValue;
         J.y = G.y;
         J.rows = G.rows;
@@ -605,7 +616,7 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
         J.cols = G.cols;
         J.t = G.t;
         J.n_pass = (G.t + bn - 1) / bn;
-        J.tiles = int((G.rows + BM - 1) / BM);
+        J.tiles = int(row_tiles(G));
         J.unit0 = units;
         units += J.tiles * J.n_pass * J.ks;
     }
