@@ -180,6 +180,18 @@ __device__ __forceinline__ Unit unit_of(const TcParams &p, int u) {
     return w;
 }
 
+// A role's position in the stage ring: slot and the parity of its current use.
+struct Ring {
+    int slot = 0;
+    uint32_t phase = 0;
+    __device__ __forceinline__ void next(int S) {
+        if (++slot == S) {
+            slot = 0;
+            phase ^= 1u;
+        }
+    }
+};
+
 __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -221,13 +233,14 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
         // ---------------------------------------------------------------- producer
         if (lane == 0) {
             int s = 0;
+            Ring ring;
             bool ok = true;
             for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
                 const Unit w = unit_of(p, u);
                 const TcJobDev &J = p.job[w.j];
-                for (int kb = w.kb0; kb < w.kb1; ++kb, ++s) {
-                    const int slot = s % S, k = s / S;
-                    if (k > 0 && !mbar_wait(&empty[slot], (k - 1) & 1)) {
+                for (int kb = w.kb0; kb < w.kb1; ++kb, ++s, ring.next(S)) {
+                    const int slot = ring.slot;
+                    if (s >= S && !mbar_wait(&empty[slot], ring.phase ^ 1)) {
                         report(p.err, ERR_TIMEOUT_MMA);
                         ok = false;
                         break;
@@ -258,16 +271,16 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
         const int h = (threadIdx.x - DQ_WARP0 * 32) / BM; // 32-column block of the stage
         const uint32_t lane_base = uint32_t(32 * (warp % 4)) << 16;
         const __half2 bias = __half2half2(__ushort_as_half(uint16_t(0x6480))); // 1152
-        int s = 0;
+        Ring ring;
         bool ok = true;
         // a pair's tile: lane 32e+l reads shared row 16e+l (gate, l < 16) or 64+16e+l-16 (up)
         const int ipair = (i & 16) ? PAIR_ROWS + 16 * (i >> 5) + (i & 15) : 16 * (i >> 5) + (i & 15);
         for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
             const Unit w = unit_of(p, u);
             const int r = p.job[w.j].pair ? ipair : i; // the shared-memory row behind this lane
-            for (int kb = w.kb0; kb < w.kb1; ++kb, ++s) {
-                const int slot = s % S; // also the A slot
-                if (!mbar_wait(&full[slot], (s / S) & 1)) {
+            for (int kb = w.kb0; kb < w.kb1; ++kb, ring.next(S)) {
+                const int slot = ring.slot; // also the A slot
+                if (!mbar_wait(&full[slot], ring.phase)) {
                     report(p.err, ERR_TIMEOUT_FULL);
                     ok = false;
                     break;
@@ -309,6 +322,10 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
         if (lane == 0) {
             const uint32_t idesc = idesc_f16(BN);
             int s = 0, tcount = 0;
+            Ring ring;
+            // descriptors of slot 0's x box and A slot; slot k adds k stages / k A slots
+            const uint64_t db0 = sw128_desc(smem + OFF_X);
+            const uint32_t ta0 = tmem + uint32_t(A_BASE);
             bool ok = true;
             for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x, ++tcount) {
                 const Unit w = unit_of(p, u);
@@ -320,18 +337,18 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
                 }
                 tc_fence_after();
                 const uint32_t tacc = tmem + uint32_t(b * ACC_STRIDE);
-                for (int kb = w.kb0; kb < w.kb1; ++kb, ++s) {
-                    const int slot = s % S;
+                for (int kb = w.kb0; kb < w.kb1; ++kb, ++s, ring.next(S)) {
+                    const int slot = ring.slot;
                     // the dequant threads arrive after waiting for the stage's copies: the x box has
                     // landed too
-                    if (!mbar_wait(&afull[slot], (s / S) & 1)) {
+                    if (!mbar_wait(&afull[slot], ring.phase)) {
                         report(p.err, ERR_TIMEOUT_MMA);
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t db = sw128_desc(smem + size_t(slot) * SB + OFF_X);
-                    const uint32_t ta = tmem + uint32_t(A_BASE + slot * A_COLS);
+                    const uint64_t db = db0 + uint64_t(slot * (SB >> 4)); // start address field, 16-byte units
+                    const uint32_t ta = ta0 + uint32_t(slot * A_COLS);
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk) // K = 16 per MMA: 8 TMEM columns of A, 32 B of B
                         tc_mma_ts(tacc, ta + uint32_t(8 * kk), db + uint64_t(2 * kk), idesc,
