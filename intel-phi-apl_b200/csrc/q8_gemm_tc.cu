@@ -538,26 +538,46 @@ int choose_bn(const GemmJob *jobs, int n) {
     return bn < 16 ? 16 : bn;
 }
 
-// K parts per job. A launch whose (row tile, token pass) units would leave more than half of the
-// SMs idle splits K so that there are about two units per SM, each part at least 32 64-column
-// blocks long (shorter parts measure slower: every unit pays its pipeline fill and epilogue); the
-// parts' fp32 partial sums are then added in order by a reduce pass.
+// K parts per job, from a cost model of the launch measured on B200: units run in waves of one
+// per SM; a unit costs its 64-column stages (~0.26 us each at 16 tokens, ~0.55 us at 256) plus its
+// pipeline fill (~2 us) and epilogue drain (~7 us for a 128 x 256 fp32 tile, in proportion for
+// fewer tokens); a split job adds the reduce pass (a launch plus its partial planes read once and
+// y written, ~5 TB/s). The model picks the number of parts (1..16, each at least 4 stages long)
+// with the least estimated time; a part count must save 3% to beat a smaller one.
 void choose_splits(const GemmJob *jobs, int n, int bn, int num_sms, bool allow, int *ks) {
-    long long base = 0;
-    for (int j = 0; j < n; ++j)
-        base += row_tiles(jobs[j]) * ((jobs[j].t + bn - 1) / bn);
     const int sms = num_sms > 0 ? num_sms : 148;
-    for (int j = 0; j < n; ++j) {
-        int k = 1;
-        if (allow && 2 * base <= sms) {
-            k = int((2 * sms + base - 1) / base);
-            const int nks = (jobs[j].cols + BK - 1) / BK;
-            const int kmax = nks / 32 > 1 ? nks / 32 : 1;
-            k = k < kmax ? k : kmax;
-            k = k < 16 ? k : 16;
+    auto kmax_of = [](const GemmJob &G) {
+        const int nks = (G.cols + BK - 1) / BK;
+        return nks / 4 > 1 ? nks / 4 : 1;
+    };
+    int best = 1;
+    if (allow) {
+        const double ts = 0.26 + 0.29 * bn / 256.0, fill = 2.0 + 7.0 * bn / 256.0;
+        double best_t = 0.0;
+        for (int k = 1; k <= 16; ++k) {
+            long long units = 0;
+            int maxst = 0;
+            double red = 0.0;
+            for (int j = 0; j < n; ++j) {
+                const GemmJob &G = jobs[j];
+                const int kj = k < kmax_of(G) ? k : kmax_of(G);
+                const int nks = (G.cols + BK - 1) / BK;
+                units += row_tiles(G) * ((G.t + bn - 1) / bn) * kj;
+                const int st = (nks + kj - 1) / kj;
+                maxst = st > maxst ? st : maxst;
+                if (kj > 1)
+                    red += double(kj + (G.w2 ? 2 : 1)) * (G.w2 ? 2 : 1) * G.t * double(G.rows) * 4.0;
+            }
+            const long long waves = (units + sms - 1) / sms;
+            const double t = double(waves) * (maxst * ts + fill) + (red > 0 ? 2.0 + red / 5e6 : 0.0);
+            if (k == 1 || t < best_t * 0.97) {
+                best_t = t;
+                best = k;
+            }
         }
-        ks[j] = k;
     }
+    for (int j = 0; j < n; ++j)
+        ks[j] = best < kmax_of(jobs[j]) ? best : kmax_of(jobs[j]);
 }
 
 size_t part_bytes(const GemmJob &G, int ks) {
