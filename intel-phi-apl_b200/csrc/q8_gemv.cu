@@ -168,50 +168,41 @@ struct StageIter {
 template <int MT>
 constexpr int row_group() { return MT == 2 ? NH : NH / 2; }
 
-// The RG rows' 32-step chains of one block for MT tokens. MT == 1: rows in packed pairs
-// (fma.rn.f32x2 and add.rn.f32x2: two independent IEEE operations). MT > 1: scalar.
+// The RG rows' 32-step chains of one block for MT tokens, rows in packed pairs (fma.rn.f32x2 and
+// add.rn.f32x2: two independent IEEE operations per instruction). A pair's converted weights serve
+// every token, so a weight costs one byte permute, half a packed add and MT halves of a packed fma.
 template <int MT, int RG>
 __device__ __forceinline__ void block_chains(const uint32_t (&wq)[RG][8], const float (&xr)[MT][Q8_QK],
                                              float (&t)[MT][RG]) {
-    if constexpr (MT == 1) {
-        float2 tp[RG / 2];
+    static_assert(RG % 2 == 0, "rows in pairs");
+    float2 tp[MT][RG / 2];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
         for (int p = 0; p < RG / 2; ++p)
-            tp[p] = make_float2(0.0f, 0.0f);
-        const float2 bias = make_float2(-8388736.0f, -8388736.0f);
+            tp[mt][p] = make_float2(0.0f, 0.0f);
+    const float2 bias = make_float2(-8388736.0f, -8388736.0f);
 #pragma unroll
-        for (int i = 0; i < Q8_QK; ++i) {
-            const float2 xx = make_float2(xr[0][i], xr[0][i]);
-#pragma unroll
-            for (int p = 0; p < RG / 2; ++p) {
-                // 2^23 + (q + 128) for the two rows, then minus 2^23 + 128: exact q
-                const float2 m =
-                    make_float2(__uint_as_float(__byte_perm(wq[2 * p][i >> 2], 0x4B000000u, 0x7650u + (i & 3))),
-                                __uint_as_float(__byte_perm(wq[2 * p + 1][i >> 2], 0x4B000000u, 0x7650u + (i & 3))));
-                tp[p] = __ffma2_rn(__fadd2_rn(m, bias), xx, tp[p]);
-            }
-        }
+    for (int i = 0; i < Q8_QK; ++i) {
 #pragma unroll
         for (int p = 0; p < RG / 2; ++p) {
-            t[0][2 * p] = tp[p].x;
-            t[0][2 * p + 1] = tp[p].y;
-        }
-    } else {
-#pragma unroll
-        for (int r = 0; r < RG; ++r)
+            // 2^23 + (q + 128) for the two rows, then minus 2^23 + 128: exact q
+            const float2 m = __fadd2_rn(
+                make_float2(__uint_as_float(__byte_perm(wq[2 * p][i >> 2], 0x4B000000u, 0x7650u + (i & 3))),
+                            __uint_as_float(__byte_perm(wq[2 * p + 1][i >> 2], 0x4B000000u, 0x7650u + (i & 3)))),
+                bias);
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt)
-                t[mt][r] = 0.0f;
-#pragma unroll
-        for (int i = 0; i < Q8_QK; ++i)
-#pragma unroll
-            for (int r = 0; r < RG; ++r) {
-                const float qf = q_to_f32(wq[r][i >> 2], i & 3);
-#pragma unroll
-                for (int mt = 0; mt < MT; ++mt)
-                    t[mt][r] = __fmaf_rn(qf, xr[mt][i], t[mt][r]);
-            }
+                tp[mt][p] = __ffma2_rn(m, make_float2(xr[mt][i], xr[mt][i]), tp[mt][p]);
+        }
     }
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int p = 0; p < RG / 2; ++p) {
+            t[mt][2 * p] = tp[mt][p].x;
+            t[mt][2 * p + 1] = tp[mt][p].y;
+        }
 }
 
 // Waits until *ctr >= target (an acquire at GPU scope), bounded like every wait here.
