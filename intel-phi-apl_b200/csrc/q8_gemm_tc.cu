@@ -56,23 +56,37 @@ constexpr int BK = 64;           // columns per stage
 constexpr int MAX_BN = 256;      // tokens per tile (MMA N)
 constexpr int PAIR_ROWS = BM / 2; // output rows per tile of a SwiGLU pair
 constexpr int MAX_STAGES = 8;
-constexpr int NDQ = 8;           // dequant warps: two per SM sub-partition, each on half of a stage's columns
-constexpr int DQ_WARP0 = 4, TMA_WARP = DQ_WARP0 + NDQ, MMA_WARP = TMA_WARP + 1;
-constexpr int EPI_WARPS = 8;     // warps 0-3 and MMA_WARP+1.. +4: two per TMEM lane quarter
-constexpr int NT = 32 * (MMA_WARP + 1 + EPI_WARPS - 4);
 // Tensor memory (512 columns x 128 lanes of 32 bits): the accumulators in columns [0, 256), two
 // of 128 columns when a tile has <= 128 tokens (double-buffered), else one of 256; the dequantised A tiles in a ring of one 32-column slot per shared stage from
 // column 256 (a 128 x 64 fp16 tile: lane = row, column j = k 2j and 2j+1; 8 slots fill [256, 512)).
-constexpr int TMEM_COLS = 512;
-constexpr int A_BASE = 256, A_COLS = BK / 2;
-static_assert(A_BASE + MAX_STAGES * A_COLS <= TMEM_COLS, "one A slot per shared stage");
+constexpr int A_COLS = BK / 2;
+
+// The CTA's shape: CPS CTAs per SM, each owning 512 / CPS TMEM columns.
+//   CPS = 1 (tiles of up to 256 tokens): 18 warps, 8 dequant (two per SM sub-partition, each on
+//     one 32-column block of a stage), 8 epilogue (two per TMEM lane quarter, each on half of
+//     the tile's columns); accumulators in columns [0, 256), up to 8 A slots from 256.
+//   CPS = 2 (tiles of up to 64 tokens): 10 warps, 4 dequant (each thread both blocks of its row),
+//     4 epilogue; accumulators in [0, 128), up to 4 A slots from 128. Two CTAs share an SM and
+//     its tensor core: at N <= 64 an MMA instruction takes ~46 cycles while each wait in the
+//     issuing thread stalls it ~200, so a second issuer keeps the pipe fed.
+template <int CPS>
+struct TcShape {
+    static constexpr int NDQ = 8 / CPS, EPI_WARPS = 8 / CPS;
+    static constexpr int DQ_WARP0 = 4, TMA_WARP = DQ_WARP0 + NDQ, MMA_WARP = TMA_WARP + 1;
+    static constexpr int NT = 32 * (MMA_WARP + 1 + EPI_WARPS - 4); // epilogue: warps 0-3 (+ after MMA_WARP)
+    static constexpr int TMEM_COLS = 512 / CPS, ACC_COLS = 256 / CPS, A_BASE = ACC_COLS;
+    static constexpr int MAX_S = (TMEM_COLS - A_BASE) / A_COLS < MAX_STAGES ? (TMEM_COLS - A_BASE) / A_COLS : MAX_STAGES;
+    static constexpr int MAX_BN_SHAPE = 256 / CPS;
+    static constexpr int BLOCKS_PER_THREAD = 2 / (NDQ / 4); // 32-column blocks per dequant thread per stage
+};
 // Shared memory per stage (1024-aligned): the quant box (128 rows x 64 B, 64B swizzle), the scale
 // box (128 rows x 8 fp16), the fp16 x box (bn rows x 128 B, 128B swizzle).
 constexpr int OFF_Q = 0, OFF_D = 8192, OFF_X = 10240;
-constexpr size_t SMEM_LIMIT = 224 * 1024; // stages + barriers (the launch adds 1 KB of alignment)
+constexpr size_t SMEM_LIMIT = 224 * 1024;   // one CTA per SM: stages + barriers (the launch adds 1 KB of alignment)
+constexpr size_t SMEM_LIMIT_2 = 110 * 1024; // two CTAs per SM
 
 __host__ __device__ constexpr int stage_bytes(int bn) { return (OFF_X + bn * 128 + 1023) / 1024 * 1024; }
-__host__ __device__ constexpr int n_acc(int bn) { return bn <= 128 ? 2 : 1; }
+__host__ __device__ constexpr int n_acc(int bn, int cps) { return bn <= 128 / cps ? 2 : 1; }
 
 struct TcJobDev {
     CUtensorMap tq, td, tq2, td2; // quants and scales of W (and of the SwiGLU up matrix)
@@ -192,10 +206,14 @@ struct Ring {
     }
 };
 
-__global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ TcParams p) {
+template <int CPS>
+__global__ void __launch_bounds__(TcShape<CPS>::NT, CPS) gemm_tc_kernel(const __grid_constant__ TcParams p) {
+    using Sh = TcShape<CPS>;
+    constexpr int NDQ = Sh::NDQ, EPI_WARPS = Sh::EPI_WARPS, DQ_WARP0 = Sh::DQ_WARP0, TMA_WARP = Sh::TMA_WARP,
+                  MMA_WARP = Sh::MMA_WARP, TMEM_COLS = Sh::TMEM_COLS, A_BASE = Sh::A_BASE;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int S = p.stages, BN = p.bn, SB = stage_bytes(BN), NACC = n_acc(BN), ACC_STRIDE = 256 / NACC;
+    const int S = p.stages, BN = p.bn, SB = stage_bytes(BN), NACC = n_acc(BN, CPS), ACC_STRIDE = Sh::ACC_COLS / NACC;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + size_t(S) * SB); // [S]: TMA landed
     uint64_t *empty = full + MAX_STAGES;                                   // [S]: the stage's MMAs done
     uint64_t *afull = empty + MAX_STAGES;                                  // [S]: the stage's A slot in TMEM
@@ -268,7 +286,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
     } else if (warp >= DQ_WARP0 && warp < DQ_WARP0 + NDQ) {
         // ---------------------------------------------------------------- dequant -> TMEM
         const int i = (threadIdx.x - DQ_WARP0 * 32) % BM; // tile row = this thread's TMEM lane
-        const int h = (threadIdx.x - DQ_WARP0 * 32) / BM; // 32-column block of the stage
+        const int h0 = (threadIdx.x - DQ_WARP0 * 32) / BM * Sh::BLOCKS_PER_THREAD; // its first 32-column block
         const uint32_t lane_base = uint32_t(32 * (warp % 4)) << 16;
         const __half2 bias = __half2half2(__ushort_as_half(uint16_t(0x6480))); // 1152
         Ring ring;
@@ -286,32 +304,36 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
                     break;
                 }
                 const uint8_t *st = smem + size_t(slot) * SB;
-                // this block's scale (one of the 8 the scale box holds) and its 32 quants
-                const __half2 dd2 =
-                    __half2half2(*reinterpret_cast<const __half *>(st + OFF_D + r * 16 + ((kb * 2 + h) & 7) * 2));
-                uint32_t outw[16];
-#pragma unroll
-                for (int cc = 0; cc < 2; ++cc) { // 16 quants per chunk; chunks 2h, 2h+1
-                    const int c = 2 * h + cc;
-                    const uint4 qv =
-                        *reinterpret_cast<const uint4 *>(st + OFF_Q + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
-                    const uint32_t wq[4] = {qv.x ^ 0x80808080u, qv.y ^ 0x80808080u, qv.z ^ 0x80808080u,
-                                            qv.w ^ 0x80808080u};
-#pragma unroll
-                    for (int v = 0; v < 4; ++v) {
-                        // (q+128) as the low byte of fp16 1024+(q+128): exact; minus 1152 -> q
-                        const uint32_t lo = __byte_perm(wq[v], 0x64646464u, 0x4140u);
-                        const uint32_t hi = __byte_perm(wq[v], 0x64646464u, 0x4342u);
-                        __half2 a = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&lo), bias), dd2);
-                        __half2 b = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&hi), bias), dd2);
-                        outw[8 * cc + 2 * v] = *reinterpret_cast<uint32_t *>(&a);
-                        outw[8 * cc + 2 * v + 1] = *reinterpret_cast<uint32_t *>(&b);
-                    }
-                }
                 // the A slot is free: the MMAs of its previous use completed before the producer
                 // refilled this shared stage, whose copies have landed
                 tc_fence_after();
-                tmem_st16(tmem + lane_base + uint32_t(A_BASE + slot * A_COLS + 16 * h), outw);
+#pragma unroll
+                for (int hb = 0; hb < Sh::BLOCKS_PER_THREAD; ++hb) {
+                    const int h = h0 + hb;
+                    // this block's scale (one of the 8 the scale box holds) and its 32 quants
+                    const __half2 dd2 = __half2half2(
+                        *reinterpret_cast<const __half *>(st + OFF_D + r * 16 + ((kb * 2 + h) & 7) * 2));
+                    uint32_t outw[16];
+#pragma unroll
+                    for (int cc = 0; cc < 2; ++cc) { // 16 quants per chunk; chunks 2h, 2h+1
+                        const int c = 2 * h + cc;
+                        const uint4 qv =
+                            *reinterpret_cast<const uint4 *>(st + OFF_Q + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+                        const uint32_t wq[4] = {qv.x ^ 0x80808080u, qv.y ^ 0x80808080u, qv.z ^ 0x80808080u,
+                                                qv.w ^ 0x80808080u};
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) {
+                            // (q+128) as the low byte of fp16 1024+(q+128): exact; minus 1152 -> q
+                            const uint32_t lo = __byte_perm(wq[v], 0x64646464u, 0x4140u);
+                            const uint32_t hi = __byte_perm(wq[v], 0x64646464u, 0x4342u);
+                            __half2 a = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&lo), bias), dd2);
+                            __half2 b = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&hi), bias), dd2);
+                            outw[8 * cc + 2 * v] = *reinterpret_cast<uint32_t *>(&a);
+                            outw[8 * cc + 2 * v + 1] = *reinterpret_cast<uint32_t *>(&b);
+                        }
+                    }
+                    tmem_st16(tmem + lane_base + uint32_t(A_BASE + slot * A_COLS + 16 * h), outw);
+                }
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(&afull[slot]);
@@ -364,10 +386,10 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
                     report(p.err, ERR_TIMEOUT_DRAIN);
         }
     } else {
-        // ---------------------------------------------------------------- epilogue (8 warps)
+        // ---------------------------------------------------------------- epilogue
         // Warp e (e = warp % 4) reads TMEM lanes 32e.. (rows 32e..32e+31 of the tile), 16 token
-        // columns at a time: warps 0-3 the first half of the tile's columns, the other four the
-        // rest. Each lane stores its row's values with plain stores (for each token the warp
+        // columns at a time: with 8 epilogue warps, warps 0-3 the first half of the tile's
+        // columns and the other four the rest; with 4, all of them. Each lane stores its row's values with plain stores (for each token the warp
         // writes 32 consecutive floats, one 128-byte segment); this measured faster here than
         // bulk tensor stores through shared-memory staging boxes, which queue behind the loads.
         // The accumulator is handed back as soon as a warp's last columns are in registers.
@@ -386,7 +408,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
             tc_fence_after();
             // this warp's columns: [cbeg, cend), halves rounded to 16 (the second half is empty
             // when BN == 16: the warp only hands the accumulator back)
-            const int chalf = BN >= 32 ? (BN / 2 + 15) / 16 * 16 : BN;
+            const int chalf = (EPI_WARPS == 8 && BN >= 32) ? (BN / 2 + 15) / 16 * 16 : BN;
             const int cbeg = eh ? chalf : 0, cend = eh ? BN : chalf;
             if (cbeg >= cend) {
                 tc_fence_before();
@@ -529,6 +551,9 @@ long long row_tiles(const GemmJob &G) {
 namespace {
 
 // Tokens per tile: the largest t split into passes of <= MAX_BN, rounded up to 16.
+// CTAs per SM for a tile of bn tokens: two issuers per tensor core up to 64 tokens.
+int cps_of(int bn) { return bn <= TcShape<2>::MAX_BN_SHAPE ? 2 : 1; }
+
 int choose_bn(const GemmJob *jobs, int n) {
     int tmax = 0;
     for (int j = 0; j < n; ++j)
@@ -539,13 +564,13 @@ int choose_bn(const GemmJob *jobs, int n) {
 }
 
 // K parts per job, from a cost model of the launch measured on B200: units run in waves of one
-// per SM; a unit costs its 64-column stages (~0.26 us each at 16 tokens, ~0.55 us at 256) plus its
+// per CTA slot (one or two per SM); a unit costs its 64-column stages (~0.26 us each at 16 tokens, ~0.55 us at 256) plus its
 // pipeline fill (~2 us) and epilogue drain (~7 us for a 128 x 256 fp32 tile, in proportion for
 // fewer tokens); a split job adds the reduce pass (a launch plus its partial planes read once and
 // y written, ~5 TB/s). The model picks the number of parts (1..16, each at least 4 stages long)
 // with the least estimated time; a part count must save 3% to beat a smaller one.
 void choose_splits(const GemmJob *jobs, int n, int bn, int num_sms, bool allow, int *ks) {
-    const int sms = num_sms > 0 ? num_sms : 148;
+    const int sms = (num_sms > 0 ? num_sms : 148) * cps_of(bn);
     auto kmax_of = [](const GemmJob &G) {
         const int nks = (G.cols + BK - 1) / BK;
         return nks / 4 > 1 ? nks / 4 : 1;
@@ -586,6 +611,39 @@ size_t part_bytes(const GemmJob &G, int ks) {
 
 size_t x_bytes(const GemmJob &G) { return (size_t(G.t) * G.cols * sizeof(__half) + 255) / 256 * 256; }
 
+// One launch of the CPS-per-SM shape. With CPS = 1 the CTA allocates all 512 TMEM columns, so a
+// second CTA on the SM would only wait in its allocation: more than half the SM's shared memory
+// keeps it off. With CPS = 2 two CTAs fit (256 columns and at most ~113 KB each).
+template <int CPS>
+cudaError_t launch_shape(const TcParams &p, size_t smem, int units, int num_sms, cudaStream_t stream, bool pdl) {
+    if (CPS == 1 && smem < 116 * 1024)
+        smem = 116 * 1024;
+    if (smem > (CPS == 1 ? 227 * 1024 : 113 * 1024))
+        return cudaErrorInvalidValue;
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<CPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             227 * 1024); // the SM's limit per CTA
+        if (e != cudaSuccess)
+            return e;
+        attr = true;
+    }
+    int grid = (num_sms > 0 ? num_sms : 148) * CPS;
+    if (grid > units)
+        grid = units;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(TcShape<CPS>::NT);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute lattr[1];
+    lattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    lattr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = lattr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<CPS>, p);
+}
+
 } // namespace
 
 size_t gemm_tc_scratch_bytes(const GemmJob *jobs, int n, int num_sms, bool split_k) {
@@ -613,10 +671,12 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
     p.njobs = n;
     p.bn = bn;
     p.err = err;
-    const int sb = stage_bytes(bn);
-    p.stages = int((SMEM_LIMIT - 512) / size_t(sb));
-    if (p.stages > MAX_STAGES)
-        p.stages = MAX_STAGES;
+    const int sb = stage_bytes(bn), cps = cps_of(bn);
+    const size_t smem_limit = cps == 1 ? SMEM_LIMIT : SMEM_LIMIT_2;
+    const int max_s = cps == 1 ? TcShape<1>::MAX_S : TcShape<2>::MAX_S;
+    p.stages = int((smem_limit - 512) / size_t(sb));
+    if (p.stages > max_s)
+        p.stages = max_s;
     if (p.stages < 2)
         return cudaErrorInvalidValue;
     uint8_t *sc = static_cast<uint8_t *>(scratch);
@@ -659,34 +719,8 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
     }
     p.total_units = units;
     size_t smem = size_t(p.stages) * sb + 8 * (3 * MAX_STAGES + 4) + 64 + 1024;
-    if (smem > 227 * 1024)
-        return cudaErrorInvalidValue;
-    // One CTA per SM: it allocates all 512 TMEM columns, so a second CTA on the SM would only wait
-    // in its allocation. More than half the SM's shared memory keeps a second one off.
-    if (smem < 116 * 1024)
-        smem = 116 * 1024;
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             227 * 1024); // the SM's limit per CTA
-        if (e != cudaSuccess)
-            return e;
-        attr = true;
-    }
-    int grid = num_sms > 0 ? num_sms : 148;
-    if (grid > units)
-        grid = units;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(NT);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute lattr[1];
-    lattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    lattr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = lattr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel, p);
+    cudaError_t e = cps == 1 ? launch_shape<1>(p, smem, units, num_sms, stream, pdl)
+                             : launch_shape<2>(p, smem, units, num_sms, stream, pdl);
     if (e != cudaSuccess)
         return e;
     // the split jobs' partial sums, added in K order (stream order after the product)
