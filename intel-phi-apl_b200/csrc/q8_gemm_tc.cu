@@ -10,8 +10,9 @@
 // tcgen05 kind::f16 rate with 3 more mantissa bits, which is what holds the product within the
 // stated 2e-3 (bf16 tiles measure ~1e-2 on the BASELINE shapes).
 //
-// A CTA (persistent, one per SM: it owns all 512 TMEM columns) runs 128-row x BN-token tiles (a
-// SwiGLU pair's tile: 64 rows of the gate matrix and the same 64 rows of the up matrix):
+// A CTA (persistent; one per SM owning all 512 TMEM columns, or two per SM with 256 each for
+// tiles of up to 64 tokens: TcShape below) runs 128-row x BN-token tiles (a SwiGLU pair's tile:
+// 64 rows of the gate matrix and the same 64 rows of the up matrix). The roles, for one CTA per SM:
 //   warp 12     TMA: per 64-column stage, the quant box (128 rows x 64 B, 64B swizzle), the scale
 //               box (128 rows x 8 scales) and the fp16 x box (BN rows x 128 B, 128B swizzle), into
 //               a ring of S <= 8 shared-memory stages;
