@@ -23,7 +23,7 @@
 //               one tcgen05.commit per stage frees the shared stage and with it the A slot, and at
 //               a tile's end another frees the accumulator;
 //   warps 0-3,  epilogue: tcgen05.ld of TMEM lanes 32*(warp%4).. -> y (or silu(g)*u for a pair);
-//   14-17       two warps per lane quarter, each on half of the tile's token columns.
+//   14-25       four warps per lane quarter, each on a quarter of the tile's token columns.
 // A pair's tile interleaves its two matrices by TMEM lane: lanes 32e..32e+15 hold gate rows
 // 16e..16e+15 and lanes 32e+16..32e+31 the same up rows, so one warp holds both factors of its
 // 16 output rows and combines them with a lane exchange (shfl.xor 16).
@@ -63,16 +63,18 @@ constexpr int MAX_STAGES = 8;
 constexpr int A_COLS = BK / 2;
 
 // The CTA's shape: CPS CTAs per SM, each owning 512 / CPS TMEM columns.
-//   CPS = 1 (tiles of up to 256 tokens): 18 warps, 8 dequant (two per SM sub-partition, each on
-//     one 32-column block of a stage), 8 epilogue (two per TMEM lane quarter, each on half of
-//     the tile's columns); accumulators in columns [0, 256), up to 8 A slots from 256.
+//   CPS = 1 (tiles of up to 256 tokens): 26 warps, 8 dequant (two per SM sub-partition, each on
+//     one 32-column block of a stage), 16 epilogue (four per TMEM lane quarter, each on a quarter
+//     of the tile's columns: the drain holds the next tile's MMAs, and a SwiGLU pair's exchange
+//     and SiLU make it longer); accumulators in columns [0, 256), up to 8 A slots from 256.
 //   CPS = 2 (tiles of up to 64 tokens): 10 warps, 4 dequant (each thread both blocks of its row),
 //     4 epilogue; accumulators in [0, 128), up to 4 A slots from 128. Two CTAs share an SM and
 //     its tensor core: at N <= 64 an MMA instruction takes ~46 cycles while each wait in the
 //     issuing thread stalls it ~200, so a second issuer keeps the pipe fed.
 template <int CPS>
 struct TcShape {
-    static constexpr int NDQ = 8 / CPS, EPI_WARPS = 8 / CPS;
+    static constexpr int EPQ = CPS == 1 ? 4 : 1; // epilogue warps per TMEM lane quarter
+    static constexpr int NDQ = 8 / CPS, EPI_WARPS = 4 * EPQ;
     static constexpr int DQ_WARP0 = 4, TMA_WARP = DQ_WARP0 + NDQ, MMA_WARP = TMA_WARP + 1;
     static constexpr int NT = 32 * (MMA_WARP + 1 + EPI_WARPS - 4); // epilogue: warps 0-3 (+ after MMA_WARP)
     static constexpr int TMEM_COLS = 512 / CPS, ACC_COLS = 256 / CPS, A_BASE = ACC_COLS;
@@ -389,12 +391,12 @@ __global__ void __launch_bounds__(TcShape<CPS>::NT, CPS) gemm_tc_kernel(const __
     } else {
         // ---------------------------------------------------------------- epilogue
         // Warp e (e = warp % 4) reads TMEM lanes 32e.. (rows 32e..32e+31 of the tile), 16 token
-        // columns at a time: with 8 epilogue warps, warps 0-3 the first half of the tile's
-        // columns and the other four the rest; with 4, all of them. Each lane stores its row's values with plain stores (for each token the warp
+        // columns at a time; the quarter's EPQ warps share the tile's columns in whole 16-column
+        // chunks. Each lane stores its row's values with plain stores (for each token the warp
         // writes 32 consecutive floats, one 128-byte segment); this measured faster here than
         // bulk tensor stores through shared-memory staging boxes, which queue behind the loads.
         // The accumulator is handed back as soon as a warp's last columns are in registers.
-        const int e = warp & 3, eh = warp > MMA_WARP ? 1 : 0;
+        const int e = warp & 3, eh = warp > MMA_WARP ? 1 + (warp - MMA_WARP - 1) / 4 : 0; // column share
         int tcount = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x, ++tcount) {
@@ -407,10 +409,11 @@ __global__ void __launch_bounds__(TcShape<CPS>::NT, CPS) gemm_tc_kernel(const __
                 break;
             }
             tc_fence_after();
-            // this warp's columns: [cbeg, cend), halves rounded to 16 (the second half is empty
-            // when BN == 16: the warp only hands the accumulator back)
-            const int chalf = (EPI_WARPS == 8 && BN >= 32) ? (BN / 2 + 15) / 16 * 16 : BN;
-            const int cbeg = eh ? chalf : 0, cend = eh ? BN : chalf;
+            // this warp's columns: [cbeg, cend), whole 16-column chunks shared out over the
+            // quarter's warps (a warp left without one only hands the accumulator back)
+            constexpr int EPQ = Sh::EPQ;
+            const int nch = BN / 16; // 16-column chunks, split as evenly as they go over the quarter's warps
+            const int cbeg = 16 * (nch * eh / EPQ), cend = 16 * (nch * (eh + 1) / EPQ);
             if (cbeg >= cend) {
                 tc_fence_before();
                 mbar_arrive(&accempty[b]);
