@@ -534,7 +534,9 @@ def main() -> int:
             "data": "synthetic (seeded Q8_0, w ~ 0.02*N(0,1), x ~ N(0,1))",
             "config": {"workload": f"BASELINE config 5: 9B-class decode step weight products, {args.layers} layers + "
                                    f"151936x4096 head, M=1", "bytes_per_step": total,
-                       "parallelism": f"row-shard x{world} + NCCL all-gather per round" if world > 1 else "1 GPU",
+                       "parallelism": (f"row-shard x{world} + per-round gather of y "
+                                + ("in the product kernel over NVLink" if b.rt.peer_gather() else "by NCCL all-gather"))
+                               if world > 1 else "1 GPU",
                        "l2": "inputs larger than L2 (7.5 GB of weights per step)", "graph": "step captured as a CUDA graph"},
             "tok_s": round(1e3 / ms1, 1),
             "verify_m2": {"ms_per_step": round(ms2, 4), "GB_s": round(total2 / ms2 / 1e6, 1),
