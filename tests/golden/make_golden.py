@@ -2,7 +2,7 @@
 
     make -C oracle && python tests/golden/make_golden.py
 
-Needs the reference tree (REF_ROOT, default /root/reference) and oracle/_ref/libq8ref.so, the
+Needs the reference source tree (its location in REF_ROOT) and oracle/_ref/libq8ref.so, the
 reference's own host-model kernels compiled from its sources by oracle/Makefile. Writes:
 
 * ref_gates.json -- the reference's golden known answers for the up-conversions, fma and tree
