@@ -79,7 +79,7 @@ struct TcShape {
     static constexpr int NT = 32 * (MMA_WARP + 1 + EPI_WARPS - 4); // epilogue: warps 0-3 (+ after MMA_WARP)
     static constexpr int TMEM_COLS = 512 / CPS, ACC_COLS = 256 / CPS, A_BASE = ACC_COLS;
     static constexpr int MAX_S = (TMEM_COLS - A_BASE) / A_COLS < MAX_STAGES ? (TMEM_COLS - A_BASE) / A_COLS : MAX_STAGES;
-    static constexpr int MAX_BN_SHAPE = 256 / CPS;
+    static constexpr int MAX_BN_SHAPE = CPS == 1 ? 256 : 64; // two accumulators of up to 64 columns
     static constexpr int BLOCKS_PER_THREAD = 2 / (NDQ / 4); // 32-column blocks per dequant thread per stage
 };
 // Shared memory per stage (1024-aligned): the quant box (128 rows x 64 B, 64B swizzle), the scale

@@ -325,11 +325,13 @@ def test_gather_index_out_of_range_is_reported_not_read(cuda, runtime, rtb, orac
 
 # ---------------------------------------------------------------- gemm on tensor cores (t >= 16)
 
-@pytest.mark.parametrize("t", [16, 17, 40, 64, 300])
+@pytest.mark.parametrize("t", [16, 17, 40, 64, 100, 300])
 @pytest.mark.parametrize("rows,cols", [(4096, 4096), (200, 12288), (129, 96), (1, 4128)])
 def test_gemm_tensor_cores(cuda, runtime, rtb, oracle, t, rows, cols):
     """BASELINE config 4 sizes and ragged ones: row tiles cut by the matrix end, K not a
-    multiple of the 64-column stage, several token passes (t = 300 > 256)."""
+    multiple of the 64-column stage, several token passes (t = 300 > 256). Tiles of up to 64
+    tokens run two CTAs per SM; t = 100 (a 112-token tile) and more run one, with two
+    accumulators up to 128 tokens."""
     m = Mat(cuda, rtb, oracle, rows, cols, 101)
     x = xs(oracle, t, cols, 102)
     xd = dev(cuda, x)
