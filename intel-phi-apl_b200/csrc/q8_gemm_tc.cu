@@ -68,7 +68,8 @@ constexpr int A_COLS = BK / 2;
 //     of the tile's columns: the drain holds the next tile's MMAs, and a SwiGLU pair's exchange
 //     and SiLU make it longer); accumulators in columns [0, 256), up to 8 A slots from 256.
 //   CPS = 2 (tiles of up to 64 tokens): 10 warps, 4 dequant (each thread both blocks of its row),
-//     4 epilogue; accumulators in [0, 128), up to 4 A slots from 128. Two CTAs share an SM and
+//     4 epilogue; accumulators at columns 0 and 64, the A slots from the next 32-column boundary
+//     (5 of them for tiles of <= 32 tokens, else 4). Two CTAs share an SM and
 //     its tensor core: at N <= 64 an MMA instruction takes ~46 cycles while each wait in the
 //     issuing thread stalls it ~200, so a second issuer keeps the pipe fed.
 template <int CPS>
@@ -78,7 +79,6 @@ struct TcShape {
     static constexpr int DQ_WARP0 = 4, TMA_WARP = DQ_WARP0 + NDQ, MMA_WARP = TMA_WARP + 1;
     static constexpr int NT = 32 * (MMA_WARP + 1 + EPI_WARPS - 4); // epilogue: warps 0-3 (+ after MMA_WARP)
     static constexpr int TMEM_COLS = 512 / CPS, ACC_COLS = 256 / CPS, A_BASE = ACC_COLS;
-    static constexpr int MAX_S = (TMEM_COLS - A_BASE) / A_COLS < MAX_STAGES ? (TMEM_COLS - A_BASE) / A_COLS : MAX_STAGES;
     static constexpr int MAX_BN_SHAPE = CPS == 1 ? 256 : 64; // two accumulators of up to 64 columns
     static constexpr int BLOCKS_PER_THREAD = 2 / (NDQ / 4); // 32-column blocks per dequant thread per stage
 };
@@ -104,6 +104,7 @@ struct TcParams {
     CUtensorMap tx[8];   // fp16 x per job
     TcJobDev job[8];
     int njobs, total_units, bn, stages;
+    int a_base; // TMEM column of the first A slot (after the accumulators)
     unsigned *err;
 };
 
@@ -213,7 +214,8 @@ template <int CPS>
 __global__ void __launch_bounds__(TcShape<CPS>::NT, CPS) gemm_tc_kernel(const __grid_constant__ TcParams p) {
     using Sh = TcShape<CPS>;
     constexpr int NDQ = Sh::NDQ, EPI_WARPS = Sh::EPI_WARPS, DQ_WARP0 = Sh::DQ_WARP0, TMA_WARP = Sh::TMA_WARP,
-                  MMA_WARP = Sh::MMA_WARP, TMEM_COLS = Sh::TMEM_COLS, A_BASE = Sh::A_BASE;
+                  MMA_WARP = Sh::MMA_WARP, TMEM_COLS = Sh::TMEM_COLS;
+    const int A_BASE = p.a_base;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int S = p.stages, BN = p.bn, SB = stage_bytes(BN), NACC = n_acc(BN, CPS), ACC_STRIDE = Sh::ACC_COLS / NACC;
@@ -677,7 +679,14 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
     p.err = err;
     const int sb = stage_bytes(bn), cps = cps_of(bn);
     const size_t smem_limit = cps == 1 ? SMEM_LIMIT : SMEM_LIMIT_2;
-    const int max_s = cps == 1 ? TcShape<1>::MAX_S : TcShape<2>::MAX_S;
+    // the A slots follow the accumulators (at columns 0 and ACC_COLS / 2 when double-buffered),
+    // on a 32-column boundary: two CTAs per SM with tiles of <= 32 tokens fit a fifth stage
+    const int acc_stride = (cps == 1 ? TcShape<1>::ACC_COLS : TcShape<2>::ACC_COLS) / n_acc(bn, cps);
+    const int acc_end = (n_acc(bn, cps) - 1) * acc_stride + bn;
+    p.a_base = cps == 1 ? TcShape<1>::A_BASE : (acc_end + A_COLS - 1) / A_COLS * A_COLS;
+    const int tmem_cols = cps == 1 ? TcShape<1>::TMEM_COLS : TcShape<2>::TMEM_COLS;
+    int max_s = (tmem_cols - p.a_base) / A_COLS;
+    max_s = max_s < MAX_STAGES ? max_s : MAX_STAGES;
     p.stages = int((smem_limit - 512) / size_t(sb));
     if (p.stages > max_s)
         p.stages = max_s;
