@@ -323,11 +323,12 @@ class Bench:
                 "us_per_launch": round(dur * 1e6, 2)}
 
     def e2e(self, steps: int, warmup: int) -> dict:
-        """The reference-facing path: blocking C-ABI calls with host buffers. Per round, the
-        round's x goes host->device from pinned memory, the product runs, and y comes back
-        device->host, as the reference engine pulls x and pushes y each phase."""
+        """The reference-facing path with host buffers, one round at a time as the reference engine
+        runs them: per round x goes host->device from pinned memory (rt_b200_pull, the engine's
+        link_pull), the product is enqueued through the C ABI, and y comes back device->host
+        (rt_b200_push, the engine's link_push), which returns once y is on the host."""
         torch, rt = self.torch, self.rt
-        rt.set_async(False)
+        rt.set_async(True)
         rt.set_stream(torch.cuda.current_stream().cuda_stream)
         hx = {k: v.cpu().pin_memory() for k, v in self.x.items() if k[1] == 1}
         hy = {k: torch.empty(v.numel(), dtype=torch.float32).pin_memory() for k, v in self.y.items() if k[1] == 1}
@@ -336,12 +337,12 @@ class Bench:
 
         def rnd(name_x, xdev, fn, name_y):
             nonlocal h2d, d2h
-            xdev.copy_(hx[(name_x, 1)], non_blocking=True)
+            nx, ny = xdev.numel() * 4, self.y[(name_y, 1)].numel() * 4
+            rt.pull(xdev.data_ptr(), hx[(name_x, 1)].data_ptr(), nx)
             fn()
-            hy[(name_y, 1)].copy_(self.y[(name_y, 1)], non_blocking=True)
-            torch.cuda.current_stream().synchronize()
-            h2d += xdev.numel() * 4
-            d2h += self.y[(name_y, 1)].numel() * 4
+            rt.push(hy[(name_y, 1)].data_ptr(), self.y[(name_y, 1)].data_ptr(), ny)
+            h2d += nx
+            d2h += ny
 
         def one_step():
             y = self.y
@@ -366,7 +367,8 @@ class Bench:
         total = WL.step_bytes(1, self.layers)
         return {"value": round(total / dt / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d // steps,
                 "d2h_bytes_per_step": d2h // steps, "ms_per_step": round(dt * 1e3, 3),
-                "tok_s": round(1.0 / dt, 1), "path": "blocking rt_gemv / rt_gemm_silu per round, pinned host x and y"}
+                "tok_s": round(1.0 / dt, 1),
+                "path": "per round: rt_b200_pull of x, rt_gemv / rt_gemm_silu, rt_b200_push of y (pinned host buffers)"}
 
     def _graph(self, fns):
         """The calls captured as one CUDA graph on a side stream (the runtime follows the stream)."""

@@ -145,6 +145,15 @@ RTB_API int rt_b200_last_error(struct rt *R, char *msg, size_t n);
 RTB_API void rt_b200_set_async(struct rt *R, int on);
 RTB_API int rt_b200_sync(struct rt *R);
 
+/* The link crossing of a round, where the engine keeps x and y in host memory (the reference's
+ * link_pull / link_push, src/card/link.c:86-118). pull enqueues a host -> device copy of `bytes`
+ * on R's stream and returns; push enqueues the device -> host copy, waits for R's stream (the
+ * bytes are on the host at return, and a kernel's error word is read) and returns 0 or the first
+ * error. Pinned host memory keeps the copies asynchronous. A round: pull x, the product (async
+ * mode), push y. */
+RTB_API int rt_b200_pull(struct rt *R, void *dev, const void *host, size_t bytes);
+RTB_API int rt_b200_push(struct rt *R, void *host, const void *dev, size_t bytes);
+
 /* 1: the caller vouches that no kernel between products writes the weight matrices (model
  * weights are read-only after load). Each product kernel is then launched with programmatic
  * dependent launch and streams its weights while the previous kernel on the stream finishes; it

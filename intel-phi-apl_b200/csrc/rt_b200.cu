@@ -802,6 +802,33 @@ int rt_b200_sync(struct rt *R) {
     return c->status;
 }
 
+int rt_b200_pull(struct rt *R, void *dev, const void *host, size_t bytes) {
+    Ctx *c = ctx_of(R);
+    if (!c)
+        return RTB_ENOTINIT;
+    if ((!dev || !host) && bytes) {
+        ctx_err(c, RTB_EINVAL, "rt_b200_pull: null pointer");
+        return RTB_EINVAL;
+    }
+    if (bytes && !cuda_ok(c, cudaMemcpyAsync(dev, host, bytes, cudaMemcpyHostToDevice, c->stream), "rt_b200_pull"))
+        return c->status;
+    return RTB_OK;
+}
+
+int rt_b200_push(struct rt *R, void *host, const void *dev, size_t bytes) {
+    Ctx *c = ctx_of(R);
+    if (!c)
+        return RTB_ENOTINIT;
+    if ((!dev || !host) && bytes) {
+        ctx_err(c, RTB_EINVAL, "rt_b200_push: null pointer");
+        return RTB_EINVAL;
+    }
+    if (bytes && !cuda_ok(c, cudaMemcpyAsync(host, dev, bytes, cudaMemcpyDeviceToHost, c->stream), "rt_b200_push"))
+        return c->status;
+    read_error_word(c); // waits for the stream: the bytes have landed, kernel errors surface here
+    return c->status;
+}
+
 void *rt_b200_stream(struct rt *R) {
     Ctx *c = ctx_of(R);
     return c ? static_cast<void *>(c->stream) : nullptr;

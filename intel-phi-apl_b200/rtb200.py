@@ -28,7 +28,7 @@ EXPORTS = ("rt_init", "rt_gemv", "rt_gemv_q", "rt_gemv_open", "rt_gemv_go", "rt_
            "rt_b200_last_error", "rt_b200_set_overlap", "rt_b200_set_async", "rt_b200_sync", "rt_b200_stream", "rt_b200_set_stream",
            "rt_b200_free", "rt_b200_nccl_id", "rt_b200_shard", "rt_b200_peer_gather", "rt_b200_chain_begin",
            "rt_b200_chain_end", "rtb_gguf_info", "rt_b200_load_gguf", "rtb_load_error", "rtb_synth_q8_0",
-           "rtb_synth_f32", "rt_gemm_static")
+           "rtb_synth_f32", "rt_gemm_static", "rt_b200_pull", "rt_b200_push")
 
 
 class RtError(RuntimeError):
@@ -89,6 +89,8 @@ def load() -> C.CDLL:
         "rt_b200_set_async": ([R, C.c_int], None),
         "rt_b200_set_overlap": ([R, C.c_int], None),
         "rt_b200_sync": ([R], C.c_int),
+        "rt_b200_pull": ([R, _P, _P, C.c_size_t], C.c_int),
+        "rt_b200_push": ([R, _P, _P, C.c_size_t], C.c_int),
         "rt_b200_stream": ([R], _P),
         "rt_b200_set_stream": ([R, _P], None),
         "rt_b200_free": ([R], None),
@@ -255,6 +257,20 @@ class Runtime:
         if code:
             _check(self)
             raise RtError(code, "rt_b200_sync")
+
+    def pull(self, dev: int, host: int, nbytes: int) -> None:
+        """Host -> device copy of nbytes on the runtime's stream (returns at once)."""
+        code = self.lib.rt_b200_pull(self._ref, dev, host, nbytes)
+        if code:
+            _check(self)
+            raise RtError(code, "rt_b200_pull")
+
+    def push(self, host: int, dev: int, nbytes: int) -> None:
+        """Device -> host copy of nbytes; returns once they are on the host."""
+        code = self.lib.rt_b200_push(self._ref, host, dev, nbytes)
+        if code:
+            _check(self)
+            raise RtError(code, "rt_b200_push")
 
     def stream(self) -> int:
         return self.lib.rt_b200_stream(self._ref) or 0

@@ -148,6 +148,28 @@ def test_gemv_two_ctas_per_sm(cuda, runtime, rtb, oracle, rows, cols):
     assert bits_equal(y.cpu().numpy(), oracle.gemv(m.q8, rows, cols, x[0]))
 
 
+def test_round_through_host_buffers(cuda, runtime, rtb, oracle):
+    """The engine's link crossing (link_pull / link_push of src/card/link.c:86-118): x pulled from
+    pinned host memory, the product enqueued, y pushed back; push returns with y on the host."""
+    rows, cols = 512, 4096
+    m = Mat(cuda, rtb, oracle, rows, cols, 31)
+    x = xs(oracle, 1, cols, 32)[0]
+    hx = cuda.from_numpy(x).pin_memory()
+    hy = cuda.zeros(rows, dtype=cuda.float32).pin_memory()
+    xd = cuda.empty(cols, dtype=cuda.float32, device="cuda")
+    yd = cuda.empty(rows, dtype=cuda.float32, device="cuda")
+    runtime.set_async(True)
+    for _ in range(3):  # repeated rounds on the same buffers
+        hy.zero_()
+        runtime.pull(xd.data_ptr(), hx.data_ptr(), 4 * cols)
+        runtime.gemv(m.ptr, rows, cols, xd.data_ptr(), yd.data_ptr())
+        runtime.push(hy.data_ptr(), yd.data_ptr(), 4 * rows)
+        assert bits_equal(hy.numpy(), oracle.gemv(m.q8, rows, cols, x))
+    runtime.set_async(False)
+    with pytest.raises(rtb.RtError):
+        runtime.push(hy.data_ptr(), 0, 4 * rows)
+
+
 def test_gemv_output_head_full_size(cuda, runtime, rtb, oracle):
     """BASELINE config 2's output head, 151936 x 4096, every output bit for bit."""
     rows, cols = 151936, 4096
