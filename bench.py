@@ -333,30 +333,38 @@ class Bench:
         hx = {k: v.cpu().pin_memory() for k, v in self.x.items() if k[1] == 1}
         hy = {k: torch.empty(v.numel(), dtype=torch.float32).pin_memory() for k, v in self.y.items() if k[1] == 1}
         xd, xf = self.x[("d", 1)], self.x[("ff", 1)]
-        h2d = d2h = 0
 
-        def rnd(name_x, xdev, fn, name_y):
-            nonlocal h2d, d2h
-            nx, ny = xdev.numel() * 4, self.y[(name_y, 1)].numel() * 4
-            rt.pull(xdev.data_ptr(), hx[(name_x, 1)].data_ptr(), nx)
-            fn()
-            rt.push(hy[(name_y, 1)].data_ptr(), self.y[(name_y, 1)].data_ptr(), ny)
-            h2d += nx
-            d2h += ny
+        # Every round as a C engine makes it: three C-ABI calls with their arguments bound once
+        # (pull x, the product, push y), push's return code carrying any error of the round.
+        lib, ref = rt.lib, rt._ref
+        y = self.y
+        rounds = []
+
+        def add(name_x, xdev, fn, args, name_y):
+            nx, ny = xdev.numel() * 4, y[(name_y, 1)].numel() * 4
+            rounds.append(((ref, xdev.data_ptr(), hx[(name_x, 1)].data_ptr(), nx), fn, (ref,) + args,
+                           (ref, hy[(name_y, 1)].data_ptr(), y[(name_y, 1)].data_ptr(), ny)))
+
+        for L in self.w:
+            add("d", xd, lib.rt_gemv, (L["qkv"].data_ptr(), WL.QKV, WL.D, xd.data_ptr(), y[("qkv", 1)].data_ptr()), "qkv")
+            add("d", xd, lib.rt_gemv, (L["out"].data_ptr(), WL.D, WL.D, xd.data_ptr(), y[("out", 1)].data_ptr()), "out")
+            add("d", xd, lib.rt_gemm_silu, (L["gate"].data_ptr(), L["up"].data_ptr(), WL.FF, WL.D, xd.data_ptr(), 1,
+                                            y[("h", 1)].data_ptr()), "h")
+            add("ff", xf, lib.rt_gemv, (L["down"].data_ptr(), WL.D, WL.FF, xf.data_ptr(), y[("down", 1)].data_ptr()), "down")
+        add("d", xd, lib.rt_gemv, (self.head.data_ptr(), WL.VOCAB, WL.D, xd.data_ptr(), y[("head", 1)].data_ptr()), "head")
+        h2d = sum(r[0][3] for r in rounds)
+        d2h = sum(r[3][3] for r in rounds)
+        pull, push = lib.rt_b200_pull, lib.rt_b200_push
 
         def one_step():
-            y = self.y
-            for L in self.w:
-                rnd("d", xd, lambda: rt.gemv(L["qkv"].data_ptr(), WL.QKV, WL.D, xd.data_ptr(), y[("qkv", 1)].data_ptr()), "qkv")
-                rnd("d", xd, lambda: rt.gemv(L["out"].data_ptr(), WL.D, WL.D, xd.data_ptr(), y[("out", 1)].data_ptr()), "out")
-                rnd("d", xd, lambda: rt.gemm_silu(L["gate"].data_ptr(), L["up"].data_ptr(), WL.FF, WL.D, xd.data_ptr(), 1,
-                                                  y[("h", 1)].data_ptr()), "h")
-                rnd("ff", xf, lambda: rt.gemv(L["down"].data_ptr(), WL.D, WL.FF, xf.data_ptr(), y[("down", 1)].data_ptr()), "down")
-            rnd("d", xd, lambda: rt.gemv(self.head.data_ptr(), WL.VOCAB, WL.D, xd.data_ptr(), y[("head", 1)].data_ptr()), "head")
+            for pa, fn, fa, qa in rounds:
+                pull(*pa)
+                fn(*fa)
+                if push(*qa):
+                    rt.sync()  # raises with the runtime's message
 
         for _ in range(warmup):
             one_step()
-        h2d = d2h = 0
         self.barrier()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
@@ -365,8 +373,8 @@ class Bench:
         torch.cuda.synchronize()
         dt = self.max_over_ranks((time.perf_counter() - t0) / steps)
         total = WL.step_bytes(1, self.layers)
-        return {"value": round(total / dt / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d // steps,
-                "d2h_bytes_per_step": d2h // steps, "ms_per_step": round(dt * 1e3, 3),
+        return {"value": round(total / dt / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(dt * 1e3, 3),
                 "tok_s": round(1.0 / dt, 1),
                 "path": "per round: rt_b200_pull of x, rt_gemv / rt_gemm_silu, rt_b200_push of y (pinned host buffers)"}
 
