@@ -48,3 +48,38 @@ def test_reference_arm_is_silent_on_other_ranks():
                   env={"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
     assert p.returncode == 0, p.stderr[-2000:]
     assert p.stdout.strip() == ""
+
+
+def check_gpu_line(d: dict) -> None:
+    """The keys and relations of the bench line of the B200 arm (one GPU)."""
+    for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+              "vs_baseline", "dtype", "data", "config", "roofline", "e2e", "gpu_launches", "clocks"):
+        assert k in d, k
+    assert d["n_gpus"] == 1 and d["warmup"] >= 3 and d["value"] > 0 and d["gpu_launches"] > 0
+    assert abs(d["value"] - d["config"]["bytes_per_step"] / d["ms_per_step"] / 1e6) <= 0.01 * d["value"]
+    r = d["roofline"]
+    assert r["bound"] == "hbm" and r["unit"] == "GB/s" and r["peak"] > 0
+    assert abs(r["frac"] - r["achieved"] / r["peak"]) < 1e-3
+    e = d["e2e"]
+    assert e["unit"] == d["unit"] and e["value"] > 0 and e["h2d_bytes_per_step"] > 0 and e["d2h_bytes_per_step"] > 0
+    assert {"sm_mhz", "sm_max_mhz", "reasons"} <= set(d["clocks"])
+
+
+def test_gpu_line_checker_accepts_a_recorded_line():
+    # a line bench.py printed on a B200 (trimmed to the keys the checker reads)
+    d = {"metric": "Q8_0 weight-product GB/s, 9B decode step (M=1)", "value": 3700.2, "unit": "GB/s", "n_gpus": 1,
+         "steps": 200, "warmup": 5, "ms_per_step": 2.0307, "higher_is_better": True, "scaling": "strong",
+         "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": {"workload": "w", "bytes_per_step": 7513769472},
+         "roofline": {"bound": "hbm", "achieved": 5592.9, "peak": 6456.2, "unit": "GB/s", "frac": 0.8663},
+         "e2e": {"value": 1302.0, "unit": "GB/s", "h2d_bytes_per_step": 3162112, "d2h_bytes_per_step": 4277760},
+         "gpu_launches": 51600, "clocks": {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []}}
+    check_gpu_line(d)
+
+
+@pytest.mark.gpu
+def test_bench_one_gpu_line():
+    p = run_bench("--steps", "3", "--warmup", "3", "--no-prompt")
+    assert p.returncode == 0, p.stderr[-2000:]
+    lines = [ln for ln in p.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 1
+    check_gpu_line(json.loads(lines[0]))
