@@ -126,9 +126,10 @@ class ClockSampler:
         except OSError:
             self.proc = None
 
-    def stop(self) -> dict | None:
+    def stop(self) -> dict:
+        none = {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}  # no nvidia-smi, or too short
         if self.proc is None:
-            return None
+            return none
         self.proc.terminate()
         try:
             out, _ = self.proc.communicate(timeout=5)
@@ -150,7 +151,7 @@ class ClockSampler:
                 if v.lower().startswith("active"):
                     reasons.add(n)
         if not sm:
-            return None
+            return none
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
 
 

@@ -62,7 +62,7 @@ def check_gpu_line(d: dict) -> None:
     assert abs(r["frac"] - r["achieved"] / r["peak"]) < 1e-3
     e = d["e2e"]
     assert e["unit"] == d["unit"] and e["value"] > 0 and e["h2d_bytes_per_step"] > 0 and e["d2h_bytes_per_step"] > 0
-    assert {"sm_mhz", "sm_max_mhz", "reasons"} <= set(d["clocks"])
+    assert {"sm_mhz", "sm_max_mhz", "reasons", "samples"} <= set(d["clocks"])
 
 
 def test_gpu_line_checker_accepts_a_recorded_line():
@@ -72,13 +72,13 @@ def test_gpu_line_checker_accepts_a_recorded_line():
          "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": {"workload": "w", "bytes_per_step": 7513769472},
          "roofline": {"bound": "hbm", "achieved": 5592.9, "peak": 6456.2, "unit": "GB/s", "frac": 0.8663},
          "e2e": {"value": 1302.0, "unit": "GB/s", "h2d_bytes_per_step": 3162112, "d2h_bytes_per_step": 4277760},
-         "gpu_launches": 51600, "clocks": {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []}}
+         "gpu_launches": 51600, "clocks": {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": [], "samples": 19}}
     check_gpu_line(d)
 
 
 @pytest.mark.gpu
 def test_bench_one_gpu_line():
-    p = run_bench("--steps", "3", "--warmup", "3", "--no-prompt")
+    p = run_bench("--steps", "40", "--warmup", "3", "--no-prompt")
     assert p.returncode == 0, p.stderr[-2000:]
     lines = [ln for ln in p.stdout.splitlines() if ln.strip()]
     assert len(lines) == 1
