@@ -5,7 +5,8 @@
 // At 16+ tokens the product is a dense contraction (the reference batches prompts of 16 and
 // verify passes of K+1 tokens through the same weight pass, src/card/gemm.c:271-294). The
 // per-(row, 32-column) fp16 scale d cannot be factored out of a K contraction, so each weight tile
-// is dequantised to fp16 in shared memory first: q is exact in fp16, and fl16(q*d) rounds once.
+// is dequantised to fp16 first, into tensor memory as the MMA's A operand: q is exact in fp16, and
+// fl16(q*d) rounds once.
 // x is rounded to fp16 once per call (a pre-pass into scratch). fp16 rather than bf16: the same
 // tcgen05 kind::f16 rate with 3 more mantissa bits, which is what holds the product within the
 // stated 2e-3 (bf16 tiles measure ~1e-2 on the BASELINE shapes).
@@ -30,8 +31,8 @@
 // A stays out of shared memory: the stage's traffic there is the bulk copies in, the dequant's
 // quant reads and the tensor core's reads of x (writing A to shared memory and reading it back
 // made the kernel shared-memory bound at ~1000 cycles per 64-column stage).
-// The MMA thread is the critical issuer: every barrier wait or commit it adds costs tensor-pipe
-// time (a shared-memory wait ~30 cycles per MMA, measured). So it waits once per stage, on the A
+// The MMA thread is the critical issuer: a barrier wait stalls it ~200 cycles and a commit ~70
+// (measured), with only about four MMAs queued behind it. So it waits once per stage, on the A
 // slot's barrier only: the dequant threads arrive there after waiting for the stage's copies, so
 // the stage's x box has landed too; and the A slot needs no barrier of its own, because the
 // producer refills a shared stage only after its MMAs completed, and the dequant writes the slot
@@ -57,16 +58,17 @@ constexpr int BK = 64;           // columns per stage
 constexpr int MAX_BN = 256;      // tokens per tile (MMA N)
 constexpr int PAIR_ROWS = BM / 2; // output rows per tile of a SwiGLU pair
 constexpr int MAX_STAGES = 8;
-// Tensor memory (512 columns x 128 lanes of 32 bits): the accumulators in columns [0, 256), two
-// of 128 columns when a tile has <= 128 tokens (double-buffered), else one of 256; the dequantised A tiles in a ring of one 32-column slot per shared stage from
-// column 256 (a 128 x 64 fp16 tile: lane = row, column j = k 2j and 2j+1; 8 slots fill [256, 512)).
+// Tensor memory (128 lanes x 512 columns of 32 bits per SM): the accumulators first, then the
+// dequantised A tiles in a ring of one 32-column slot per shared stage (a 128 x 64 fp16 tile:
+// lane = row, column j = k 2j and 2j+1). How the columns are shared out: TcShape.
 constexpr int A_COLS = BK / 2;
 
 // The CTA's shape: CPS CTAs per SM, each owning 512 / CPS TMEM columns.
 //   CPS = 1 (tiles of up to 256 tokens): 26 warps, 8 dequant (two per SM sub-partition, each on
 //     one 32-column block of a stage), 16 epilogue (four per TMEM lane quarter, each on a quarter
 //     of the tile's columns: the drain holds the next tile's MMAs, and a SwiGLU pair's exchange
-//     and SiLU make it longer); accumulators in columns [0, 256), up to 8 A slots from 256.
+//     and SiLU make it longer); accumulators in columns [0, 256) (two of 128 columns, double-
+//     buffered, for tiles of <= 128 tokens, else one of 256), up to 8 A slots from 256.
 //   CPS = 2 (tiles of up to 64 tokens): 10 warps, 4 dequant (each thread both blocks of its row),
 //     4 epilogue; accumulators at columns 0 and 64, the A slots from the next 32-column boundary
 //     (5 of them for tiles of <= 32 tokens, else 4). Two CTAs share an SM and
@@ -108,8 +110,9 @@ struct TcParams {
     unsigned *err;
 };
 
-// The fp16 copy of x is written by the conversion kernel just before this one on the stream: the
-// producer waits for it (a no-op without programmatic launch) before its first x load.
+// The fp16 copy of x is written by the conversion kernel just before this one on the stream: every
+// thread waits for it (griddepcontrol.wait, a no-op without programmatic launch) before the roles
+// start.
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, int c0, int c1, uint64_t *bar) {
     asm volatile(
