@@ -103,12 +103,4 @@ __device__ __forceinline__ void report(unsigned *err, unsigned bits) {
         atomicOr(err, bits);
 }
 
-// fp32 from the 8-bit two's complement q through the exponent trick: 2^23 + (q + 128) as bits,
-// minus 2^23 + 128. Exact for every q. `w` holds four quants; k selects the byte (0..3).
-__device__ __forceinline__ float q_to_f32(uint32_t biased_word, int k) {
-    // biased_word = word ^ 0x80808080: byte k is q_k + 128
-    const uint32_t bits = __byte_perm(biased_word, 0x4B000000u, 0x7650u + static_cast<uint32_t>(k));
-    return __uint_as_float(bits) - 8388736.0f;
-}
-
 }  // namespace q8
