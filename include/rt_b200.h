@@ -128,7 +128,8 @@ enum {
     RTB_OK = 0,
     RTB_EINVAL = 1,   /* an argument the products cannot take (size, alignment, null) */
     RTB_ECUDA = 2,    /* a CUDA runtime call failed */
-    RTB_EKERNEL = 3,  /* a kernel reported a bounded wait that gave up (error word) */
+    RTB_EKERNEL = 3,  /* a kernel reported through its error word: a bounded wait that gave up, or a
+                         gather index outside the matrix */
     RTB_ENOMEM = 4,   /* device memory */
     RTB_ENOTINIT = 5, /* R was not initialised by rt_init */
     RTB_EQUEUE = 6,   /* more than RT_BATCH*2 queued products */

@@ -13,7 +13,7 @@ enum : unsigned {
     ERR_TIMEOUT_TEMPTY = 1u << 2, // the chain never released a partial-sum buffer
     ERR_TIMEOUT_MMA = 1u << 3,    // a tensor-core stage never completed
     ERR_TIMEOUT_DRAIN = 1u << 4,  // copies in flight at exit never completed
-    ERR_BAD_JOB = 1u << 5,        // a job the kernel cannot run (host checks missed it)
+    ERR_BAD_JOB = 1u << 5,        // a gather index outside the matrix (its y is NaN), or a job the kernel cannot run
     ERR_TIMEOUT_PEER = 1u << 6,   // a peer GPU's flag never arrived
     ERR_TIMEOUT_ROUND = 1u << 7,  // a chained round's dependency never completed
 };

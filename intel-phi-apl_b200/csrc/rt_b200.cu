@@ -163,6 +163,27 @@ bool check_product(Ctx *c, const char *fn, const void *w, long long rows, long l
     return true;
 }
 
+// The error word's bits (q8_ptx.cuh), named for the message.
+void error_word_text(unsigned h, char *out, size_t n) {
+    static const char *const names[] = {
+        "a stage's bulk copy never completed",
+        "a stage's partial sums never arrived",
+        "the chain never released a partial-sum buffer",
+        "a tensor-core stage never completed",
+        "copies in flight at exit never completed",
+        "a gather index outside the matrix (its y is NaN)",
+        "a peer GPU's flag never arrived",
+        "a chained round's dependency never completed",
+    };
+    size_t used = 0;
+    out[0] = 0;
+    for (unsigned b = 0; b < sizeof names / sizeof names[0] && used + 1 < n; ++b)
+        if (h & (1u << b)) {
+            const int k = snprintf(out + used, n - used, "%s%s", used ? "; " : "", names[b]);
+            used = k < 0 ? n : used + size_t(k) < n ? used + size_t(k) : n - 1;
+        }
+}
+
 bool read_error_word(Ctx *c) {
     unsigned h = 0;
     if (!cuda_ok(c, cudaMemcpyAsync(&h, c->d_err, sizeof h, cudaMemcpyDeviceToHost, c->stream), "read error word"))
@@ -170,7 +191,9 @@ bool read_error_word(Ctx *c) {
     if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "synchronize"))
         return false;
     if (h) {
-        ctx_err(c, RTB_EKERNEL, "kernel error word 0x%x (a bounded wait gave up)", h);
+        char what[200];
+        error_word_text(h, what, sizeof what);
+        ctx_err(c, RTB_EKERNEL, "kernel error word 0x%x: %s", h, what);
         cuda_ok(c, cudaMemsetAsync(c->d_err, 0, sizeof(unsigned), c->stream), "clear error word");
         return false;
     }
@@ -241,8 +264,6 @@ bool flush_tc(Ctx *c, std::vector<q8::GemmJob> &jobs) {
     return true;
 }
 
-// Splits the items into kernel jobs (t >= 16: one tensor-core job; else passes of <= 4 tokens on
-// CUDA cores), launches them, then all-gathers the sharded outputs.
 // One row-sharded product of <= 4 tokens on CUDA cores, its y gathered through the peers' staging
 // images in the same launch (plus the receiving kernel), instead of an NCCL all-gather.
 bool peer_gatherable(const Ctx *c, const std::vector<Item> &items) {
@@ -286,6 +307,8 @@ bool run_peer_gathered(Ctx *c, const Item &it) {
                    "peer gather");
 }
 
+// Splits the items into kernel jobs (t >= 16: one tensor-core job; else passes of <= 4 tokens on
+// CUDA cores), launches them, then all-gathers the sharded outputs.
 bool run_items(Ctx *c, const std::vector<Item> &items) {
     if (peer_gatherable(c, items))
         return run_peer_gathered(c, items[0]);
