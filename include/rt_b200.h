@@ -203,7 +203,10 @@ RTB_API int rt_b200_chain_end(struct rt *R, int serial);
 /* ---------------------------------------------------------------- the weight loader
  * A GGUF file into device memory, its Q8_0 matrices repacked in place into the row-split layout
  * (the engine's load step: src/card/engine.c:268-330, src/card/stream.c:77-104).
- * rtb_gguf_info parses the header only (host): the tensor table and the file size.
+ * rtb_gguf_info parses the header only (host): the tensor table and the file size. A header whose
+ * sizes cannot be right (dims whose product wraps or exceeds 2^50 elements, a tensor running past
+ * the file's end, rows that are not whole blocks, an alignment that is not a power of two) is
+ * refused with RTB_EINVAL by both calls, before anything is read into the arena.
  * rt_b200_load_gguf reads the whole file into `arena` (device, >= the file size rounded up to 8,
  * 256-byte aligned) through page-aligned O_DIRECT reads into pinned buffers (buffered reads where
  * the file system refuses O_DIRECT), each slot's copy to the GPU overlapping the next read; then

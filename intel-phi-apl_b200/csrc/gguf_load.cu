@@ -171,8 +171,14 @@ bool parse(const char *path, Table *tab) {
         const uint32_t vt = r.u32();
         uint64_t v = 0;
         read_value(r, vt, &v);
-        if (r.ok && key == "general.alignment" && v)
+        if (r.ok && key == "general.alignment") {
+            if (v == 0 || (v & (v - 1)) || v > (1u << 20)) { // GGUF: a power of two
+                r.ok = false;
+                r.err = "general.alignment " + std::to_string(v) + " is not a power of two <= 1 MiB";
+                break;
+            }
             alignment = v;
+        }
     }
     for (uint64_t i = 0; i < n_tensors && r.ok; ++i) {
         rtb_tensor t;
@@ -185,10 +191,18 @@ bool parse(const char *path, Table *tab) {
             r.err = "tensor " + name + ": dims";
             break;
         }
+        // every size below stays far from 2^63, so no later sum or product of them wraps
         uint64_t ne = 1;
+        bool dims_ok = true;
         for (int d = 0; d < t.n_dims; ++d) {
-            t.dim[d] = (long long)r.u64();
-            ne *= uint64_t(t.dim[d]);
+            const uint64_t v = r.u64();
+            t.dim[d] = (long long)v;
+            dims_ok = dims_ok && v <= (1ull << 40) && !__builtin_mul_overflow(ne, v, &ne) && ne <= (1ull << 50);
+        }
+        if (r.ok && !dims_ok) {
+            r.ok = false;
+            r.err = "tensor " + name + ": implausible dims";
+            break;
         }
         t.type = int(r.u32());
         t.offset = r.u64();
@@ -198,9 +212,9 @@ bool parse(const char *path, Table *tab) {
             r.err = "tensor " + name + ": unsupported type " + std::to_string(t.type);
             break;
         }
-        if (r.ok && ne % be) {
+        if (r.ok && (ne % be || uint64_t(t.dim[0]) % be)) { // GGUF: every row is whole blocks
             r.ok = false;
-            r.err = "tensor " + name + ": elements not a whole number of blocks";
+            r.err = "tensor " + name + ": rows not a whole number of blocks";
             break;
         }
         t.bytes = ne / be * bb;
@@ -213,12 +227,13 @@ bool parse(const char *path, Table *tab) {
         return false;
     }
     tab->data_start = (header_end + alignment - 1) / alignment * alignment;
+    const uint64_t fb = tab->file_bytes; // < 2^63 (an off_t), so data_start + offset below cannot wrap
     for (rtb_tensor &t : tab->t) {
-        t.offset += tab->data_start;
-        if (t.offset + t.bytes > tab->file_bytes) {
+        if (t.offset > fb || t.bytes > fb || tab->data_start > fb || tab->data_start + t.offset > fb - t.bytes) {
             tab->err = std::string(path) + ": tensor " + t.name + " runs past the end of the file";
             return false;
         }
+        t.offset += tab->data_start;
     }
     return true;
 }
@@ -389,8 +404,9 @@ RTB_API int rt_b200_load_gguf(struct rt *R, const char *path, void *arena, unsig
         long long rows = 1;
         for (int d = 1; d < t.n_dims; ++d)
             rows *= t.dim[d];
-        if (q8s_row_bytes(cols) != q8_gguf_row_bytes(cols) || t.offset % 16)
-            continue; // a row would change length (cols % 256 != 0): left in GGUF layout
+        if (rows < 1 || cols > (1ll << 30) || q8s_row_bytes(cols) != q8_gguf_row_bytes(cols) || t.offset % 16)
+            continue; // empty, wider than the products take, or a row would change length (cols % 256
+                      // != 0): left in GGUF layout
         bool seen = false;
         for (uint64_t o : done)
             seen |= o == t.offset;

@@ -63,6 +63,52 @@ def test_gguf_info_rejects_what_is_not_gguf(rtb, tmp_path):
         rtb.gguf_info(str(short))
 
 
+def one_tensor_gguf(path, dims, typ, rel_offset, data: bytes, alignment: int = 32) -> None:
+    """A GGUF holding one tensor info with the given raw fields (sizes as an engine file would
+    never hold them), then `data` at the aligned data start."""
+    import struct
+    name = b"t"
+    head = b"GGUF" + struct.pack("<IQQ", 3, 1, 1)
+    key = b"general.alignment"
+    head += struct.pack("<Q", len(key)) + key + struct.pack("<II", 4, alignment)
+    head += struct.pack("<Q", len(name)) + name + struct.pack("<I", len(dims))
+    head += b"".join(struct.pack("<Q", d % 2 ** 64) for d in dims) + struct.pack("<IQ", typ, rel_offset % 2 ** 64)
+    a = alignment if alignment > 0 and alignment & (alignment - 1) == 0 else 32
+    start = (len(head) + a - 1) // a * a
+    with open(path, "wb") as f:
+        f.write(head + b"\0" * (start - len(head)) + data)
+
+
+def test_gguf_info_takes_a_well_formed_one_tensor_file(rtb, tmp_path):
+    p = str(tmp_path / "ok.gguf")
+    one_tensor_gguf(p, [256, 2], G.GGML_Q8_0, 0, bytes(2 * 8 * 34))
+    table, _ = rtb.gguf_info(p)
+    assert table[0]["dims"] == [256, 2] and table[0]["bytes"] == 2 * 8 * 34
+
+
+@pytest.mark.parametrize("case", ["dims_overflow", "dim_huge", "offset_wraps", "past_end", "ragged_q8_rows",
+                                  "alignment_not_pow2", "alignment_zero"])
+def test_gguf_info_rejects_crafted_sizes(rtb, tmp_path, case):
+    """Sizes that would wrap the loader's arithmetic or send the in-place repack outside the file:
+    refused while parsing the header, before anything is read into the arena."""
+    p = str(tmp_path / f"{case}.gguf")
+    data = bytes(2 * 8 * 34)
+    args = {
+        "dims_overflow": ([2 ** 32, 2 ** 32, 32], G.GGML_Q8_0, 0, data),  # the product wraps to 0
+        "dim_huge": ([32, 2 ** 45], G.GGML_Q8_0, 0, data),
+        "offset_wraps": ([256, 2], G.GGML_Q8_0, -32, data),  # offset + bytes wraps past 2^64
+        "past_end": ([256, 4], G.GGML_Q8_0, 0, data),
+        "ragged_q8_rows": ([48, 2], G.GGML_Q8_0, 0, data),  # 96 weights, but rows of 1.5 blocks
+        "alignment_not_pow2": ([256, 2], G.GGML_Q8_0, 0, data),
+        "alignment_zero": ([256, 2], G.GGML_Q8_0, 0, data),
+    }[case]
+    alignment = {"alignment_not_pow2": 48, "alignment_zero": 0}.get(case, 32)
+    one_tensor_gguf(p, *args, alignment=alignment)
+    with pytest.raises(rtb.RtError) as e:
+        rtb.gguf_info(p)
+    assert e.value.code == 1
+
+
 def test_file_sum_is_position_weighted(tmp_path):
     p = tmp_path / "w.bin"
     w = np.array([3, 5, 7], dtype=np.uint64)
