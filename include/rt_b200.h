@@ -88,6 +88,7 @@ RTB_API long gemv_s_bytes(long rows, long cols);
 /* GGUF Q8_0 rows (per 32 columns: fp16 d, 32 int8 q) -> the row-split layout, on the device.
  * q8 and out are device pointers; out == q8 (in place) is allowed when cols % 256 == 0, as the
  * reference repacks in place at load (src/card/gemv.c:42-52, src/card/engine.c:303-316).
+ * cols <= 192,736 (a GGUF row of at most 200 KiB, staged whole in shared memory).
  * Returns 0 or an RTB_E* code. Replaces gemv_i_repack (src/card/gemv.h:55). */
 RTB_API int gemv_s_repack(const void *q8, long rows, long cols, void *out);
 

@@ -404,8 +404,9 @@ RTB_API int rt_b200_load_gguf(struct rt *R, const char *path, void *arena, unsig
         long long rows = 1;
         for (int d = 1; d < t.n_dims; ++d)
             rows *= t.dim[d];
-        if (rows < 1 || cols > (1ll << 30) || q8s_row_bytes(cols) != q8_gguf_row_bytes(cols) || t.offset % 16)
-            continue; // empty, wider than the products take, or a row would change length (cols % 256
+        if (rows < 1 || q8_gguf_row_bytes(cols) > q8::REPACK_MAX_ROW_BYTES ||
+            q8s_row_bytes(cols) != q8_gguf_row_bytes(cols) || t.offset % 16)
+            continue; // empty, wider than the repack stages, or a row would change length (cols % 256
                       // != 0): left in GGUF layout
         bool seen = false;
         for (uint64_t o : done)

@@ -111,6 +111,9 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
                            unsigned *err, cudaStream_t stream, bool pdl, bool split_k);
 
 // ---- utilities
+// The repack stages a whole GGUF row in shared memory (what makes it safe in place): rows of at
+// most this many GGUF bytes, i.e. cols <= 192,736.
+constexpr long long REPACK_MAX_ROW_BYTES = 200 * 1024;
 cudaError_t launch_repack(const uint8_t *gguf, long long rows, int cols, uint8_t *out, cudaStream_t stream);
 cudaError_t launch_synth_q8(uint8_t *out_split, long long row0, long long rows, int cols, uint64_t seed,
                             uint64_t stream_id, float sigma, cudaStream_t stream);

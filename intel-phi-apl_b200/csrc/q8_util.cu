@@ -126,7 +126,7 @@ cudaError_t launch_repack(const uint8_t *gguf, long long rows, int cols, uint8_t
     if (rows < 1 || cols < Q8_QK || cols % Q8_QK)
         return cudaErrorInvalidValue;
     const long long gb = q8_gguf_row_bytes(cols);
-    if (gb > 200 * 1024)
+    if (gb > REPACK_MAX_ROW_BYTES)
         return cudaErrorInvalidValue;
     if (gb > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(repack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(gb));

@@ -761,6 +761,11 @@ int gemv_s_repack(const void *q8, long rows, long cols, void *out) {
         thread_err(RTB_EINVAL, "gemv_s_repack: bad argument");
         return RTB_EINVAL;
     }
+    if (q8_gguf_row_bytes(cols) > q8::REPACK_MAX_ROW_BYTES) {
+        thread_err(RTB_EINVAL, "gemv_s_repack: cols %ld above the repack's %lld", cols,
+                   q8::REPACK_MAX_ROW_BYTES / Q8_GGUF_BLOCK * Q8_QK);
+        return RTB_EINVAL;
+    }
     if (q8 == out && q8s_row_bytes(cols) != q8_gguf_row_bytes(cols)) {
         thread_err(RTB_EINVAL, "gemv_s_repack: in place needs cols %% 256 == 0");
         return RTB_EINVAL;
