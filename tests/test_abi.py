@@ -5,6 +5,10 @@ from __future__ import annotations
 import ctypes as C
 import os
 import re
+import shutil
+import subprocess
+
+import pytest
 
 from conftest import ROOT
 
@@ -54,3 +58,58 @@ def test_calls_without_init_record_an_error(rtb):
     code, msg = rtb.last_error(None)
     assert code == 5 and "rt_init" in msg
     assert rtb.last_error(None)[0] == 0  # reading clears
+
+
+# A C translation unit shaped like the engine's generated model code (a struct rt on the stack,
+# products on frame addresses, a queued round closed by rt_gemv_go): it must compile as C against
+# include/rt_b200.h and link against the library unchanged. Run without rt_init, every product
+# records RTB_ENOTINIT and touches no device.
+GENERATED_STYLE_C = r"""
+#include <stdio.h>
+#include "rt_b200.h"
+
+static float frame[4096 + 64] __attribute__((aligned(64)));
+
+int main(void)
+{
+    struct rt R = {0};
+    R.frame = (char *)frame;
+    const void *W = (const void *)0x1000;
+    float *X = frame, *V = frame + 4096;
+    int codes[8], k = 0;
+    rt_gemv(&R, W, 16, 4096, X, V);
+    codes[k++] = rt_b200_last_error(NULL, NULL, 0);
+    rt_gemv_open(&R);
+    codes[k++] = rt_b200_last_error(NULL, NULL, 0);
+    rt_gemv_q(&R, W, 16, 4096, X, V);
+    codes[k++] = rt_b200_last_error(NULL, NULL, 0);
+    rt_gemm_q(&R, W, 16, 256, X, 16, V);
+    codes[k++] = rt_b200_last_error(NULL, NULL, 0);
+    rt_gemv_go(&R);
+    codes[k++] = rt_b200_last_error(NULL, NULL, 0);
+    rt_gemm(&R, W, 16, 256, X, 2, V);
+    codes[k++] = rt_b200_last_error(NULL, NULL, 0);
+    for (int i = 0; i < k; i++)
+        printf("%d ", codes[i]);
+    printf("| %ld %ld\n", gemv_s_bytes(4096, 4096), (long)sizeof(struct rt));
+    return 0;
+}
+"""
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="no C compiler")
+def test_generated_style_c_code_compiles_and_links(rtb, tmp_path):
+    rtb.load()  # the library is built
+    src = tmp_path / "model_card.c"
+    src.write_text(GENERATED_STYLE_C)
+    exe = tmp_path / "model_card"
+    pkg = os.path.dirname(rtb.LIB_PATH)
+    cc = subprocess.run(["gcc", "-std=gnu11", "-O2", "-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include"),
+                         str(src), "-o", str(exe), f"-L{pkg}", "-l:librt_b200.so", f"-Wl,-rpath,{pkg}"],
+                        capture_output=True, text=True)
+    assert cc.returncode == 0, cc.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0, run.stderr
+    codes, sizes = run.stdout.strip().split("|")
+    assert codes.split() == ["5"] * 6  # RTB_ENOTINIT for every product: nothing reached a device
+    assert sizes.split() == [str(4096 * 4096 * 34 // 32), "40"]
