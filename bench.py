@@ -86,6 +86,18 @@ def cpu_sample_matrices():
     return O, mats
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (/proc/cpuinfo), for the baseline's description."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown CPU"
+
+
 def reference_cpu(steps: int, warmup: int) -> dict:
     """The reference's host implementation (oracle/_ref: its gemv_i_repack + gemv_i_thread over
     the lane-exact host model, team of all host threads pinned to CPUs 0..n-1)."""
@@ -107,7 +119,7 @@ def reference_cpu(steps: int, warmup: int) -> dict:
     return {"value": nbytes / med / 1e9, "unit": "GB/s", "cores": threads, "kind": "reference",
             "sample": f"one decode layer's 5 Q8_0 products (QKV, out, gate, up, down; {nbytes / 1e6:.0f} MB) at M=1, "
                       f"median of {steps} after {warmup} warm-up, the reference's gemv_i_thread on a team of "
-                      f"{threads} pinned threads", "ms_per_sample": med * 1e3}
+                      f"{threads} pinned threads ({cpu_model()})", "ms_per_sample": med * 1e3}
 
 
 # ---------------------------------------------------------------- clocks
