@@ -72,17 +72,23 @@ def tensor_peak() -> tuple[float, str]:
 
 # ---------------------------------------------------------------- the reference's CPU path
 
-def cpu_sample_matrices():
-    """One decode layer's five products (QKV, out, gate, up, down) as GGUF Q8_0 bytes from the
-    seeded CPU generator, plus fp32 x vectors."""
+CPU_LAYERS = 5  # 5 x 214 MB of distinct matrices: larger than a server CPU's L3, so DRAM-bound as the step is
+CPU_MIN_SECONDS = 10.0  # the B200 arm's CPU baseline times at least this much work
+
+
+def cpu_sample_matrices(layers: int = CPU_LAYERS):
+    """`layers` decode layers' five products each (QKV, out, gate, up, down) as GGUF Q8_0 bytes
+    from the seeded CPU generator (distinct matrices per layer), plus fp32 x vectors."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
+    threads = len(os.sched_getaffinity(0))
     mats = []
-    for i, (name, rows, cols) in enumerate([("qkv", WL.QKV, WL.D), ("out", WL.D, WL.D), ("gate", WL.FF, WL.D),
-                                            ("up", WL.FF, WL.D), ("down", WL.D, WL.FF)]):
-        q8 = O.synth_q8_0(rows, cols, SEED, 500 + i)
-        x = O.synth_f32(cols, SEED, 600 + i)
-        mats.append((name, rows, cols, q8, x))
+    for layer in range(layers):
+        for i, (name, rows, cols) in enumerate([("qkv", WL.QKV, WL.D), ("out", WL.D, WL.D), ("gate", WL.FF, WL.D),
+                                                ("up", WL.FF, WL.D), ("down", WL.D, WL.FF)]):
+            q8 = O.synth_q8_0(rows, cols, SEED, 500 + 10 * layer + i, threads=threads)
+            x = O.synth_f32(cols, SEED, 600 + 10 * layer + i)
+            mats.append((name, rows, cols, q8, x))
     return O, mats
 
 
@@ -98,28 +104,36 @@ def cpu_model() -> str:
     return "unknown CPU"
 
 
-def reference_cpu(steps: int, warmup: int) -> dict:
+def reference_cpu(steps: int, warmup: int, min_seconds: float = 0.0) -> dict:
     """The reference's host implementation (oracle/_ref: its gemv_i_repack + gemv_i_thread over
-    the lane-exact host model, team of all host threads pinned to CPUs 0..n-1)."""
+    the lane-exact host model, team of all host threads pinned to CPUs 0..n-1). One sample is one
+    pass over CPU_LAYERS layers' products; at least `steps` samples are timed, and more until
+    `min_seconds` of timed work."""
     O, mats = cpu_sample_matrices()
     if not O.ref_available():
         raise RuntimeError("oracle/_ref/libq8ref.so missing (make -C oracle ref, with the reference tree)")
     threads = len(os.sched_getaffinity(0))
-    refs = [(O.RefMatrix(q8, rows, cols, threads=threads), x, rows, cols) for _, rows, cols, q8, x in mats]
-    nbytes = sum(rows * cols * 34 // 32 + 4 * cols + 4 * rows for _, rows, cols, _, _ in mats)
+    refs = []
+    while mats:  # each GGUF copy is dropped once its form-I copy exists
+        _, rows, cols, q8, x = mats.pop(0)
+        refs.append((O.RefMatrix(q8, rows, cols, threads=threads), x, rows, cols))
+    nbytes = sum(rows * cols * 34 // 32 + 4 * cols + 4 * rows for _, _, rows, cols in refs)
     times = []
-    for k in range(warmup + steps):
+    k = 0
+    while len(times) < steps or sum(times) < min_seconds:
         t0 = time.perf_counter()
         for m, x, rows, cols in refs:
             m.gemv(x)
         dt = time.perf_counter() - t0
         if k >= warmup:
             times.append(dt)
+        k += 1
     med = statistics.median(times)
     return {"value": nbytes / med / 1e9, "unit": "GB/s", "cores": threads, "kind": "reference",
-            "sample": f"one decode layer's 5 Q8_0 products (QKV, out, gate, up, down; {nbytes / 1e6:.0f} MB) at M=1, "
-                      f"median of {steps} after {warmup} warm-up, the reference's gemv_i_thread on a team of "
-                      f"{threads} pinned threads ({cpu_model()})", "ms_per_sample": med * 1e3}
+            "sample": f"{CPU_LAYERS} decode layers' 5 Q8_0 products each (QKV, out, gate, up, down; distinct "
+                      f"matrices, {nbytes / 1e6:.0f} MB, larger than the host's L3) at M=1, median of {len(times)} "
+                      f"samples ({sum(times):.1f} s timed) after {warmup} warm-up, the reference's gemv_i_thread "
+                      f"on a team of {threads} pinned threads ({cpu_model()})", "ms_per_sample": med * 1e3}
 
 
 # ---------------------------------------------------------------- clocks
@@ -547,7 +561,7 @@ def main() -> int:
     cpu = None
     if world == 1 and rank == 0:
         try:
-            cpu = reference_cpu(5, 1)
+            cpu = reference_cpu(5, 1, CPU_MIN_SECONDS)
         except Exception as e:  # noqa: BLE001 -- reported, not fatal: the GPU numbers stand alone
             log("cpu baseline unavailable:", e)
     if rank == 0:

@@ -90,10 +90,22 @@ def gguf_bytes(rows: int, cols: int) -> int:
     return rows * (cols // 32) * 34
 
 
-def synth_q8_0(rows: int, cols: int, seed: int, stream: int, sigma: float = 0.02, row0: int = 0) -> np.ndarray:
-    """Rows [row0, row0+rows) of a seeded synthetic Q8_0 matrix, GGUF layout (uint8)."""
+def synth_q8_0(rows: int, cols: int, seed: int, stream: int, sigma: float = 0.02, row0: int = 0,
+               threads: int = 1) -> np.ndarray:
+    """Rows [row0, row0+rows) of a seeded synthetic Q8_0 matrix, GGUF layout (uint8). With
+    threads > 1 the rows are filled in ranges on host threads (the C fill runs without the GIL);
+    every value depends only on its own index, so the bytes are the same."""
     out = np.empty(gguf_bytes(rows, cols), dtype=np.uint8)
-    port().q8o_fill_q8_0(out, row0, rows, cols, seed, stream, sigma)
+    rb = gguf_bytes(1, cols)
+    n = max(1, min(threads, rows))
+    if n == 1:
+        port().q8o_fill_q8_0(out, row0, rows, cols, seed, stream, sigma)
+        return out
+    from concurrent.futures import ThreadPoolExecutor
+    cuts = [rows * k // n for k in range(n + 1)]
+    with ThreadPoolExecutor(n) as pool:
+        list(pool.map(lambda k: port().q8o_fill_q8_0(out[cuts[k] * rb:cuts[k + 1] * rb], row0 + cuts[k],
+                                                     cuts[k + 1] - cuts[k], cols, seed, stream, sigma), range(n)))
     return out
 
 

@@ -103,6 +103,13 @@ def test_split_layout_round_trip(oracle):
         assert np.array_equal(r1[cols:cols + 2], blk[:2])
 
 
+def test_threaded_generator_is_the_same_matrix(oracle):
+    """The bench's CPU baseline fills its matrices on host threads: the same bytes, any split."""
+    a = oracle.synth_q8_0(37, 4096, 5, 9, row0=3)
+    for threads in (2, 5, 64):
+        assert np.array_equal(oracle.synth_q8_0(37, 4096, 5, 9, row0=3, threads=threads), a)
+
+
 def test_generator_distribution(oracle):
     x = oracle.synth_f32(200000, 3, 4)
     assert abs(x.mean()) < 0.01 and abs(x.std() - 1.0) < 0.01
