@@ -74,14 +74,15 @@ constexpr int A_COLS = BK / 2;
 //     (5 of them for tiles of <= 32 tokens, else 4). Two CTAs share an SM and
 //     its tensor core: at N <= 64 an MMA instruction takes ~46 cycles while each wait in the
 //     issuing thread stalls it ~200, so a second issuer keeps the pipe fed.
+constexpr int MAX_BN_TWO_CTAS = 64; // the two-CTA shape's tiles: two accumulators of up to 64 columns
+
 template <int CPS>
 struct TcShape {
     static constexpr int EPQ = CPS == 1 ? 4 : 1; // epilogue warps per TMEM lane quarter
     static constexpr int NDQ = 8 / CPS, EPI_WARPS = 4 * EPQ;
     static constexpr int DQ_WARP0 = 4, TMA_WARP = DQ_WARP0 + NDQ, MMA_WARP = TMA_WARP + 1;
     static constexpr int NT = 32 * (MMA_WARP + 1 + EPI_WARPS - 4); // epilogue: warps 0-3 (+ after MMA_WARP)
-    static constexpr int TMEM_COLS = 512 / CPS, ACC_COLS = 256 / CPS, A_BASE = ACC_COLS;
-    static constexpr int MAX_BN_SHAPE = CPS == 1 ? 256 : 64; // two accumulators of up to 64 columns
+    static constexpr int TMEM_COLS = 512 / CPS, ACC_COLS = 256 / CPS;
     static constexpr int BLOCKS_PER_THREAD = 2 / (NDQ / 4); // 32-column blocks per dequant thread per stage
 };
 // Shared memory per stage (1024-aligned): the quant box (128 rows x 64 B, 64B swizzle), the scale
@@ -561,7 +562,7 @@ namespace {
 
 // Tokens per tile: the largest t split into passes of <= MAX_BN, rounded up to 16.
 // CTAs per SM for a tile of bn tokens: two issuers per tensor core up to 64 tokens.
-int cps_of(int bn) { return bn <= TcShape<2>::MAX_BN_SHAPE ? 2 : 1; }
+int cps_of(int bn) { return bn <= MAX_BN_TWO_CTAS ? 2 : 1; }
 
 int choose_bn(const GemmJob *jobs, int n) {
     int tmax = 0;
@@ -686,7 +687,7 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
     // on a 32-column boundary: two CTAs per SM with tiles of <= 32 tokens fit a fifth stage
     const int acc_stride = (cps == 1 ? TcShape<1>::ACC_COLS : TcShape<2>::ACC_COLS) / n_acc(bn, cps);
     const int acc_end = (n_acc(bn, cps) - 1) * acc_stride + bn;
-    p.a_base = cps == 1 ? TcShape<1>::A_BASE : (acc_end + A_COLS - 1) / A_COLS * A_COLS;
+    p.a_base = cps == 1 ? TcShape<1>::ACC_COLS : (acc_end + A_COLS - 1) / A_COLS * A_COLS;
     const int tmem_cols = cps == 1 ? TcShape<1>::TMEM_COLS : TcShape<2>::TMEM_COLS;
     int max_s = (tmem_cols - p.a_base) / A_COLS;
     max_s = max_s < MAX_STAGES ? max_s : MAX_STAGES;
