@@ -188,6 +188,13 @@ RTB_API int rt_b200_nccl_id(void *out128);
 RTB_API int rt_b200_shard(struct rt *R, int rank, int world, const void *nccl_id);
 RTB_API int rt_b200_peer_gather(struct rt *R);
 
+/* A self-test of the failure path: one kernel on R's stream waits, bounded, on a device counter
+ * that nothing advances and then on an mbarrier that nothing arrives on, the two kinds of wait the
+ * product kernels make. Each gives up after about a second and reports through the error word, as
+ * a stuck wait in a product does. Returns RTB_EKERNEL (also recorded for rt_b200_last_error, whose
+ * message names both waits) after about two seconds; R stays usable. No GPU fault is involved. */
+RTB_API int rt_b200_wait_probe(struct rt *R);
+
 /* ---------------------------------------------------------------- chains: rounds in one launch
  * Between rt_b200_chain_begin and rt_b200_chain_end, products (rt_gemv, rt_gemm, rt_gemm_silu,
  * rt_gemv_rows) and queued rounds (rt_gemv_go) are recorded, not run: each call or go is one round.

@@ -221,6 +221,20 @@ __device__ __noinline__ bool wait_count(const unsigned *ctr, unsigned target) {
     }
 }
 
+// The failure path's self-test: one thread waits on a device counter that nothing advances, then
+// on an mbarrier that nothing arrives on. Each wait gives up after WAIT_LIMIT_CYCLES (about a
+// second) and reports its bit, as a stuck wait in a product kernel does; the kernel then returns.
+__global__ void wait_probe_kernel(const unsigned *ctr, unsigned *err) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x != 0)
+        return;
+    if (!wait_count(ctr, 1u))
+        report(err, ERR_TIMEOUT_ROUND);
+    mbar_init(&bar, 1);
+    if (!mbar_wait(&bar, 0))
+        report(err, ERR_TIMEOUT_FULL);
+}
+
 template <int MT, int CTAS, class P>
 __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(const __grid_constant__ P p) {
     using C = Cfg<MT, CTAS>;
@@ -629,6 +643,13 @@ cudaError_t launch_gemv(GemvParams &p, int num_sms, int grid_limit, cudaStream_t
     case 3: return launch_mt<3, 1>(p, num_sms, grid_limit, stream, pdl);
     default: return launch_mt<4, 1>(p, num_sms, grid_limit, stream, pdl);
     }
+}
+
+cudaError_t launch_wait_probe(const unsigned *ctr, unsigned *err, cudaStream_t stream) {
+    if (!ctr || !err)
+        return cudaErrorInvalidValue;
+    wait_probe_kernel<<<1, 32, 0, stream>>>(ctr, err);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_gemv_chain(ChainParams &p, int num_sms, cudaStream_t stream) {

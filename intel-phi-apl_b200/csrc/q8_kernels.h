@@ -78,6 +78,8 @@ constexpr int MAX_CHAIN_JOBS = 160;
 using ChainParams = GemvParamsT<MAX_CHAIN_JOBS>;
 // Fills the tile fields (the done/wait fields are the caller's). One CTA shape for the chain.
 cudaError_t launch_gemv_chain(ChainParams &p, int num_sms, cudaStream_t stream);
+// The bounded waits' self-test (rt_b200_wait_probe): *ctr must be 0 and stay 0.
+cudaError_t launch_wait_probe(const unsigned *ctr, unsigned *err, cudaStream_t stream);
 
 // After a peer-gathered launch: wait for every peer's flag of this round, then copy their rows
 // of y ([t][ldy], ldy = rows_total) from the staging image.

@@ -960,6 +960,21 @@ int rt_b200_chain_end(struct rt *R, int serial) {
     return ok ? RTB_OK : (c->status != RTB_OK ? c->status : RTB_ECUDA);
 }
 
+int rt_b200_wait_probe(struct rt *R) {
+    Ctx *c = ctx_of(R);
+    if (!c)
+        return RTB_ENOTINIT;
+    unsigned *ctr = nullptr; // a counter that nothing advances
+    if (!cuda_ok(c, cudaMalloc(&ctr, sizeof(unsigned)), "wait probe"))
+        return c->status;
+    if (cuda_ok(c, cudaMemsetAsync(ctr, 0, sizeof(unsigned), c->stream), "wait probe") &&
+        cuda_ok(c, q8::launch_wait_probe(ctr, c->d_err, c->stream), "wait probe launch"))
+        read_error_word(c); // waits for the kernel: RTB_EKERNEL with the two waits' bits
+    cudaStreamSynchronize(c->stream);
+    cudaFree(ctr);
+    return c->status;
+}
+
 int rt_b200_peer_gather(struct rt *R) {
     Ctx *c = ctx_of(R);
     return c && c->peer_ok ? 1 : 0;

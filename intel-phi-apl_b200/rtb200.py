@@ -28,7 +28,7 @@ EXPORTS = ("rt_init", "rt_gemv", "rt_gemv_q", "rt_gemv_open", "rt_gemv_go", "rt_
            "rt_b200_last_error", "rt_b200_set_overlap", "rt_b200_set_async", "rt_b200_sync", "rt_b200_stream", "rt_b200_set_stream",
            "rt_b200_free", "rt_b200_nccl_id", "rt_b200_shard", "rt_b200_peer_gather", "rt_b200_chain_begin",
            "rt_b200_chain_end", "rtb_gguf_info", "rt_b200_load_gguf", "rtb_load_error", "rtb_synth_q8_0",
-           "rtb_synth_f32", "rt_gemm_static", "rt_b200_pull", "rt_b200_push")
+           "rtb_synth_f32", "rt_gemm_static", "rt_b200_pull", "rt_b200_push", "rt_b200_wait_probe")
 
 
 class RtError(RuntimeError):
@@ -97,6 +97,7 @@ def load() -> C.CDLL:
         "rt_b200_nccl_id": ([_P], C.c_int),
         "rt_b200_shard": ([R, C.c_int, C.c_int, _P], C.c_int),
         "rt_b200_peer_gather": ([R], C.c_int),
+        "rt_b200_wait_probe": ([R], C.c_int),
         "rt_b200_chain_begin": ([R], C.c_int),
         "rt_b200_chain_end": ([R, C.c_int], C.c_int),
         "rtb_gguf_info": ([C.c_char_p, C.POINTER(Tensor), C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_ulonglong)],
@@ -318,3 +319,9 @@ class Runtime:
     def peer_gather(self) -> bool:
         """True when single products gather y in their own kernel (else through NCCL)."""
         return bool(self.lib.rt_b200_peer_gather(self._ref))
+
+    def wait_probe(self) -> tuple[int, str]:
+        """The failure path's self-test: a kernel whose two bounded waits never complete. Returns
+        the library's code (RTB_EKERNEL expected) and the recorded message, which it clears."""
+        code = self.lib.rt_b200_wait_probe(self._ref)
+        return code, last_error(self)[1]

@@ -58,6 +58,8 @@ def test_calls_without_init_record_an_error(rtb):
     code, msg = rtb.last_error(None)
     assert code == 5 and "rt_init" in msg
     assert rtb.last_error(None)[0] == 0  # reading clears
+    assert lib.rt_b200_wait_probe(C.byref(R)) == 5  # the failure self-test needs rt_init too
+    assert rtb.last_error(None)[0] == 5
 
 
 # A C translation unit shaped like the engine's generated model code (a struct rt on the stack,
