@@ -147,7 +147,11 @@ bool parse(const char *path, Table *tab) {
         return false;
     }
     struct stat st;
-    fstat(fileno(r.f), &st);
+    if (fstat(fileno(r.f), &st) != 0 || st.st_size < 0) {
+        tab->err = std::string(path) + ": " + strerror(errno);
+        fclose(r.f);
+        return false;
+    }
     tab->file_bytes = uint64_t(st.st_size);
     char magic[4] = {0};
     r.get(magic, 4);
