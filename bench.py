@@ -25,7 +25,14 @@ roofline of the gemv kernel on the output head; the reference's own CPU implemen
 
 --impl reference: the reference's CPU implementation of the product (its host-model gemv_i_thread
 built from its sources, oracle/_ref) on all host cores, same metric and unit, each step a bounded
-sample (one decode layer's five products). Rank 0 only.
+sample (five decode layers' five products each). Rank 0 only.
+
+Two single-purpose modes, for profiler captures and the loader (one JSON line each, 1 GPU):
+
+    python bench.py --probe SHAPE [--t T] [--launches N]   one product kernel on a BASELINE shape
+        (gate_up_silu, down, qkv, out, head, draft_head) through the C ABI, N timed launches
+    python bench.py --load [--load-layers L] [--dir DIR]    rt_b200_load_gguf on a synthetic GGUF of
+        L decode layers plus the head (written to DIR, then removed)
 """
 from __future__ import annotations
 
@@ -47,6 +54,7 @@ SEED = 20261201
 METRIC = "Q8_0 weight-product GB/s, 9B decode step (M=1)"
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 TRAFFIC_PATH = os.path.join(ROOT, "profiles", "gemv_exact_head_151936x4096.md")
+STEP_TRAFFIC_PATH = os.path.join(ROOT, "profiles", "launches_bench_decode_step_m1.md")
 
 
 def log(*a):
@@ -302,15 +310,19 @@ class Bench:
         res = {"ms1": ms1, "ms2": ms2, "launches": args.steps * (n1 + n2), "clocks": clk}
         del g1, g2  # graphs holding NCCL work go before the process group
         torch.cuda.synchronize()
-        res["roofline"] = self.roofline(args.steps)
+        res["head_launch"] = self.head_launch(args.steps)
         res["e2e"] = self.e2e(max(3, min(args.steps, 10)), args.warmup)
         if self.world == 1 and self.rank == 0:
+            clocks = ClockSampler([0])
             res["sweep"] = self.sweep()
+            res["sweep"]["clocks"] = clocks.stop()
             if not self.args.no_prompt:
+                clocks = ClockSampler([0])
                 res["prompt"] = self.prompt()
+                res["prompt"]["clocks"] = clocks.stop()
         return res
 
-    def roofline(self, steps: int) -> dict:
+    def head_launch(self, steps: int) -> dict:
         """The gemv kernel alone on the output head (this rank's shard, 661 MB at N=1: larger
         than L2), each launch timed with CUDA events on its stream."""
         torch = self.torch
@@ -344,66 +356,73 @@ class Bench:
         except (OSError, ValueError):
             pass
         achieved = nbytes / dur / 1e9
-        return {"kernel": "gemv_exact_kernel<1>", "shape": f"{n}x{WL.D} M=1 (output head shard)", "bound": "hbm",
+        return {"kernel": "gemv_exact_kernel<1>", "shape": f"{n}x{WL.D} M=1 (output head shard)",
                 "achieved": round(achieved, 1), "peak": peak, "peak_kind": how, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": traffic, "algorithmic_bytes": nbytes,
                 "us_per_launch": round(dur * 1e6, 2)}
 
     def e2e(self, steps: int, warmup: int) -> dict:
         """The reference-facing path with host buffers, one round at a time as the reference engine
-        runs them: per round x goes host->device from pinned memory (rt_b200_pull, the engine's
-        link_pull), the product is enqueued through the C ABI, and y comes back device->host
-        (rt_b200_push, the engine's link_push), which returns once y is on the host."""
+        runs them, driven from C (intel-phi-apl_b200/engine_rounds.c, eng_run_rounds) against the C
+        ABI: per round the product is queued (rt_gemv_q / rt_gemm_silu_q), the round is opened
+        (rt_gemv_open: its kernel is launched and streams its weights while x is still on the
+        host), x goes host->device from pinned memory (rt_b200_pull, the engine's link_pull), the
+        round runs (rt_gemv_go) and y comes back device->host (rt_b200_push, the engine's
+        link_push), which returns once y is on the host. Wall-clock time of whole steps, after
+        `warmup` steps. Also timed: the same rounds without rt_gemv_open."""
+        import ctypes as C
         torch, rt = self.torch, self.rt
         rt.set_async(True)
         rt.set_stream(torch.cuda.current_stream().cuda_stream)
         hx = {k: v.cpu().pin_memory() for k, v in self.x.items() if k[1] == 1}
         hy = {k: torch.empty(v.numel(), dtype=torch.float32).pin_memory() for k, v in self.y.items() if k[1] == 1}
         xd, xf = self.x[("d", 1)], self.x[("ff", 1)]
-
-        # Every round as a C engine makes it: three C-ABI calls with their arguments bound once
-        # (pull x, the product, push y), push's return code carrying any error of the round.
-        lib, ref = rt.lib, rt._ref
         y = self.y
-        rounds = []
 
-        def add(name_x, xdev, fn, args, name_y):
-            nx, ny = xdev.numel() * 4, y[(name_y, 1)].numel() * 4
-            rounds.append(((ref, xdev.data_ptr(), hx[(name_x, 1)].data_ptr(), nx), fn, (ref,) + args,
-                           (ref, hy[(name_y, 1)].data_ptr(), y[(name_y, 1)].data_ptr(), ny)))
+        class Round(C.Structure):
+            _fields_ = [("kind", C.c_int), ("open", C.c_int), ("w", C.c_void_p), ("w2", C.c_void_p),
+                        ("rows", C.c_long), ("cols", C.c_long), ("t", C.c_long), ("x_dev", C.c_void_p),
+                        ("x_host", C.c_void_p), ("x_bytes", C.c_size_t), ("y_dev", C.c_void_p),
+                        ("y_host", C.c_void_p), ("y_bytes", C.c_size_t)]
 
+        spec = []
         for L in self.w:
-            add("d", xd, lib.rt_gemv, (L["qkv"].data_ptr(), WL.QKV, WL.D, xd.data_ptr(), y[("qkv", 1)].data_ptr()), "qkv")
-            add("d", xd, lib.rt_gemv, (L["out"].data_ptr(), WL.D, WL.D, xd.data_ptr(), y[("out", 1)].data_ptr()), "out")
-            add("d", xd, lib.rt_gemm_silu, (L["gate"].data_ptr(), L["up"].data_ptr(), WL.FF, WL.D, xd.data_ptr(), 1,
-                                            y[("h", 1)].data_ptr()), "h")
-            add("ff", xf, lib.rt_gemv, (L["down"].data_ptr(), WL.D, WL.FF, xf.data_ptr(), y[("down", 1)].data_ptr()), "down")
-        add("d", xd, lib.rt_gemv, (self.head.data_ptr(), WL.VOCAB, WL.D, xd.data_ptr(), y[("head", 1)].data_ptr()), "head")
-        h2d = sum(r[0][3] for r in rounds)
-        d2h = sum(r[3][3] for r in rounds)
-        pull, push = lib.rt_b200_pull, lib.rt_b200_push
+            spec += [(0, L["qkv"], None, WL.QKV, WL.D, "d", "qkv"), (0, L["out"], None, WL.D, WL.D, "d", "out"),
+                     (1, L["gate"], L["up"], WL.FF, WL.D, "d", "h"), (0, L["down"], None, WL.D, WL.FF, "ff", "down")]
+        spec.append((0, self.head, None, WL.VOCAB, WL.D, "d", "head"))
+        rounds = (Round * len(spec))()
+        for i, (kind, w, w2, rows, cols, nx, ny) in enumerate(spec):
+            xdev = xd if nx == "d" else xf
+            rounds[i] = Round(kind, 1, w.data_ptr(), w2.data_ptr() if w2 is not None else None, rows, cols, 1,
+                              xdev.data_ptr(), hx[(nx, 1)].data_ptr(), xdev.numel() * 4, y[(ny, 1)].data_ptr(),
+                              hy[(ny, 1)].data_ptr(), y[(ny, 1)].numel() * 4)
+        h2d = sum(r.x_bytes for r in rounds)
+        d2h = sum(r.y_bytes for r in rounds)
+        eng = C.CDLL(os.path.join(PKG, "libengine_rounds.so"))
+        eng.eng_run_rounds.argtypes = [C.POINTER(self.rtb.StructRt), C.POINTER(Round), C.c_int, C.c_int]
+        eng.eng_run_rounds.restype = C.c_int
 
-        def one_step():
-            for pa, fn, fa, qa in rounds:
-                pull(*pa)
-                fn(*fa)
-                if push(*qa):
-                    rt.sync()  # raises with the runtime's message
+        def timed(n: int) -> float:
+            if eng.eng_run_rounds(rt._ref, rounds, len(spec), warmup):
+                rt.sync()  # raises with the runtime's message
+            self.barrier()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            if eng.eng_run_rounds(rt._ref, rounds, len(spec), n):
+                rt.sync()
+            torch.cuda.synchronize()
+            return self.max_over_ranks((time.perf_counter() - t0) / n)
 
-        for _ in range(warmup):
-            one_step()
-        self.barrier()
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        for _ in range(steps):
-            one_step()
-        torch.cuda.synchronize()
-        dt = self.max_over_ranks((time.perf_counter() - t0) / steps)
+        dt = timed(steps)
+        for r in rounds:
+            r.open = 0
+        dt_plain = timed(steps)
         total = WL.step_bytes(1, self.layers)
         return {"value": round(total / dt / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": round(dt * 1e3, 3),
-                "tok_s": round(1.0 / dt, 1),
-                "path": "per round: rt_b200_pull of x, rt_gemv / rt_gemm_silu, rt_b200_push of y (pinned host buffers)"}
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(dt * 1e3, 3), "tok_s": round(1.0 / dt, 1),
+                "path": "per round, from C (engine_rounds.c): rt_gemv_q / rt_gemm_silu_q, rt_gemv_open, rt_b200_pull "
+                        "of x, rt_gemv_go, rt_b200_push of y (pinned host buffers)",
+                "without_open": {"ms_per_step": round(dt_plain * 1e3, 3), "value": round(total / dt_plain / 1e9, 1)}}
 
     def _graph(self, fns):
         """The calls captured as one CUDA graph on a side stream (the runtime follows the stream)."""
@@ -485,36 +504,194 @@ class Bench:
         return out
 
     def sweep(self) -> dict:
-        """each decode shape alone, GB/s. The 32 layer copies of a shape run
-        back to back as one CUDA graph (1.1-3.4 GB: larger than L2); the head is one 661 MB matrix,
-        8 launches per graph."""
+        """BASELINE configs 2 and 3: each decode shape alone at M = 1 and at M = 2 (the verify pass),
+        GB/s. The 32 layer copies of a shape run back to back as one CUDA graph (1.1-3.4 GB: larger
+        than L2); the head is one 661 MB matrix, 8 launches per graph. Config 3's draft-head gather
+        (32,768 of the head's 151,936 rows, 142.6 MB) rotates over four disjoint seeded row sets,
+        8 launches per graph, so consecutive launches read different rows."""
+        import numpy as np
         torch, rt = self.torch, self.rt
         rt.set_async(True)
         rt.set_stream(torch.cuda.current_stream().cuda_stream)
+        hpeak, _ = peaks()
         out = {}
-        xd, xf = self.x[("d", 1)].data_ptr(), self.x[("ff", 1)].data_ptr()
         y = self.y
-        calls = {
-            "gate_up_silu": lambda L: rt.gemm_silu(L["gate"].data_ptr(), L["up"].data_ptr(), WL.FF, WL.D, xd, 1, y[("h", 1)].data_ptr()),
-            "down": lambda L: rt.gemv(L["down"].data_ptr(), WL.D, WL.FF, xf, y[("down", 1)].data_ptr()),
-            "qkv": lambda L: rt.gemv(L["qkv"].data_ptr(), WL.QKV, WL.D, xd, y[("qkv", 1)].data_ptr()),
-            "out": lambda L: rt.gemv(L["out"].data_ptr(), WL.D, WL.D, xd, y[("out", 1)].data_ptr()),
-        }
-        for p in WL.SWEEP:
-            if p.name == "head":
-                fn = [lambda: rt.gemv(self.head.data_ptr(), WL.VOCAB, WL.D, xd, y[("head", 1)].data_ptr())] * 8
-            else:
-                fn = [(lambda L=L: calls[p.name](L)) for L in self.w]
-            for f in fn:  # eager once (kernel attributes), then the launches as one CUDA graph
+
+        def run(fns, reps=3):
+            for f in fns:  # eager once (kernel attributes), then the launches as one CUDA graph
                 f()
             torch.cuda.synchronize()
-            g = self._graph(fn)
-            us = self._time_graph(g, 3) * 1e3 / len(fn)
+            g = self._graph(fns)
+            us = self._time_graph(g, reps) * 1e3 / len(fns)
             del g
-            out[p.name] = {"shape": f"{p.rows}x{p.cols}" + (" x2 +silu" if p.kind == "silu" else ""),
-                           "us": round(us, 2), "GB_s": round(p.bytes(1) / us / 1e3, 1)}
+            return us
+
+        for m in (1, 2):
+            xd, xf = self.x[("d", m)].data_ptr(), self.x[("ff", m)].data_ptr()
+            calls = {
+                "gate_up_silu": lambda L: rt.gemm_silu(L["gate"].data_ptr(), L["up"].data_ptr(), WL.FF, WL.D, xd, m,
+                                                       y[("h", m)].data_ptr()),
+                "down": lambda L: rt.gemm(L["down"].data_ptr(), WL.D, WL.FF, xf, m, y[("down", m)].data_ptr()),
+                "qkv": lambda L: rt.gemm(L["qkv"].data_ptr(), WL.QKV, WL.D, xd, m, y[("qkv", m)].data_ptr()),
+                "out": lambda L: rt.gemm(L["out"].data_ptr(), WL.D, WL.D, xd, m, y[("out", m)].data_ptr()),
+            }
+            row = {}
+            for p in WL.SWEEP:
+                if p.name == "head":
+                    fns = [lambda: rt.gemm(self.head.data_ptr(), WL.VOCAB, WL.D, xd, m, y[("head", m)].data_ptr())] * 8
+                else:
+                    fns = [(lambda L=L, p=p: calls[p.name](L)) for L in self.w]
+                us = run(fns)
+                row[p.name] = {"shape": f"{p.rows}x{p.cols}" + (" x2 +silu" if p.kind == "silu" else ""),
+                               "us": round(us, 2), "GB_s": round(p.bytes(m) / us / 1e3, 1),
+                               "hbm_frac": round(p.bytes(m) / us / 1e3 / hpeak, 3)}
+            out[f"m{m}"] = row
+        # config 3: the draft head's gather (M = 1)
+        perm = np.random.default_rng(SEED).permutation(WL.VOCAB).astype(np.int32)
+        sets = [torch.from_numpy(perm[k * WL.HOT:(k + 1) * WL.HOT].copy()).cuda() for k in range(4)]
+        yd = torch.empty(WL.HOT, dtype=torch.float32, device="cuda")
+        xd = self.x[("d", 1)].data_ptr()
+        fns = [(lambda k=k: rt.gemv_rows(self.head.data_ptr(), WL.VOCAB, sets[k % 4].data_ptr(), WL.HOT, WL.D, xd,
+                                         yd.data_ptr())) for k in range(8)]
+        us = run(fns)
+        p = WL.DRAFT
+        out["draft_head_gather"] = {"shape": f"{WL.HOT} of {WL.VOCAB} rows x{WL.D}", "us": round(us, 2),
+                                    "GB_s": round(p.bytes(1) / us / 1e3, 1),
+                                    "hbm_frac": round(p.bytes(1) / us / 1e3 / hpeak, 3)}
         rt.sync()
         return out
+
+
+# ---------------------------------------------------------------- single-purpose modes
+
+def probe(args) -> None:
+    """One product kernel on a BASELINE shape through the C ABI, `args.launches` launches each
+    timed with CUDA events after one warm-up launch: for profiler captures and quick timing.
+    Prints the mean time per launch and one launch's algorithmic bytes and flops."""
+    import numpy as np
+    import torch
+
+    import rtb200
+    p = WL.DRAFT if args.probe == "draft_head" else next(q for q in WL.SWEEP if q.name == args.probe)
+    t = args.t
+    rt = rtb200.Runtime()
+    rt.set_async(True)
+    rt.set_stream(torch.cuda.current_stream().cuda_stream)
+    nb = rtb200.gemv_s_bytes(p.rows, p.cols)
+    w = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    rtb200.synth_q8_0(w.data_ptr(), 0, p.rows, p.cols, 1, 1)
+    w2 = None
+    if p.kind == "silu":
+        w2 = torch.empty(nb, dtype=torch.uint8, device="cuda")
+        rtb200.synth_q8_0(w2.data_ptr(), 0, p.rows, p.cols, 1, 2)
+    x = torch.empty(t * p.cols, dtype=torch.float32, device="cuda")
+    rtb200.synth_f32(x.data_ptr(), t * p.cols, 1, 3)
+    nout = p.nsel if p.kind == "rows" else p.rows
+    y = torch.empty(t * nout, dtype=torch.float32, device="cuda")
+    idx = None
+    if p.kind == "rows":
+        idx = torch.from_numpy(np.random.default_rng(1).choice(p.rows, p.nsel, replace=False).astype(np.int32)).cuda()
+
+    def launch():
+        if p.kind == "silu":
+            rt.gemm_silu(w.data_ptr(), w2.data_ptr(), p.rows, p.cols, x.data_ptr(), t, y.data_ptr())
+        elif p.kind == "rows":
+            rt.gemv_rows(w.data_ptr(), p.rows, idx.data_ptr(), p.nsel, p.cols, x.data_ptr(), y.data_ptr())
+        else:
+            rt.gemm(w.data_ptr(), p.rows, p.cols, x.data_ptr(), t, y.data_ptr())
+
+    launch()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.launches)]
+    for e0, e1 in ev:
+        e0.record()
+        launch()
+        e1.record()
+    torch.cuda.synchronize()
+    rt.sync()
+    us = sum(e0.elapsed_time(e1) for e0, e1 in ev) / len(ev) * 1e3
+    print(json.dumps({"probe": p.name, "rows": p.rows, "cols": p.cols, "t": t, "us_per_launch": round(us, 2),
+                      "bytes": p.bytes(t), "flops": p.flops(t), "GB_s": round(p.bytes(t) / us / 1e3, 1)}), flush=True)
+    rt.close()
+
+
+def load_probe(args) -> None:
+    """rt_b200_load_gguf on a synthetic GGUF of `args.load_layers` decode layers (QKV, out, gate, up,
+    down; Q8_0 with random quants and fp16 scales) plus the 151936 x 4096 head: O_DIRECT reads into
+    pinned buffers, copies overlapping the reads, the file's sum and the in-place repacks on the
+    GPU. The reference measures its own load at 3.05-3.29 GB/s for the transfer and 9.27 GB/s for
+    the repack (its docs/measurements.md). The GGUF writer is the tests' (tests/gguf_synth.py)."""
+    import numpy as np
+    import torch
+
+    import rtb200
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import gguf_synth as G
+
+    def q8_bytes(rows: int, cols: int, rng) -> bytes:
+        blocks = rows * cols // 32
+        raw = np.empty((blocks, 34), dtype=np.uint8)
+        raw[:, 2:] = rng.integers(0, 256, size=(blocks, 32), dtype=np.uint8)
+        d = (rng.random(blocks, dtype=np.float32) * 1e-3 + 1e-4).astype(np.float16)
+        raw[:, :2] = d.view(np.uint8).reshape(blocks, 2)
+        return raw.tobytes()
+
+    rng = np.random.default_rng(1)
+    tensors = []
+    for L in range(args.load_layers):
+        for name, rows, cols in (("attn_qkv", WL.QKV, WL.D), ("attn_output", WL.D, WL.D), ("ffn_gate", WL.FF, WL.D),
+                                 ("ffn_up", WL.FF, WL.D), ("ffn_down", WL.D, WL.FF)):
+            tensors.append((f"blk.{L}.{name}.weight", G.GGML_Q8_0, [cols, rows], q8_bytes(rows, cols, rng)))
+    tensors.append(("output.weight", G.GGML_Q8_0, [WL.D, WL.VOCAB], q8_bytes(WL.VOCAB, WL.D, rng)))
+    path = os.path.join(args.dir, "rtb_load_probe.gguf")
+    G.write_gguf(path, tensors, kv={"general.architecture": "qwen35"})
+    size = os.path.getsize(path)
+    arena = torch.empty((size + 4095) // 4096 * 4096, dtype=torch.uint8, device="cuda")
+    with rtb200.Runtime() as rt:
+        rt.load_gguf(path, arena.data_ptr(), arena.numel())  # warm-up (driver, pinned buffers)
+        table, st = rt.load_gguf(path, arena.data_ptr(), arena.numel())
+    ok = st["file_sum"] == G.file_sum(path)
+    os.remove(path)
+    print(json.dumps({"file_bytes": size, "seconds": round(st["seconds"], 4), "GB_s": round(size / st["seconds"] / 1e9, 2),
+                      "repack_seconds": round(st["seconds_repack"], 5),
+                      "repack_GB_s": round(size / st["seconds_repack"] / 1e9, 1) if st["seconds_repack"] else None,
+                      "o_direct": bool(st["direct"]), "q8_matrices": st["q8_matrices"], "sum_ok": ok,
+                      "tensors": len(table)}), flush=True)
+
+
+def profile_figure(path: str, key: str):
+    """An integer `key: value` line of a committed profile summary, or None."""
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith(key + ":"):
+                    return int(line.split(":", 1)[1].split()[0])
+    except (OSError, ValueError, IndexError):
+        pass
+    return None
+
+
+def step_roofline(total: int, ms1: float, world: int, res: dict, layers: int = WL.LAYERS) -> dict:
+    """The roofline of the decode step, the metric's own workload: its 129 gemv_exact_kernel
+    launches (each rank streams its row shard) against one GPU's measured HBM copy bandwidth.
+    achieved = the step's algorithmic bytes per GPU / the step time. traffic = ncu DRAM read+write
+    bytes of one step's launches (profiles/launches_bench_decode_step_m1.md, 1 GPU), per step.
+    per_shape (1 GPU): each shape's launch alone (the sweep's graph of 32 copies), its fraction of
+    the peak and its share of the step (launches per step x time / step time)."""
+    peak, how = peaks()
+    achieved = total / world / (ms1 * 1e6)
+    out = {"kernel": "gemv_exact_kernel (the decode step's 129 launches, graph-replayed)", "bound": "hbm",
+           "achieved": round(achieved, 1), "peak": peak, "peak_kind": how, "unit": "GB/s",
+           "frac": round(achieved / peak, 4),
+           "traffic": profile_figure(STEP_TRAFFIC_PATH, "traffic_bytes_per_step") if world == 1 else None,
+           "algorithmic_bytes": total // world, "us_per_launch": round(ms1 * 1e3 / len(WL.step_rounds(layers)), 2)}
+    sw = res.get("sweep", {}).get("m1")
+    if sw:
+        counts = {p.name: sum(1 for q in WL.step_rounds(layers) if q.name == p.name) for p in WL.SWEEP}
+        out["per_shape"] = {k: {"us": v["us"], "GB_s": v["GB_s"], "frac": v["hbm_frac"],
+                                "share_of_step": round(counts[k] * v["us"] / (ms1 * 1e3), 3)} for k, v in sw.items()}
+    out["head_launch"] = res["head_launch"]
+    return out
 
 
 def main() -> int:
@@ -525,7 +702,20 @@ def main() -> int:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--layers", type=int, default=WL.LAYERS)
     ap.add_argument("--no-prompt", action="store_true", help="skip the config-4 prompt gemm section")
+    ap.add_argument("--probe", choices=[p.name for p in WL.SWEEP] + ["draft_head"],
+                    help="time one product kernel on this BASELINE shape (profiler captures)")
+    ap.add_argument("--t", type=int, default=1, help="--probe: tokens")
+    ap.add_argument("--launches", type=int, default=3, help="--probe: timed launches")
+    ap.add_argument("--load", action="store_true", help="time the weight loader on a synthetic GGUF file")
+    ap.add_argument("--load-layers", type=int, default=4, help="--load: decode layers in the file")
+    ap.add_argument("--dir", default="/tmp", help="--load: where the file is written")
     args = ap.parse_args()
+    if args.probe:
+        probe(args)
+        return 0
+    if args.load:
+        load_probe(args)
+        return 0
     args.warmup = max(3, args.warmup)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -539,7 +729,8 @@ def main() -> int:
                 "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": round(cpu["ms_per_sample"], 3), "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Q8_0, w ~ 0.02*N(0,1), x ~ N(0,1))",
-                "config": {"workload": "BASELINE config 5 sample: one 9B-class decode layer's weight products, M=1",
+                "config": {"workload": f"BASELINE config 5 sample: {CPU_LAYERS} 9B-class decode layers' weight "
+                                       f"products (QKV, out, gate, up, down; distinct matrices), M=1",
                            "parallelism": "host threads"},
                 "cpu_baseline": {**{k: cpu[k] for k in ("unit", "cores", "kind", "sample")},
                                  "value": round(cpu["value"], 3)},
@@ -579,7 +770,7 @@ def main() -> int:
             "tok_s": round(1e3 / ms1, 1),
             "verify_m2": {"ms_per_step": round(ms2, 4), "GB_s": round(total2 / ms2 / 1e6, 1),
                           "tok_s_max": round(2e3 / ms2, 1)},
-            "roofline": res["roofline"], "e2e": res["e2e"], "gpu_launches": res["launches"],
+            "roofline": step_roofline(total, ms1, world, res, args.layers), "e2e": res["e2e"], "gpu_launches": res["launches"],
             "clocks": res["clocks"],
         }
         if cpu:

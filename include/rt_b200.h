@@ -62,8 +62,18 @@ RTB_API void rt_gemv(struct rt *R, const void *w, long rows, long cols, const fl
 
 /* src/card/rt.h:65-69 (rt.c:217-285). The round: queue up to RT_BATCH products that do not read
  * each other's results, then rt_gemv_go runs all of them in one launch per kind and clears the
- * queue. rt_gemv_open marks the point where the reference starts its read-ahead before x has
- * landed; on B200 it does nothing (the launch at go takes microseconds). */
+ * queue.
+ * rt_gemv_open opens the round before its x has landed, as the reference does (rt.c:267-285: its
+ * threads read ahead until go). Here the round's CUDA-core products (t < 16) are launched at once:
+ * they stream their weights while the host still prepares x, and wait on the GPU (bounded, about a
+ * second) for go before they read x or a row list. Between open and go the host may pull the
+ * round's inputs (rt_b200_pull then copies on a link stream of R's, which first waits for the work
+ * already on R's stream); rt_gemv_go releases the round after those copies and launches the rest.
+ * As in the reference (src/card/team.h:21-24), nothing else may use R between open and go: a
+ * product or push on R's stream would wait for the opened round, whose wait for go then gives up
+ * and reports RTB_EKERNEL. rt_b200_sync closes an open round without releasing it (its kernel gives
+ * up and the error is returned). Open does nothing (go runs everything) for tensor-core products,
+ * row-sharded runtimes, chains, and while R's stream is being captured into a graph. */
 #define RT_BATCH 8
 RTB_API void rt_gemv_q(struct rt *R, const void *w, long rows, long cols, const float *x, float *y);
 RTB_API void rt_gemv_open(struct rt *R);
@@ -149,10 +159,10 @@ RTB_API int rt_b200_sync(struct rt *R);
 
 /* The link crossing of a round, where the engine keeps x and y in host memory (the reference's
  * link_pull / link_push, src/card/link.c:86-118). pull enqueues a host -> device copy of `bytes`
- * on R's stream and returns; push enqueues the device -> host copy, waits for R's stream (the
- * bytes are on the host at return, and a kernel's error word is read) and returns 0 or the first
- * error. Pinned host memory keeps the copies asynchronous. A round: pull x, the product (async
- * mode), push y. */
+ * on R's stream (on its link stream while a round is open) and returns; push enqueues the
+ * device -> host copy, waits for R's stream (the bytes are on the host at return, and a kernel's
+ * error word is read) and returns 0 or the first error. Pinned host memory keeps the copies
+ * asynchronous. A round: queue the product, rt_gemv_open, pull x, rt_gemv_go (async mode), push y. */
 RTB_API int rt_b200_pull(struct rt *R, void *dev, const void *host, size_t bytes);
 RTB_API int rt_b200_push(struct rt *R, void *host, const void *dev, size_t bytes);
 
@@ -200,11 +210,14 @@ RTB_API int rt_b200_wait_probe(struct rt *R);
  * rt_gemv_rows) and queued rounds (rt_gemv_go) are recorded, not run: each call or go is one round.
  * rt_b200_chain_end runs them in order as ONE persistent launch per 160 products (one decode step
  * is 129 rounds): weights stream across round boundaries with no launch in between, and a round
- * that reads an earlier round's y waits for that round on the GPU before reading x. serial != 0
- * makes every round wait for the one before (a decode step's dependency chain); serial == 0
- * derives the waits from overlapping x and y ranges. Rounds that cannot chain (t > 4, the
- * tensor-core path, several GPUs) run as separate launches in the same order. Blocking mode
- * waits at rt_b200_chain_end. 0 or an RTB_E* code. */
+ * that depends on earlier rounds waits for them on the GPU before it reads x or writes y.
+ * serial != 0 makes every round wait for the one before (a decode step's dependency chain);
+ * serial == 0 makes a round wait for every earlier round it conflicts with: its x overlaps their
+ * y (read after write), or its y overlaps their x (write after read) or their y (write after
+ * write). A round with more than four such rounds not already covered by each other's waits
+ * starts a new launch. Rounds that cannot chain (t > 4, the tensor-core path, several GPUs) run
+ * as separate launches in the same order. Blocking mode waits at rt_b200_chain_end. 0 or an
+ * RTB_E* code. */
 RTB_API int rt_b200_chain_begin(struct rt *R);
 RTB_API int rt_b200_chain_end(struct rt *R, int serial);
 

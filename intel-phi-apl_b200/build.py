@@ -4,7 +4,9 @@
 
 One nvcc invocation per source (objects under _build/, skipped when newer than their inputs),
 then one shared-library link. The library goes next to this file so it travels with the
-repository snapshot to a GPU host.
+repository snapshot to a GPU host. Then libengine_rounds.so: engine_rounds.c, a caller of that
+C ABI (rounds run as the reference engine runs them; bench.py's end-to-end timing), built with
+the host C compiler and linked against librt_b200.so.
 """
 from __future__ import annotations
 
@@ -27,6 +29,9 @@ FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", 
 # The exact products depend on IEEE fp32 fma and division: no fast-math, no flush-to-zero.
 FLAGS += ["-fmad=true", "-ftz=false", "-prec-div=true", "-prec-sqrt=true"]
 LIBS = ["-lcudart", "-ldl"]  # NCCL is opened at run time, on first use
+ENGINE_SRC = os.path.join(HERE, "engine_rounds.c")
+ENGINE_LIB = os.path.join(HERE, "libengine_rounds.so")
+CC = os.environ.get("CC", "gcc")
 
 
 def _newer(target: str, deps: list[str]) -> bool:
@@ -54,6 +59,12 @@ def build(force: bool = False, verbose: bool = False) -> str:
         subprocess.run(cmd, check=True)
     if force or not _newer(LIB, objects):
         cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objects, *LIBS]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+    if force or not _newer(ENGINE_LIB, [ENGINE_SRC, LIB, os.path.join(ROOT, "include", "rt_b200.h"), __file__]):
+        cmd = [CC, "-std=gnu11", "-O2", "-Wall", "-Wextra", "-Werror", "-fPIC", "-shared", "-I", os.path.join(ROOT, "include"),
+               "-o", ENGINE_LIB, ENGINE_SRC, "-L", HERE, "-lrt_b200", "-Wl,-rpath,$ORIGIN"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

@@ -255,6 +255,50 @@ __global__ void file_sum_kernel(const unsigned long long *w, long long words, un
 
 thread_local char t_load_msg[256];
 
+// Whether the load repacks tensor t in place (a Q8_0 matrix whose rows keep their length:
+// cols % 256 == 0, rows narrow enough for the repack's staging, 16-byte aligned), and its shape.
+bool repackable(const rtb_tensor &t, long long *rows_out, long long *cols_out) {
+    if (t.type != GT_Q8_0 || t.n_dims < 2)
+        return false;
+    const long long cols = t.dim[0];
+    long long rows = 1;
+    for (int d = 1; d < t.n_dims; ++d)
+        rows *= t.dim[d];
+    if (rows < 1 || q8_gguf_row_bytes(cols) > q8::REPACK_MAX_ROW_BYTES || q8s_row_bytes(cols) != q8_gguf_row_bytes(cols) ||
+        t.offset % 16)
+        return false; // empty, wider than the repack stages, or a row would change length: left in GGUF layout
+    *rows_out = rows;
+    *cols_out = cols;
+    return true;
+}
+
+// An in-place repack rewrites its tensor's bytes, so no other tensor may share any of them,
+// except a tied copy of the same matrix (same offset, type and dims: repacked once, both marked
+// repacked). A table with any other overlap (a crafted or mis-tied file) is refused before
+// anything is read.
+bool check_repack_overlaps(const Table &tab, std::string *why) {
+    for (size_t i = 0; i < tab.t.size(); ++i) {
+        const rtb_tensor &a = tab.t[i];
+        long long rows, cols;
+        if (!repackable(a, &rows, &cols))
+            continue;
+        for (size_t j = 0; j < tab.t.size(); ++j) {
+            const rtb_tensor &b = tab.t[j];
+            if (j == i || b.bytes == 0 || !(a.offset < b.offset + b.bytes && b.offset < a.offset + a.bytes))
+                continue;
+            bool tie = a.offset == b.offset && a.type == b.type && a.n_dims == b.n_dims && a.bytes == b.bytes;
+            for (int d = 0; tie && d < a.n_dims; ++d)
+                tie = a.dim[d] == b.dim[d];
+            if (!tie) {
+                *why = std::string("tensors ") + a.name + " and " + b.name +
+                       " share bytes but are not the same matrix (the in-place repack would corrupt one)";
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
 int fail(int code, const std::string &msg) {
     snprintf(t_load_msg, sizeof t_load_msg, "%s", msg.c_str());
     return code;
@@ -293,6 +337,11 @@ RTB_API int rt_b200_load_gguf(struct rt *R, const char *path, void *arena, unsig
     const uint64_t fb = tab.file_bytes;
     if (arena_bytes < (fb + 7) / 8 * 8)
         return fail(RTB_EINVAL, "rt_b200_load_gguf: arena smaller than the file");
+    {
+        std::string why;
+        if (!check_repack_overlaps(tab, &why))
+            return fail(RTB_EINVAL, "rt_b200_load_gguf: " + why);
+    }
     if (out && cap < int(tab.t.size()))
         return fail(RTB_EINVAL, "rt_b200_load_gguf: tensor table too small");
 
@@ -402,17 +451,10 @@ RTB_API int rt_b200_load_gguf(struct rt *R, const char *path, void *arena, unsig
     for (size_t i = 0; ok && i < tab.t.size(); ++i) {
         rtb_tensor &t = tab.t[i];
         t.dev = static_cast<char *>(arena) + t.offset;
-        if (t.type != GT_Q8_0 || t.n_dims < 2)
+        long long rows, cols;
+        if (!repackable(t, &rows, &cols))
             continue;
-        const long long cols = t.dim[0];
-        long long rows = 1;
-        for (int d = 1; d < t.n_dims; ++d)
-            rows *= t.dim[d];
-        if (rows < 1 || q8_gguf_row_bytes(cols) > q8::REPACK_MAX_ROW_BYTES ||
-            q8s_row_bytes(cols) != q8_gguf_row_bytes(cols) || t.offset % 16)
-            continue; // empty, wider than the repack stages, or a row would change length (cols % 256
-                      // != 0): left in GGUF layout
-        bool seen = false;
+        bool seen = false; // a tied copy (same offset, type and dims: check_repack_overlaps)
         for (uint64_t o : done)
             seen |= o == t.offset;
         t.repacked = 1;

@@ -9,16 +9,21 @@
 // size instead. The caller passes only inputs and outputs. Nothing here calls cudaMalloc,
 // cudaFree or an allocating library routine.
 //
-//   - Limit: the fp16 copy of x must fit STATIC_X_BYTES = 8 MiB, so t * cols <= 4,194,304
-//     (e.g. 512 tokens of 8192 columns). Larger calls are rejected with RTB_EINVAL.
-//   - Every GPU that loads the library holds the array (8 MiB + 256 bytes) until the process
+//   - Limits: the fp16 copy of x must fit STATIC_X_BYTES = 8 MiB, so t * cols <= 4,194,304
+//     (e.g. 512 tokens of 8192 columns), and the per-row scale exponents STATIC_ROW_BYTES, so
+//     rows <= 1,048,576. Larger calls are rejected with RTB_EINVAL.
+//   - Every GPU that loads the library holds the array (9.5 MiB + 256 bytes) until the process
 //     exits.
 //   - All calls share the one array. Calls that overlap on the GPU (from two host threads, or on
 //     two streams) race on it and must not be issued.
 //   - The first call on a device looks up the array's device address on that device (the name
 //     of the array in host code is only a stand-in, not a device address). Make that first call
-//     before any stream capture.
+//     before any stream capture. A later call repeats the look-up only if the device's context
+//     changed (after cudaDeviceReset, say).
+//   - Each call waits for `stream` before it returns: it reads the kernel's error word back.
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <mutex>
 
@@ -28,14 +33,18 @@
 
 namespace {
 
-constexpr size_t STATIC_HEADER = 256;          // the kernel's error word, then padding
-constexpr size_t STATIC_X_BYTES = 8ull << 20;  // the fp16 copy of x
+constexpr size_t STATIC_HEADER = 256;             // the kernel's error word, then padding
+constexpr size_t STATIC_X_BYTES = 8ull << 20;     // the fp16 copy of x
+constexpr size_t STATIC_TOKEN_BYTES = 512ull << 10; // 2^-s_t per token: t <= 131,072 (t * cols <= 4 Mi, cols >= 32)
+constexpr size_t STATIC_ROW_BYTES = 1ull << 20;   // r_o per weight row: rows <= 1,048,576
+constexpr size_t STATIC_SCRATCH = STATIC_X_BYTES + STATIC_TOKEN_BYTES + STATIC_ROW_BYTES;
 constexpr int MAX_DEVICES = 64;
 
-static __device__ __align__(256) unsigned char g_static_scratch[STATIC_HEADER + STATIC_X_BYTES];
+static __device__ __align__(256) unsigned char g_static_scratch[STATIC_HEADER + STATIC_SCRATCH];
 
 struct DeviceScratch {
     bool ready = false;
+    void *ctx = nullptr;           // the device's context when the address was looked up
     unsigned char *base = nullptr; // device address of g_static_scratch on this device
     int num_sms = 0;
 };
@@ -43,20 +52,43 @@ struct DeviceScratch {
 std::mutex g_setup_mutex;
 DeviceScratch g_devices[MAX_DEVICES];
 
-// Once per device, with that device current: the array's device address and the SM count.
+// The calling thread's current context (the driver's cuCtxGetCurrent, looked up through the
+// runtime), or null.
+void *current_context() {
+    static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void *f = nullptr;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 4000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(f);
+    });
+    CUcontext c = nullptr;
+    if (!fn || fn(&c) != CUDA_SUCCESS)
+        return nullptr;
+    return c;
+}
+
+// Once per device (again if its context changed), with that device current: the array's device
+// address and the SM count.
 int device_scratch(DeviceScratch **out) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES)
         return RTB_ECUDA;
+    void *ctx = current_context(); // null before this thread's first CUDA work on the device
     std::lock_guard<std::mutex> lock(g_setup_mutex);
     DeviceScratch &d = g_devices[dev];
-    if (!d.ready) {
+    if (!d.ready || !ctx || d.ctx != ctx) {
+        d.ready = false;
         void *p = nullptr;
+        // (the look-up also makes the device's primary context current when none was)
         if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || !p)
             return RTB_ECUDA;
         if (cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
             return RTB_ECUDA;
         d.base = static_cast<unsigned char *>(p);
+        d.ctx = current_context();
         d.ready = true;
     }
     *out = &d;
@@ -73,8 +105,8 @@ extern "C" RTB_API int rt_gemm_static(const void *w, long rows, long cols, const
         t > (1l << 20) || !aligned(w, 16) || !aligned(x, 16) || !aligned(y, 4))
         return RTB_EINVAL;
     const size_t xh_bytes = (size_t(t) * size_t(cols) * 2 + 255) / 256 * 256;
-    if (xh_bytes > STATIC_X_BYTES)
-        return RTB_EINVAL; // t * cols beyond the static scratch: use rt_gemm
+    if (xh_bytes > STATIC_X_BYTES || size_t(rows) > STATIC_ROW_BYTES)
+        return RTB_EINVAL; // beyond the static scratch: use rt_gemm
     DeviceScratch *d = nullptr;
     const int rc = device_scratch(&d);
     if (rc != RTB_OK)
@@ -94,7 +126,9 @@ extern "C" RTB_API int rt_gemm_static(const void *w, long rows, long cols, const
     job.rows = rows;
     job.cols = int(cols);
     job.t = int(t);
-    if (q8::launch_gemm_tc(&job, 1, d->base + STATIC_HEADER, STATIC_X_BYTES, d->num_sms, err, s, false, false) !=
+    if (q8::gemm_tc_scratch_bytes(&job, 1, d->num_sms, false) > STATIC_SCRATCH)
+        return RTB_EINVAL;
+    if (q8::launch_gemm_tc(&job, 1, d->base + STATIC_HEADER, STATIC_SCRATCH, d->num_sms, err, s, false, false) !=
         cudaSuccess)
         return RTB_ECUDA;
     unsigned h = 0;

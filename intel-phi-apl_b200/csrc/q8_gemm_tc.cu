@@ -10,6 +10,14 @@
 // x is rounded to fp16 once per call (a pre-pass into scratch). fp16 rather than bf16: the same
 // tcgen05 kind::f16 rate with 3 more mantissa bits, which is what holds the product within the
 // stated 2e-3 (bf16 tiles measure ~1e-2 on the BASELINE shapes).
+// fp16's range is narrow (normal from 2^-14, finite below 65504) while the reference takes any
+// fp32 x and any fp16 scale (src/card/gemm.c:271-294). So both operands are scaled by powers of
+// two into the middle of that range before rounding: token t's x by 2^s_t, with |x| <= 2^15 at
+// its largest entry, and row o's weights by 2^r_o, with 127 * (the row's largest scale) in
+// [2^14, 2^15). The accumulator then holds y * 2^(r_o + s_t), and the epilogue multiplies by
+// 2^-r_o and 2^-s_t, which is exact. Where nothing under- or overflowed the fp16 operands are the
+// unscaled ones' bits with a shifted exponent, so the product rounds exactly as it did unscaled.
+// The pre-pass that rounds x also finds the factors (tc_prep_kernel).
 //
 // A CTA (persistent; one per SM owning all 512 TMEM columns, or two per SM with 256 each for
 // tiles of up to 64 tokens: TcShape below) runs 128-row x BN-token tiles (a SwiGLU pair's tile:
@@ -96,6 +104,8 @@ __host__ __device__ constexpr int n_acc(int bn, int cps) { return bn <= 128 / cp
 
 struct TcJobDev {
     CUtensorMap tq, td, tq2, td2; // quants and scales of W (and of the SwiGLU up matrix)
+    const int8_t *rexp;           // r_o per row: W's rows, then (a pair) the up matrix's rows
+    const float *tokf;            // 2^-s_t per token
     float *y;
     float *part;                  // split-K partial sums as [plane][t][rows]: plane = (up ? ks : 0) + K part
     long long rows, ldy;
@@ -214,6 +224,20 @@ struct Ring {
     }
 };
 
+// 2^k as a float, for k in [-126, 127] (a normal number: exact).
+__device__ __forceinline__ float pow2i(int k) { return __int_as_float((127 + k) << 23); }
+
+// The fp16 scale of a row for its weights: 127 * dmax * 2^r in [2^14, 2^15), r in [-9, 31] for
+// every finite nonzero fp16 dmax (given as its bits without the sign); 0 for a zero or
+// non-finite maximum (an inf or NaN scale then propagates as in the reference).
+__device__ __forceinline__ int row_exponent(unsigned dmax_bits) {
+    if (dmax_bits == 0 || dmax_bits >= 0x7c00u)
+        return 0;
+    int e;
+    frexpf(127.0f * __half2float(__ushort_as_half(uint16_t(dmax_bits))), &e); // value in [2^(e-1), 2^e)
+    return 15 - e;
+}
+
 template <int CPS>
 __global__ void __launch_bounds__(TcShape<CPS>::NT, CPS) gemm_tc_kernel(const __grid_constant__ TcParams p) {
     using Sh = TcShape<CPS>;
@@ -302,9 +326,25 @@ __global__ void __launch_bounds__(TcShape<CPS>::NT, CPS) gemm_tc_kernel(const __
         bool ok = true;
         // a pair's tile: lane 32e+l reads shared row 16e+l (gate, l < 16) or 64+16e+l-16 (up)
         const int ipair = (i & 16) ? PAIR_ROWS + 16 * (i >> 5) + (i & 15) : 16 * (i >> 5) + (i & 15);
+        // this lane's weight row exponent r_o, loaded one unit ahead (its latency then hides
+        // behind a unit's stages)
+        auto row_exp = [&](int u) -> int {
+            if (u >= p.total_units)
+                return 0;
+            const Unit w = unit_of(p, u);
+            const TcJobDev &J = p.job[w.j];
+            const long long row = J.pair ? (long long)w.rt * PAIR_ROWS + 16 * (i >> 5) + (i & 15)
+                                         : (long long)w.rt * BM + i;
+            if (row >= J.rows)
+                return 0; // a tail tile's missing rows: zeros from the copy
+            return J.rexp[(J.pair && (i & 16)) ? J.rows + row : row];
+        };
+        int rx_next = row_exp(blockIdx.x);
         for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
             const Unit w = unit_of(p, u);
             const int r = p.job[w.j].pair ? ipair : i; // the shared-memory row behind this lane
+            const float rowf = pow2i(rx_next);
+            rx_next = row_exp(u + gridDim.x);
             for (int kb = w.kb0; kb < w.kb1; ++kb, ring.next(S)) {
                 const int slot = ring.slot; // also the A slot
                 if (!mbar_wait(&full[slot], ring.phase)) {
@@ -319,9 +359,11 @@ __global__ void __launch_bounds__(TcShape<CPS>::NT, CPS) gemm_tc_kernel(const __
 #pragma unroll
                 for (int hb = 0; hb < Sh::BLOCKS_PER_THREAD; ++hb) {
                     const int h = h0 + hb;
-                    // this block's scale (one of the 8 the scale box holds) and its 32 quants
-                    const __half2 dd2 = __half2half2(
-                        *reinterpret_cast<const __half *>(st + OFF_D + r * 16 + ((kb * 2 + h) & 7) * 2));
+                    // this block's scale (one of the 8 the scale box holds) times 2^r_o (exact
+                    // while the result is a normal fp16), and its 32 quants
+                    const __half2 dd2 = __half2half2(__float2half_rn(
+                        __half2float(*reinterpret_cast<const __half *>(st + OFF_D + r * 16 + ((kb * 2 + h) & 7) * 2)) *
+                        rowf));
                     uint32_t outw[16];
 #pragma unroll
                     for (int cc = 0; cc < 2; ++cc) { // 16 quants per chunk; chunks 2h, 2h+1
@@ -402,6 +444,7 @@ __global__ void __launch_bounds__(TcShape<CPS>::NT, CPS) gemm_tc_kernel(const __
         // writes 32 consecutive floats, one 128-byte segment); this measured faster here than
         // bulk tensor stores through shared-memory staging boxes, which queue behind the loads.
         // The accumulator is handed back as soon as a warp's last columns are in registers.
+        // Each value is multiplied back by 2^-r_o (its row) and 2^-s_t (its token) first.
         const int e = warp & 3, eh = warp > MMA_WARP ? 1 + (warp - MMA_WARP - 1) / 4 : 0; // column share
         int tcount = 0;
         bool ok = true;
@@ -409,6 +452,11 @@ __global__ void __launch_bounds__(TcShape<CPS>::NT, CPS) gemm_tc_kernel(const __
             const Unit w = unit_of(p, u);
             const TcJobDev &J = p.job[w.j];
             const int b = tcount % NACC;
+            // this lane's row exponent, loaded before the wait for the accumulator
+            const bool up_lane = J.pair && (lane & 16);
+            const long long orow = J.pair ? (long long)w.rt * PAIR_ROWS + 16 * e + (lane & 15)
+                                          : (long long)w.rt * BM + 32 * e + lane;
+            const float rinv = orow < J.rows ? pow2i(-int(J.rexp[up_lane ? J.rows + orow : orow])) : 1.0f;
             if (!mbar_wait(&accfull[b], (tcount / NACC) & 1)) {
                 report(p.err, ERR_TIMEOUT_MMA);
                 ok = false;
@@ -434,6 +482,11 @@ __global__ void __launch_bounds__(TcShape<CPS>::NT, CPS) gemm_tc_kernel(const __
             const long long row = J.pair ? (long long)w.rt * PAIR_ROWS + 16 * e + (lane & 15)
                                          : (long long)w.rt * BM + 32 * e + lane;
             for (int c0 = cbeg; c0 < cend; c0 += 16) {
+                // the 16 tokens' factors 2^-s_t (1 past the last token: those columns are zero)
+                float tf[16];
+#pragma unroll
+                for (int c = 0; c < 16; ++c)
+                    tf[c] = n0 + c0 + c < ntok ? __ldg(J.tokf + n0 + c0 + c) : 1.0f;
                 uint32_t r[16];
                 tmem_ld16(tacc + uint32_t(c0), r);
                 tmem_wait_ld();
@@ -441,16 +494,20 @@ __global__ void __launch_bounds__(TcShape<CPS>::NT, CPS) gemm_tc_kernel(const __
                     tc_fence_before();
                     mbar_arrive(&accempty[b]);
                 }
+                float v[16];
+#pragma unroll
+                for (int c = 0; c < 16; ++c)
+                    v[c] = __uint_as_float(r[c]) * rinv * tf[c];
                 if (J.pair && !split) {
                     // y = silu(g) * u: the gate lane finishes tokens c0..c0+7 of its row, the up
                     // lane tokens c0+8..c0+15, each taking the other factor from its partner
                     float g[8], uv[8];
 #pragma unroll
                     for (int k = 0; k < 8; ++k) {
-                        const float give = __uint_as_float(up ? r[k] : r[8 + k]);
+                        const float give = up ? v[k] : v[8 + k];
                         const float got = __shfl_xor_sync(0xffffffffu, give, 16);
-                        g[k] = up ? got : __uint_as_float(r[k]);
-                        uv[k] = up ? __uint_as_float(r[8 + k]) : got;
+                        g[k] = up ? got : v[k];
+                        uv[k] = up ? v[8 + k] : got;
                     }
                     const int tk0 = n0 + c0 + (up ? 8 : 0);
                     if (row < nrows) {
@@ -474,7 +531,7 @@ __global__ void __launch_bounds__(TcShape<CPS>::NT, CPS) gemm_tc_kernel(const __
 #pragma unroll
                     for (int c = 0; c < 16; ++c)
                         if (n0 + c0 + c < ntok)
-                            yp[(long long)c * ld] = __uint_as_float(r[c]);
+                            yp[(long long)c * ld] = v[c];
                 }
             }
         }
@@ -486,11 +543,66 @@ __global__ void __launch_bounds__(TcShape<CPS>::NT, CPS) gemm_tc_kernel(const __
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
 }
 
-__global__ void x_to_half_kernel(const float *x, long long ldx, int cols, int t, __half *xh) {
-    const long long n = (long long)t * cols;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-        const long long r = i / cols, c = i - r * cols;
-        xh[i] = __float2half_rn(x[r * ldx + c]);
+// The pre-pass of a job, before its product on the stream. Blocks [0, t): one token each: the
+// largest |x| of the token gives s_t (|x| * 2^s_t <= 2^15 at that entry; s_t <= 126), then
+// xh = fp16(x * 2^s_t) and tokf[t] = 2^-s_t. Blocks from t: one warp per matrix row (W's rows, then
+// a pair's up rows): the row's largest scale gives r_o (row_exponent) into rexp.
+constexpr int PREP_THREADS = 256;
+
+__global__ void __launch_bounds__(PREP_THREADS) tc_prep_kernel(const float *x, long long ldx, int cols, int t,
+                                                               __half *xh, float *tokf, const uint8_t *w,
+                                                               const uint8_t *w2, long long rows, int8_t *rexp) {
+    if (blockIdx.x < unsigned(t)) {
+        __shared__ float part[PREP_THREADS / 32];
+        __shared__ int s_sh;
+        const float *xt = x + (long long)blockIdx.x * ldx;
+        float amax = 0.0f;
+        for (int c = threadIdx.x; c < cols; c += PREP_THREADS)
+            amax = fmaxf(amax, fabsf(xt[c]));
+        for (int o = 16; o; o >>= 1)
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if (threadIdx.x % 32 == 0)
+            part[threadIdx.x / 32] = amax;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float m = part[0];
+            for (int k = 1; k < PREP_THREADS / 32; ++k)
+                m = fmaxf(m, part[k]);
+            int sx = 0;
+            if (m > 0.0f && m <= 3.4028234663852886e38f) {
+                int e;
+                frexpf(m, &e); // m in [2^(e-1), 2^e)
+                sx = 15 - e;   // m * 2^sx in [2^14, 2^15)
+                sx = sx > 126 ? 126 : sx;
+            }
+            s_sh = sx;
+            tokf[blockIdx.x] = pow2i(-sx);
+        }
+        __syncthreads();
+        const float f = pow2i(s_sh);
+        __half *ht = xh + (long long)blockIdx.x * cols;
+        for (int c = threadIdx.x; c < cols; c += PREP_THREADS)
+            ht[c] = __float2half_rn(xt[c] * f);
+        return;
+    }
+    const long long nrows = w2 ? 2 * rows : rows;
+    const long long rb = q8s_row_bytes(cols), nsc16 = q8s_scale_stride(cols) / 8; // 16-byte scale chunks
+    const int lane = threadIdx.x % 32;
+    const long long wstep = (long long)(gridDim.x - t) * (PREP_THREADS / 32);
+    for (long long o = (long long)(blockIdx.x - t) * (PREP_THREADS / 32) + threadIdx.x / 32; o < nrows; o += wstep) {
+        const uint8_t *row = (o < rows ? w + o * rb : w2 + (o - rows) * rb) + cols;
+        unsigned mb = 0;
+        for (long long k = lane; k < nsc16; k += 32) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4 *>(row) + k);
+            const unsigned a[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                mb = max(mb, max(a[j] & 0x7fffu, (a[j] >> 16) & 0x7fffu));
+        }
+        for (int off = 16; off; off >>= 1)
+            mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, off));
+        if (lane == 0)
+            rexp[o] = int8_t(row_exponent(mb));
     }
 }
 
@@ -619,7 +731,11 @@ size_t part_bytes(const GemmJob &G, int ks) {
     return ks > 1 ? (size_t(G.w2 ? 2 : 1) * ks * G.t * G.rows * sizeof(float) + 255) / 256 * 256 : 0;
 }
 
-size_t x_bytes(const GemmJob &G) { return (size_t(G.t) * G.cols * sizeof(__half) + 255) / 256 * 256; }
+// A job's pre-pass output: fp16 x, 2^-s_t per token and r_o per weight row, each 256-aligned.
+size_t xh_bytes(const GemmJob &G) { return (size_t(G.t) * G.cols * sizeof(__half) + 255) / 256 * 256; }
+size_t tokf_bytes(const GemmJob &G) { return (size_t(G.t) * sizeof(float) + 255) / 256 * 256; }
+size_t rexp_bytes(const GemmJob &G) { return (size_t(G.rows) * (G.w2 ? 2 : 1) + 255) / 256 * 256; }
+size_t x_bytes(const GemmJob &G) { return xh_bytes(G) + tokf_bytes(G) + rexp_bytes(G); }
 
 // One launch of the CPS-per-SM shape. With CPS = 1 the CTA allocates all 512 TMEM columns, so a
 // second CTA on the SM would only wait in its allocation: more than half the SM's shared memory
@@ -703,16 +819,26 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
         if (G.cols < Q8_QK || G.cols % Q8_QK || G.t < 1 || G.rows < 1)
             return cudaErrorInvalidValue;
         __half *xh = reinterpret_cast<__half *>(sc);
+        float *tokf = reinterpret_cast<float *>(sc + xh_bytes(G));
+        int8_t *rexp = reinterpret_cast<int8_t *>(sc + xh_bytes(G) + tokf_bytes(G));
         sc += x_bytes(G);
-        const long long nconv = (long long)G.t * G.cols;
-        int grid = int((nconv + 255) / 256);
-        grid = grid > 4096 ? 4096 : grid;
-        x_to_half_kernel<<<grid, 256, 0, stream>>>(G.x, G.ldx, G.cols, G.t, xh);
+        {
+            const long long nrows = G.rows * (G.w2 ? 2 : 1);
+            long long rblocks = (nrows + PREP_THREADS / 32 - 1) / (PREP_THREADS / 32);
+            rblocks = rblocks > 1184 ? 1184 : rblocks;
+            tc_prep_kernel<<<unsigned(G.t + rblocks), PREP_THREADS, 0, stream>>>(G.x, G.ldx, G.cols, G.t, xh, tokf, G.w,
+                                                                               G.w2, G.rows, rexp);
+            cudaError_t e = cudaGetLastError();
+            if (e != cudaSuccess)
+                return e;
+        }
         if (!make_map(&p.tx[j], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh, uint64_t(G.cols), uint64_t(G.t),
                       uint64_t(G.cols) * 2, 64, uint32_t(bn), CU_TENSOR_MAP_SWIZZLE_128B))
             return cudaErrorInvalidValue;
         TcJobDev &J = p.job[j];
         J.pair = G.w2 != nullptr;
+        J.rexp = rexp;
+        J.tokf = tokf;
         const uint32_t box_rows = J.pair ? PAIR_ROWS : BM;
         if (!weight_maps(G.w, G.rows, G.cols, box_rows, &J.tq, &J.td))
             return cudaErrorInvalidValue;

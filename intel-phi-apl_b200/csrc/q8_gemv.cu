@@ -20,7 +20,8 @@
 //              stay on one);
 //   last warp  copies: issues a stage's bulk copies as soon as its slot is free.
 // One token runs two CTAs per SM, more tokens one (Cfg).
-// Barriers: full (copies landed), empty (slot read), tfull/tempty (partial sums). Every wait is
+// Barriers: full (copies landed), empty (slot read), tfull/tempty (partial sums; tfull one set per
+// chain warp: see the chain warps' loop). Every wait is
 // bounded: a timeout sets a bit in the context's error word and the CTA leaves.
 #include <cuda_fp16.h>
 
@@ -80,7 +81,7 @@ constexpr size_t smem_bytes() {
     using C = Cfg<MT, CTAS>;
     static_assert(FRING >= C::STAGES + C::TBUF + 2, "row-flag ring");
     return size_t(C::STAGES) * SLOT + size_t(C::TBUF) * (MT + 1) * R * TPAD * 4 +
-           (C::STAGES * 2 + C::TBUF * 2 + 1) * 8 + FRING * R;
+           (C::STAGES * 2 + C::TBUF * (C::NCHAIN + 1) + 1) * 8 + FRING * R;
 }
 
 // One job's fields, cached in registers by every role when its stage sequence enters the job:
@@ -91,15 +92,13 @@ struct JobView {
     const float *x;
     float *y;
     unsigned *done_ctr;
-    const unsigned *wait_ctr;
-    unsigned wait_target;
+    int nwait; // the waits themselves stay in the kernel parameters (read once per job)
     int x_written;
     long long rows, src_rows, ldx, ldy, rb;
     int cols, m, tile0, rpt, nchunk;
     __device__ __forceinline__ void load(const GemvJob &J) {
         done_ctr = J.done_ctr;
-        wait_ctr = J.wait_ctr;
-        wait_target = J.wait_target;
+        nwait = J.nwait;
         x_written = J.x_written;
         w = J.w;
         w2 = J.w2;
@@ -221,6 +220,23 @@ __device__ __noinline__ bool wait_count(const unsigned *ctr, unsigned target) {
     }
 }
 
+// Waits until the gate word has reached `value` (modulo 2^32: the host counts rounds), read at
+// system scope: the link stream's write-value operation sets it after the round's copies.
+__device__ __noinline__ bool wait_gate(const unsigned *gate, unsigned value) {
+    const long long t0 = clock64();
+    for (;;) {
+        unsigned v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(gate) : "memory");
+        if (int(v - value) >= 0)
+            return true;
+        const long long dt = clock64() - t0;
+        if (dt > WAIT_LIMIT_CYCLES)
+            return false;
+        if (dt > 20000)
+            __nanosleep(200);
+    }
+}
+
 // The failure path's self-test: one thread waits on a device counter that nothing advances, then
 // on an mbarrier that nothing arrives on. Each wait gives up after WAIT_LIMIT_CYCLES (about a
 // second) and reports its bit, as a stuck wait in a product kernel does; the kernel then returns.
@@ -245,8 +261,8 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
     float *TD = T + TBUF * MT * R * TPAD;                                 // [TBUF][R][TPAD]
     uint64_t *full = reinterpret_cast<uint64_t *>(TD + TBUF * R * TPAD);  // [STAGES]
     uint64_t *empty = full + STAGES;                                      // [STAGES]
-    uint64_t *tfull = empty + STAGES;                                     // [TBUF]
-    uint64_t *tempty = tfull + TBUF;                                      // [TBUF]
+    uint64_t *tfull = empty + STAGES;                                     // [NCHAIN][TBUF]
+    uint64_t *tempty = tfull + NCHAIN * TBUF;                             // [TBUF]
     uint64_t *depbar = tempty + TBUF;                                     // a chained round's dependency met
     uint8_t *rowflag = reinterpret_cast<uint8_t *>(depbar + 1);           // [FRING][R]: row was loaded
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
@@ -257,7 +273,8 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
             mbar_init(&empty[s], NC);
         }
         for (int b = 0; b < TBUF; ++b) {
-            mbar_init(&tfull[b], NC);
+            for (int w = 0; w < NCHAIN; ++w)
+                mbar_init(&tfull[w * TBUF + b], NC);
             mbar_init(&tempty[b], 1);
         }
         mbar_init(depbar, 1);
@@ -270,8 +287,22 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
         // ---------------------------------------------------------------- compute threads
         float xr[MT][Q8_QK];
         int xjob = -1, xc = -1, wjob = -1, ndep = 0;
+        int ctile = 0; // the CTA's tiles so far: tile i's partial sums go to chain warp i % NCHAIN
         const int b = tid % NBK, half = tid / NBK;
         grid_wait(); // x comes from the previous kernel on the stream
+        if (p.gate) {
+            // an opened round: x lands after the launch. Compute thread 0 polls the gate and
+            // passes it on through the CTA barrier (its first phase), as for a chained round.
+            if (tid == 0) {
+                if (!wait_gate(p.gate, p.gate_value))
+                    report(p.err, ERR_TIMEOUT_GATE);
+                mbar_arrive(depbar);
+            } else if (lane == 0 && !mbar_wait(depbar, 0)) {
+                report(p.err, ERR_TIMEOUT_GATE);
+            }
+            ndep = 1;
+            __syncwarp();
+        }
         StageIter it;
         it.start(p);
         for (int s = 0; it.valid(p); it.next(p), ++s) {
@@ -284,15 +315,20 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
             const int nbk = min(KC, it.J.cols - c0) / Q8_QK;
             const bool active = b < nbk;
             if (it.job != wjob) {
-                // A chained job that depends on an earlier round: its x is that round's output,
-                // written during this launch. Compute thread 0 alone polls the round's counter
-                // (bounded, an acquire at GPU scope) and passes it on through a CTA barrier that
-                // the other compute warps wait on, bounded like every wait here.
+                // A chained job that depends on earlier rounds of this launch: its x may be their
+                // output (read after write), its y may overwrite their x (write after read) or
+                // their y (write after write). Compute thread 0 alone polls those rounds' tile
+                // counters (bounded, acquires at GPU scope) and passes the result on through a
+                // CTA barrier that the other compute warps wait on, bounded like every wait here.
+                // The tile's y is written by the chain warps only after these warps computed it,
+                // so the one wait here orders the writes too.
                 wjob = it.job;
-                if (it.J.wait_ctr) {
+                if (it.J.nwait) {
                     if (tid == 0) {
-                        if (!wait_count(it.J.wait_ctr, it.J.wait_target))
-                            report(p.err, ERR_TIMEOUT_ROUND);
+                        const GemvJob &PJ = p.job[it.job];
+                        for (int k = 0; k < it.J.nwait; ++k)
+                            if (!wait_count(PJ.wait_ctr[k], PJ.wait_target[k]))
+                                report(p.err, ERR_TIMEOUT_ROUND);
                         mbar_arrive(depbar);
                     } else if (lane == 0 && !mbar_wait(depbar, ndep & 1)) {
                         report(p.err, ERR_TIMEOUT_ROUND);
@@ -373,7 +409,9 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
             }
             if (!ok)
                 break;
-            mbar_arrive(&tfull[tb]);
+            mbar_arrive(&tfull[(ctile % NCHAIN) * TBUF + tb]);
+            if (it.c == it.J.nchunk - 1)
+                ++ctile;
         }
     } else if (warp < COPY_WARP) {
         // ---------------------------------------------------------------- chain warps
@@ -400,6 +438,12 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
                         reinterpret_cast<float *>(po.region[w] + stage_off)[gi] = v;
             }
         };
+        // The chain warps take the CTA's tiles in turn, so a chain warp skips the other's tiles:
+        // after a tile of at least TBUF chunks it would wait on a shared barrier more than one
+        // phase ahead, which a parity wait cannot tell from the phase before. So each chain
+        // warp has its own TBUF barriers, which advance only on its own stages, and keeps their
+        // parities here (bit b: buffer b).
+        uint32_t tpar = 0;
         StageIter it;
         it.start(p);
         for (int s = 0, tile = 0; it.valid(p); ++s) {
@@ -407,10 +451,11 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
             const int tb = s % TBUF;
             const bool last_chunk = it.c == it.J.nchunk - 1;
             if (own) {
-                if (!mbar_wait(&tfull[tb], (s / TBUF) & 1)) {
+                if (!mbar_wait(&tfull[cw * TBUF + tb], (tpar >> tb) & 1u)) {
                     report(p.err, ERR_TIMEOUT_TFULL);
                     break;
                 }
+                tpar ^= 1u << tb;
                 const int nbk = min(KC, it.J.cols - it.c * KC) / Q8_QK;
                 const long long o = it.out_row(r);
                 const bool valid = o < it.J.rows;
@@ -477,6 +522,11 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
             gathers |= p.job[j].idx != nullptr;
         if (!p.early || gathers)
             grid_wait(); // weights (unless the caller vouches for them) and row lists may be outputs of it
+        if (gathers && p.gate) { // an opened round's row lists may land with its x
+            if (lane == 0 && !wait_gate(p.gate, p.gate_value))
+                report(p.err, ERR_TIMEOUT_GATE);
+            __syncwarp();
+        }
         StageIter it;
         it.start(p);
         long long src = -1; // this lane's source row for the current stage (gathers: prefetched)

@@ -9,6 +9,7 @@ namespace q8 {
 
 constexpr int MAX_JOBS = 16;  // products one launch serves (a round: the reference queues <= 8)
 constexpr int GEMV_MAX_T = 4; // tokens per pass of the CUDA-core kernel (larger t: several passes)
+constexpr int MAX_WAITS = 4;  // earlier rounds a chained round can wait on (more: a new launch)
 
 // One product of the CUDA-core kernel: y[t][o] = sum_k W[row(o)][k] * x[t][k] for o < rows,
 // t < m, in the reference's rounding order. row(o) = idx ? idx[o] : o. With w2 set the job is a
@@ -27,11 +28,13 @@ struct GemvJob {
     int tiles;          // row tiles of this job (filled by the launcher)
     int tile0;          // its first tile in the launch (filled by the launcher)
     // Chained launches (launch_gemv_chain): the job's round counts its finished row tiles into
-    // done_ctr; with wait_ctr set, the job reads x only once *wait_ctr >= wait_target (the tiles
-    // of the round it depends on). Null in plain launches.
+    // done_ctr; the job starts its tiles (reads x, and later writes y) only once
+    // *wait_ctr[i] >= wait_target[i] for every i < nwait: the tile counts of the earlier rounds it
+    // depends on. Null / 0 in plain launches.
     unsigned *done_ctr;
-    const unsigned *wait_ctr;
-    unsigned wait_target;
+    const unsigned *wait_ctr[MAX_WAITS];
+    unsigned wait_target[MAX_WAITS];
+    int nwait;
     int x_written;      // chained: x overlaps a y written earlier in the launch (read it past L1)
 };
 // Chained launches' round counters sit one per 128-byte line (pollers and the tile counts of
@@ -67,6 +70,12 @@ struct GemvParamsT {
     int early;     // 1: weights may stream in before the previous kernel on the stream completes
     unsigned *err; // the context's device error word
     PeerOut peer;  // peer.on: one job, row-sharded; y is gathered through the peers' staging
+    // An opened round (rt_gemv_open): the kernel is launched before its x has landed. It streams
+    // its weights at once, but reads x (and row lists) only once *gate has reached gate_value
+    // (written by the link stream after the round's pulls, at rt_gemv_go), bounded like every
+    // wait. Null: no gate.
+    const unsigned *gate;
+    unsigned gate_value;
 };
 using GemvParams = GemvParamsT<MAX_JOBS>;
 

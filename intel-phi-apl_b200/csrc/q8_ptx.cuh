@@ -16,6 +16,7 @@ enum : unsigned {
     ERR_BAD_JOB = 1u << 5,        // a gather index outside the matrix (its y is NaN), or a job the kernel cannot run
     ERR_TIMEOUT_PEER = 1u << 6,   // a peer GPU's flag never arrived
     ERR_TIMEOUT_ROUND = 1u << 7,  // a chained round's dependency never completed
+    ERR_TIMEOUT_GATE = 1u << 8,   // an opened round's x never landed (no rt_gemv_go)
 };
 
 // A spin of about this many SM clocks (~1 s at 2 GHz) is a hang, not a slow GPU.

@@ -2,10 +2,12 @@
 // the split of a product into kernel launches, row sharding with an NCCL all-gather, and the
 // error state. The reference's counterparts are src/card/rt.c:179-285 (products) and 484-501
 // (rt_q8_row); there the work runs on a thread team, here on the GPU.
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <bitset>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -97,7 +99,32 @@ struct Ctx {
     bool chaining = false;
     std::vector<std::vector<Item>> chain;
     unsigned *d_round = nullptr;
+    // opened rounds (rt_gemv_open .. rt_gemv_go): the gate word the pre-launched kernel waits on,
+    // the rounds counted so far, and the link stream that carries the round's pulls and then the
+    // gate's new value
+    unsigned *d_gate = nullptr;
+    unsigned gate_seq = 0;
+    cudaStream_t link = nullptr;
+    cudaEvent_t ev_before = nullptr, ev_link = nullptr;
+    bool round_open = false;
 };
+
+// cuStreamWriteValue32 (the driver's stream memory operation: executed by the GPU's front end in
+// stream order, it needs no SM, so it cannot queue behind the gated kernel it releases), looked up
+// through the runtime; null where the driver lacks it (rt_gemv_open then does nothing).
+using WriteValue32 = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+WriteValue32 write_value32() {
+    static WriteValue32 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void *f = nullptr;
+        if (cudaGetDriverEntryPointByVersion("cuStreamWriteValue32", &f, 11070, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<WriteValue32>(f);
+    });
+    return fn;
+}
 
 // Errors of the calls that take no struct rt.
 thread_local int t_status = RTB_OK;
@@ -174,6 +201,7 @@ void error_word_text(unsigned h, char *out, size_t n) {
         "a gather index outside the matrix (its y is NaN)",
         "a peer GPU's flag never arrived",
         "a chained round's dependency never completed",
+        "an opened round's x never landed (rt_gemv_open without rt_gemv_go)",
     };
     size_t used = 0;
     out[0] = 0;
@@ -418,10 +446,27 @@ bool chainable(const Ctx *c) {
 
 long long item_tiles(const Item &it) { return (it.rows + (it.kind == K_SILU ? 3 : 7)) / (it.kind == K_SILU ? 4 : 8); }
 
-// One chained launch per <= MAX_CHAIN_JOBS jobs. Round r's jobs count their tiles into d_round[r];
-// a round waits for the latest earlier round of the same launch whose y its x (or, with serial,
-// simply the previous round) overlaps. Rounds in different launches are ordered by the stream.
+// Whether round b (later) must wait for round a (earlier): b reads what a writes (x over a's y),
+// or b writes what a reads or writes (y over a's x or y).
+bool round_conflict(const std::vector<Item> &a, const std::vector<Item> &b) {
+    for (const Item &o : a)
+        for (const Item &it : b) {
+            const size_t xb = size_t(it.t * it.cols) * 4, yb = size_t(it.t * it.rows) * 4;
+            const size_t oxb = size_t(o.t * o.cols) * 4, oyb = size_t(o.t * o.rows) * 4;
+            if (overlaps(it.x, xb, o.y, oyb) || overlaps(it.y, yb, o.x, oxb) || overlaps(it.y, yb, o.y, oyb))
+                return true;
+        }
+    return false;
+}
+
+// One chained launch per <= MAX_CHAIN_JOBS jobs. Round r's jobs count their tiles into d_round[r]
+// and wait (before their first tile) for the earlier rounds of the same launch they conflict
+// with (round_conflict), or with `serial` simply for the previous round. A round finished means
+// its own waits were met, so a wait on round q also covers everything q waited on: the list keeps
+// only the rounds not already covered that way. A round that would still need more than
+// MAX_WAITS waits starts a new launch. Rounds in different launches are ordered by the stream.
 bool run_chain(Ctx *c, bool serial) {
+    using Bits = std::bitset<q8::MAX_CHAIN_JOBS>;
     const size_t nr = c->chain.size();
     size_t r = 0;
     while (r < nr) {
@@ -430,19 +475,27 @@ bool run_chain(Ctx *c, bool serial) {
         p.err = c->d_err;
         const size_t r0 = r;
         std::vector<long long> round_tiles;
+        std::vector<Bits> covered; // per round of this launch: the rounds its finish implies
         for (; r < nr && p.njobs + int(c->chain[r].size()) <= q8::MAX_CHAIN_JOBS; ++r) {
             const size_t lr = r - r0; // round index inside this launch
-            long long tiles = 0;
-            int wait = -1;
-            for (const Item &it : c->chain[r]) {
-                tiles += item_tiles(it);
-                if (serial && lr > 0)
-                    wait = int(lr) - 1;
-                for (size_t q = r0; !serial && q < r; ++q)
-                    for (const Item &o : c->chain[q])
-                        if (overlaps(it.x, size_t(it.t * it.cols) * 4, o.y, size_t(o.t * o.rows) * 4) && int(q - r0) > wait)
-                            wait = int(q - r0);
+            std::vector<int> deps;     // latest first
+            for (size_t q = lr; q-- > 0;)
+                if (serial ? q + 1 == lr : round_conflict(c->chain[r0 + q], c->chain[r]))
+                    deps.push_back(int(q));
+            std::vector<int> waits;
+            Bits cov;
+            for (int q : deps) { // a later round's finish covers the earlier ones it waited on
+                if (cov[size_t(q)])
+                    continue;
+                waits.push_back(q);
+                cov |= covered[size_t(q)];
+                cov.set(size_t(q));
             }
+            if (waits.size() > size_t(q8::MAX_WAITS))
+                break; // this round opens the next launch, after every round before it
+            long long tiles = 0;
+            for (const Item &it : c->chain[r])
+                tiles += item_tiles(it);
             for (const Item &it : c->chain[r]) {
                 q8::GemvJob &j = p.job[p.njobs++];
                 j.w = it.w;
@@ -457,8 +510,11 @@ bool run_chain(Ctx *c, bool serial) {
                 j.cols = int(it.cols);
                 j.m = int(it.t);
                 j.done_ctr = c->d_round + q8::ROUND_CTR_STRIDE * lr;
-                j.wait_ctr = wait >= 0 ? c->d_round + q8::ROUND_CTR_STRIDE * wait : nullptr;
-                j.wait_target = wait >= 0 ? unsigned(round_tiles[size_t(wait)]) : 0u;
+                j.nwait = int(waits.size());
+                for (size_t k = 0; k < waits.size(); ++k) {
+                    j.wait_ctr[k] = c->d_round + q8::ROUND_CTR_STRIDE * size_t(waits[k]);
+                    j.wait_target[k] = unsigned(round_tiles[size_t(waits[k])]);
+                }
                 j.x_written = 0;
                 for (size_t q = 0; q < r && !j.x_written; ++q) // any earlier round of the chain
                     for (const Item &o : c->chain[q])
@@ -466,6 +522,7 @@ bool run_chain(Ctx *c, bool serial) {
                             j.x_written = 1;
             }
             round_tiles.push_back(tiles);
+            covered.push_back(cov);
         }
         if (r == r0) {
             ctx_err(c, RTB_EINVAL, "chain: a round of more than %d products", q8::MAX_CHAIN_JOBS);
@@ -502,6 +559,92 @@ Item make_item(Kind k, const void *w, const void *w2, const int32_t *idx, long l
     it.t = t;
     it.src_rows = rows;
     return it;
+}
+
+// rt_gemv_open: launches the queued round's CUDA-core products now, gated: their weights stream in
+// while the host still prepares x, and their compute waits on the device for the gate to reach this
+// round's number. The link stream first waits for everything already on R's stream (the round's
+// pulls must not overwrite an x an earlier product still reads). Tensor-core products (their
+// pre-pass reads x at once), several GPUs, chains and stream capture (the gate value would be
+// frozen into the graph) keep the plain round: open then does nothing and go runs everything.
+void open_round(Ctx *c) {
+    if (c->round_open || c->chaining || c->world > 1 || c->queue.empty() || !write_value32())
+        return;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(c->stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
+        return;
+    std::vector<q8::GemvJob> jobs;
+    std::vector<Item> rest;
+    for (const Item &it : c->queue) {
+        if (it.t >= TC_MIN_T) {
+            rest.push_back(it);
+            continue;
+        }
+        for (long long k = 0; k < it.t; k += q8::GEMV_MAX_T) {
+            q8::GemvJob j;
+            memset(&j, 0, sizeof j);
+            j.w = it.w;
+            j.w2 = it.kind == K_SILU ? it.w2 : nullptr;
+            j.idx = it.kind == K_ROWS ? it.idx : nullptr;
+            j.x = it.x + k * it.cols;
+            j.ldx = it.cols;
+            j.ldy = it.rows;
+            j.y = it.y + k * it.rows;
+            j.rows = it.rows;
+            j.src_rows = it.kind == K_ROWS ? it.src_rows : it.rows;
+            j.cols = int(it.cols);
+            j.m = int(it.t - k < q8::GEMV_MAX_T ? it.t - k : q8::GEMV_MAX_T);
+            j.x_written = 1; // x lands during the kernel: read it past L1
+            jobs.push_back(j);
+        }
+    }
+    if (jobs.empty())
+        return;
+    if (!cuda_ok(c, cudaEventRecord(c->ev_before, c->stream), "open: event") ||
+        !cuda_ok(c, cudaStreamWaitEvent(c->link, c->ev_before, 0), "open: link stream wait"))
+        return;
+    const unsigned value = c->gate_seq + 1;
+    while (!jobs.empty()) { // one gated launch per token count, as flush_gemv groups them
+        const int m = jobs[0].m;
+        q8::GemvParams p;
+        memset(&p, 0, sizeof p);
+        p.err = c->d_err;
+        p.early = c->overlap ? 1 : 0;
+        p.gate = c->d_gate;
+        p.gate_value = value;
+        std::vector<q8::GemvJob> later;
+        for (const q8::GemvJob &j : jobs) {
+            if (j.m == m && p.njobs < q8::MAX_JOBS)
+                p.job[p.njobs++] = j;
+            else
+                later.push_back(j);
+        }
+        if (!cuda_ok(c, q8::launch_gemv(p, c->num_sms, 0, c->stream, c->overlap), "open: gated launch")) {
+            // the kernels already launched wait for this value: release them now
+            c->gate_seq = value;
+            write_value32()(reinterpret_cast<CUstream>(c->link), reinterpret_cast<CUdeviceptr>(c->d_gate), value, 0);
+            return;
+        }
+        jobs.swap(later);
+    }
+    c->gate_seq = value;
+    c->queue.swap(rest);
+    c->round_open = true;
+}
+
+// rt_gemv_go of an opened round: after the round's pulls on the link stream, the gate takes the
+// round's number (the write is fenced after the copies); R's stream then also waits for the link
+// stream, so whatever follows on it sees the pulled data.
+bool release_gate(Ctx *c) {
+    c->round_open = false;
+    const CUresult r = write_value32()(reinterpret_cast<CUstream>(c->link), reinterpret_cast<CUdeviceptr>(c->d_gate),
+                                       c->gate_seq, 0);
+    if (r != CUDA_SUCCESS) {
+        ctx_err(c, RTB_ECUDA, "rt_gemv_go: cuStreamWriteValue32 failed (%d)", int(r));
+        return false;
+    }
+    return cuda_ok(c, cudaEventRecord(c->ev_link, c->link), "go: event") &&
+           cuda_ok(c, cudaStreamWaitEvent(c->stream, c->ev_link, 0), "go: stream wait");
 }
 
 } // namespace
@@ -591,9 +734,21 @@ int rt_init(struct rt *R, int threads) {
     }
     c->stream = c->own_stream;
     if (cudaMalloc(&c->d_err, sizeof(unsigned)) != cudaSuccess || cudaMemset(c->d_err, 0, sizeof(unsigned)) != cudaSuccess ||
-        cudaMalloc(&c->d_round, sizeof(unsigned) * q8::ROUND_CTR_STRIDE * q8::MAX_CHAIN_JOBS) != cudaSuccess) {
+        cudaMalloc(&c->d_round, sizeof(unsigned) * q8::ROUND_CTR_STRIDE * q8::MAX_CHAIN_JOBS) != cudaSuccess ||
+        cudaMalloc(&c->d_gate, sizeof(unsigned)) != cudaSuccess || cudaMemset(c->d_gate, 0, sizeof(unsigned)) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&c->link, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->ev_before, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->ev_link, cudaEventDisableTiming) != cudaSuccess) {
         // (the chains' round counters: allocated here, so a chain can be captured in a graph)
         cudaFree(c->d_err);
+        cudaFree(c->d_round);
+        cudaFree(c->d_gate);
+        if (c->link)
+            cudaStreamDestroy(c->link);
+        if (c->ev_before)
+            cudaEventDestroy(c->ev_before);
+        if (c->ev_link)
+            cudaEventDestroy(c->ev_link);
         cudaStreamDestroy(c->own_stream);
         delete c;
         return -1;
@@ -610,13 +765,20 @@ void rt_b200_free(struct rt *R) {
     if (!R || !R->chain)
         return;
     Ctx *c = static_cast<Ctx *>(R->chain);
+    if (c->round_open) // release the pre-launched kernel: its results are not wanted
+        release_gate(c);
     cudaStreamSynchronize(c->stream);
+    cudaStreamSynchronize(c->link);
     drop_peers(c);
     if (c->comm)
         nccl().CommDestroy(c->comm);
     cudaFree(c->d_round);
+    cudaFree(c->d_gate);
     cudaFree(c->scratch);
     cudaFree(c->d_err);
+    cudaEventDestroy(c->ev_before);
+    cudaEventDestroy(c->ev_link);
+    cudaStreamDestroy(c->link);
     cudaStreamDestroy(c->own_stream);
     delete c;
     R->chain = nullptr;
@@ -646,7 +808,11 @@ void rt_gemm_q(struct rt *R, const void *w, long rows, long cols, const float *x
         enqueue(c, make_item(K_GEMM, w, nullptr, nullptr, rows, cols, x, t, y));
 }
 
-void rt_gemv_open(struct rt *R) { (void)ctx_of(R); }
+void rt_gemv_open(struct rt *R) {
+    Ctx *c = ctx_of(R);
+    if (c)
+        open_round(c);
+}
 
 void rt_gemv_go(struct rt *R) {
     Ctx *c = ctx_of(R);
@@ -654,13 +820,18 @@ void rt_gemv_go(struct rt *R) {
         return;
     std::vector<Item> items;
     items.swap(c->queue);
-    if (items.empty())
-        return;
-    if (c->chaining) {
-        c->chain.push_back(items);
+    bool ok = true;
+    if (c->round_open) {
+        ok = release_gate(c);
+    } else if (items.empty()) {
         return;
     }
-    if (run_items(c, items))
+    if (c->chaining) {
+        if (!items.empty())
+            c->chain.push_back(items);
+        return;
+    }
+    if (ok && (items.empty() || run_items(c, items)))
         finish(c);
 }
 
@@ -826,7 +997,11 @@ int rt_b200_sync(struct rt *R) {
     Ctx *c = ctx_of(R);
     if (!c)
         return RTB_ENOTINIT;
+    // An open round whose go never came: its kernel gives up on the gate (about a second) and
+    // reports it through the error word; the round is closed either way.
+    c->round_open = false;
     read_error_word(c);
+    cuda_ok(c, cudaStreamSynchronize(c->link), "synchronize the link stream");
     return c->status;
 }
 
@@ -838,7 +1013,10 @@ int rt_b200_pull(struct rt *R, void *dev, const void *host, size_t bytes) {
         ctx_err(c, RTB_EINVAL, "rt_b200_pull: null pointer");
         return RTB_EINVAL;
     }
-    if (bytes && !cuda_ok(c, cudaMemcpyAsync(dev, host, bytes, cudaMemcpyHostToDevice, c->stream), "rt_b200_pull"))
+    // while a round is open its kernel is already on R's stream, waiting for this x: the copy goes
+    // on the link stream, which rt_gemv_go then orders before the gate's release
+    cudaStream_t s = c->round_open ? c->link : c->stream;
+    if (bytes && !cuda_ok(c, cudaMemcpyAsync(dev, host, bytes, cudaMemcpyHostToDevice, s), "rt_b200_pull"))
         return c->status;
     return RTB_OK;
 }

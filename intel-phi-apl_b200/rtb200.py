@@ -215,6 +215,7 @@ class Runtime:
 
     def gemv_open(self) -> None:
         self.lib.rt_gemv_open(self._ref)
+        _check(self)
 
     def gemv_go(self) -> None:
         self.lib.rt_gemv_go(self._ref)
@@ -260,7 +261,8 @@ class Runtime:
             raise RtError(code, "rt_b200_sync")
 
     def pull(self, dev: int, host: int, nbytes: int) -> None:
-        """Host -> device copy of nbytes on the runtime's stream (returns at once)."""
+        """Host -> device copy of nbytes on the runtime's stream, or while a round is open on its
+        link stream (returns at once)."""
         code = self.lib.rt_b200_pull(self._ref, dev, host, nbytes)
         if code:
             _check(self)

@@ -20,6 +20,9 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_PATH = os.path.join(HERE, "libq8oracle.so")
 REF_PATH = os.path.join(HERE, "_ref", "libq8ref.so")
+# The reference's source tree (read only; only oracle/Makefile's `ref` target and the fixture
+# script read it): $REF_ROOT, else a checkout named `reference` beside this repository.
+REF_ROOT = os.environ.get("REF_ROOT") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
 
 _u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
 _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")

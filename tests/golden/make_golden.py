@@ -2,7 +2,8 @@
 
     make -C oracle && python tests/golden/make_golden.py
 
-Needs the reference source tree (its location in REF_ROOT) and oracle/_ref/libq8ref.so, the
+Needs the reference source tree ($REF_ROOT, by default a checkout named `reference` beside this
+repository) and oracle/_ref/libq8ref.so, the
 reference's own host-model kernels compiled from its sources by oracle/Makefile. Writes:
 
 * ref_gates.json -- the reference's golden known answers for the up-conversions, fma and tree
@@ -29,7 +30,7 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 import oracle as O  # noqa: E402
 
-REF_ROOT = os.environ.get("REF_ROOT", "/root/reference")
+REF_ROOT = O.REF_ROOT
 
 # (name, rows, cols, t, seed, weight stream, x stream). rows % 16 == 0 (the reference's form I).
 CASES = [

@@ -1,7 +1,8 @@
 """Chained launches (rt_b200_chain_begin / rt_b200_chain_end, GPU).
 
-A chain runs recorded rounds as one persistent launch; a round that reads an earlier round's y
-waits for it on the device. Each round here feeds the next (x of round r+1 is y of round r, with
+A chain runs recorded rounds as one persistent launch; a round waits on the device for every
+earlier round whose y its x reads, or whose x or y its y overwrites. In the decode-layer tests
+each round feeds the next (x of round r+1 is y of round r, with
 the shapes of a decode layer), so a round that read its x early would read the NaNs the buffers
 start with. Every product is checked bit for bit against the oracle applied to the x the GPU
 actually fed it (the SwiGLU pair within 1e-5, as in test_gpu_products).
@@ -114,3 +115,48 @@ def test_chain_misuse_is_an_error(cuda, rtb):
         with pytest.raises(rtb.RtError):
             rt.chain_begin()
         rt.chain_end()
+
+
+def test_chain_fan_in_waits_for_every_writer(cuda, rtb, oracle):
+    """Round C reads one buffer whose halves rounds A and B write. B finishes first (A's tiles are
+    four stages long and ten CTAs run two of them), so C must wait for both writers, not only the
+    latest: otherwise the CTAs with one A tile read A's last rows before they are written."""
+    ra, rb_, ca, cb = 1264, 784, 16384, 4096  # 158 and 98 eight-row tiles
+    a = Mat(cuda, rtb, oracle, ra, ca, 81)
+    b = Mat(cuda, rtb, oracle, rb_, cb, 82)
+    cm = Mat(cuda, rtb, oracle, 512, ra + rb_, 83)
+    xa, xb = dev(cuda, xs(oracle, 1, ca, 84)), dev(cuda, xs(oracle, 1, cb, 85))
+    ybuf = cuda.full((ra + rb_,), float("nan"), device="cuda")
+    yc = cuda.full((512,), float("nan"), device="cuda")
+    with rtb.Runtime() as rt:
+        rt.chain_begin()
+        rt.gemv(a.ptr, ra, ca, xa.data_ptr(), ybuf.data_ptr())
+        rt.gemv(b.ptr, rb_, cb, xb.data_ptr(), ybuf.data_ptr() + 4 * ra)
+        rt.gemv(cm.ptr, 512, ra + rb_, ybuf.data_ptr(), yc.data_ptr())
+        rt.chain_end(serial=False)
+    y = ybuf.cpu().numpy()
+    assert bits_equal(y[:ra], oracle.gemv(a.q8, ra, ca, xa.cpu().numpy()[0]))
+    assert bits_equal(y[ra:], oracle.gemv(b.q8, rb_, cb, xb.cpu().numpy()[0]))
+    assert bits_equal(yc.cpu().numpy(), oracle.gemv(cm.q8, 512, ra + rb_, y))
+
+
+def test_chain_write_after_read_waits_for_the_reader(cuda, rtb, oracle):
+    """Round R writes into the last 4096 columns of round Q's x. Q's tiles are eight stages long
+    and 74 CTAs run two of them, reading that part of x last; the other CTAs reach R after one Q
+    tile. R must wait for Q, or Q's late tiles read R's output instead of their x."""
+    rq, cq, rr, cr = 1776, 32768, 4096, 4096  # Q: 222 eight-row tiles of 8 stages
+    qm = Mat(cuda, rtb, oracle, rq, cq, 91)
+    rm = Mat(cuda, rtb, oracle, rr, cr, 92)
+    x_host = xs(oracle, 1, cq, 93)[0]
+    xq = dev(cuda, x_host)
+    xr = dev(cuda, xs(oracle, 1, cr, 94))
+    yq = cuda.full((rq,), float("nan"), device="cuda")
+    with rtb.Runtime() as rt:
+        rt.chain_begin()
+        rt.gemv(qm.ptr, rq, cq, xq.data_ptr(), yq.data_ptr())
+        rt.gemv(rm.ptr, rr, cr, xr.data_ptr(), xq.data_ptr() + 4 * (cq - rr))
+        rt.chain_end(serial=False)
+    assert bits_equal(yq.cpu().numpy(), oracle.gemv(qm.q8, rq, cq, x_host))
+    x_after = xq.cpu().numpy()
+    assert bits_equal(x_after[:cq - rr], x_host[:cq - rr])
+    assert bits_equal(x_after[cq - rr:], oracle.gemv(rm.q8, rr, cr, xr.cpu().numpy()[0]))

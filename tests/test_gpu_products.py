@@ -170,6 +170,74 @@ def test_round_through_host_buffers(cuda, runtime, rtb, oracle):
         runtime.push(hy.data_ptr(), 0, 4 * rows)
 
 
+@pytest.mark.parametrize("blocking", [False, True])
+def test_opened_round(cuda, rtb, oracle, blocking):
+    """The reference's opened round (src/card/rt.c:267-285, placed by src/apl/compiler/em.apl:
+    1014-1046): products queued, rt_gemv_open before x has landed (the CUDA-core products are
+    launched and stream their weights, their compute gated on the device), x pulled from pinned
+    host memory, rt_gemv_go, y pushed back. A plain gemv, a SwiGLU pair, a row gather, a 2-token
+    gemm and a 16-token tensor-core gemm (launched at go) in one round, over three rounds."""
+    cols = 4096
+    a = Mat(cuda, rtb, oracle, 8192, cols, 191)
+    g = Mat(cuda, rtb, oracle, 512, cols, 192)
+    u = Mat(cuda, rtb, oracle, 512, cols, 193)
+    idx = np.array([8191, 0, 4000, 17, 17], dtype=np.int32)
+    idx_d = dev(cuda, idx)
+    xd = cuda.empty((16, cols), dtype=cuda.float32, device="cuda")
+    ya = cuda.empty(8192, dtype=cuda.float32, device="cuda")
+    h = cuda.empty(512, dtype=cuda.float32, device="cuda")
+    yr = cuda.empty(5, dtype=cuda.float32, device="cuda")
+    y2 = cuda.empty((2, 8192), dtype=cuda.float32, device="cuda")
+    y16 = cuda.empty((16, 8192), dtype=cuda.float32, device="cuda")
+    hy = cuda.zeros(8192, dtype=cuda.float32).pin_memory()
+    with rtb.Runtime() as rt:
+        rt.set_async(not blocking)
+        for k in range(3):
+            x = xs(oracle, 16, cols, 194 + k)
+            hx = cuda.from_numpy(x).pin_memory()
+            rt.gemv_q(a.ptr, 8192, cols, xd.data_ptr(), ya.data_ptr())
+            rt.gemm_silu_q(g.ptr, u.ptr, 512, cols, xd.data_ptr(), 1, h.data_ptr())
+            rt.gemv_rows_q(a.ptr, 8192, idx_d.data_ptr(), 5, cols, xd.data_ptr(), yr.data_ptr())
+            rt.gemm_q(a.ptr, 8192, cols, xd.data_ptr(), 2, y2.data_ptr())
+            rt.gemm_q(a.ptr, 8192, cols, xd.data_ptr(), 16, y16.data_ptr())
+            rt.gemv_open()
+            rt.pull(xd.data_ptr(), hx.data_ptr(), 4 * 16 * cols)
+            rt.gemv_go()
+            rt.push(hy.data_ptr(), ya.data_ptr(), 4 * 8192)
+            want = oracle.gemm(a.q8, 8192, cols, x, 16)
+            assert bits_equal(hy.numpy(), want[0])
+            assert bits_equal(ya.cpu().numpy(), want[0])
+            assert bits_equal(yr.cpu().numpy(), want[0][idx])
+            assert bits_equal(y2.cpu().numpy(), want[:2])
+            assert rel_err(y16.cpu().numpy(), want) < TC_TOL
+            yg = oracle.gemv(g.q8, 512, cols, x[0]).astype(np.float64)
+            yu = oracle.gemv(u.q8, 512, cols, x[0]).astype(np.float64)
+            assert rel_err(h.cpu().numpy(), yg / (1 + np.exp(-yg)) * yu) < 1e-5
+
+
+def test_opened_round_without_go_gives_up_and_recovers(cuda, rtb, oracle):
+    """An opened round whose go never comes: the pre-launched kernel's wait for its x gives up
+    after about a second and reports it (RTB_EKERNEL, naming the missing go); the runtime then
+    runs the next round bit for bit. No GPU fault: the wait is bounded."""
+    rows, cols = 1024, 4096
+    m = Mat(cuda, rtb, oracle, rows, cols, 201)
+    x = xs(oracle, 1, cols, 202)
+    xd = dev(cuda, x)
+    y = cuda.full((rows,), float("nan"), dtype=cuda.float32, device="cuda")
+    with rtb.Runtime() as rt:
+        rt.set_async(True)
+        rt.gemv_q(m.ptr, rows, cols, xd.data_ptr(), y.data_ptr())
+        rt.gemv_open()
+        with pytest.raises(rtb.RtError) as e:
+            rt.sync()
+        assert e.value.code == 3 and "never landed" in str(e.value), str(e.value)
+        rt.set_async(False)
+        rt.gemv_q(m.ptr, rows, cols, xd.data_ptr(), y.data_ptr())
+        rt.gemv_open()
+        rt.gemv_go()
+        assert bits_equal(y.cpu().numpy(), oracle.gemv(m.q8, rows, cols, x[0]))
+
+
 def test_gemv_output_head_full_size(cuda, runtime, rtb, oracle):
     """BASELINE config 2's output head, 151936 x 4096, every output bit for bit."""
     rows, cols = 151936, 4096
@@ -188,6 +256,20 @@ def test_gemv_output_head_full_size(cuda, runtime, rtb, oracle):
 def test_gemm_small_t_bit_exact(cuda, runtime, rtb, oracle, t, rows, cols):
     m = Mat(cuda, rtb, oracle, rows, cols, 21)
     x = xs(oracle, t, cols, 22)
+    xd = dev(cuda, x)
+    y = cuda.full((t, rows), float("nan"), dtype=cuda.float32, device="cuda")
+    runtime.gemm(m.ptr, rows, cols, xd.data_ptr(), t, y.data_ptr())
+    assert bits_equal(y.cpu().numpy(), oracle.gemm(m.q8, rows, cols, x, t))
+
+
+@pytest.mark.parametrize("t", [2, 3, 4])
+def test_gemm_wide_rows_many_tiles_per_cta(cuda, runtime, rtb, oracle, t):
+    """Rows of four 4096-column chunks, 3-4 row tiles per CTA: the two chain warps take alternate
+    tiles, each tile as long as the ring of partial-sum buffers (so each chain warp skips a whole
+    ring's worth of the other's stages between its own). Bit for bit."""
+    rows, cols = 4096, 16384
+    m = Mat(cuda, rtb, oracle, rows, cols, 25)
+    x = xs(oracle, t, cols, 26)
     xd = dev(cuda, x)
     y = cuda.full((t, rows), float("nan"), dtype=cuda.float32, device="cuda")
     runtime.gemm(m.ptr, rows, cols, xd.data_ptr(), t, y.data_ptr())
@@ -449,3 +531,118 @@ def test_dependent_chain_async(cuda, rtb, oracle, overlap):
         assert rel_err(ys[1].cpu().numpy(), oracle.gemm(b.q8, rows, cols, y0, 16)) < TC_TOL
     finally:
         rt.close()
+
+
+# ---------------------------------------------------------------- tensor cores: any fp32 x, any fp16 scale
+
+def _banded_q8(oracle, bands, cols, stream):
+    """GGUF Q8_0 rows in bands of different weight scales, [(rows, sigma), ...]."""
+    return np.concatenate([oracle.synth_q8_0(r, cols, SEED, stream + 7 * k, sigma=s) for k, (r, s) in enumerate(bands)])
+
+
+def _worst_block_err(got, ref, cuts):
+    """rel_err per (token, row band), each with its own rms floor: a band of tiny weights is held to
+    the same 2e-3 as the others instead of hiding under their magnitude."""
+    return max(rel_err(got[k, a:b], ref[k, a:b]) for k in range(got.shape[0]) for a, b in zip(cuts[:-1], cuts[1:]))
+
+
+@pytest.mark.parametrize("t,cols", [(16, 4096), (40, 4096), (100, 4096), (24, 12288)])
+def test_tensor_cores_take_any_fp32_range(cuda, runtime, rtb, oracle, t, cols):
+    """The reference takes any fp32 x and any fp16 scale (src/card/gemm.c:271-294). Rows whose
+    scales are ~2e-7 (fp16 subnormals: q*d underflows fp16) or ~2000 (q*d overflows it) sit in the
+    same tiles as ordinary rows, and tokens hold entries of +-1e5 (beyond fp16), values ~1e-6
+    (fp16 subnormals) or ~1e4 throughout. Each (token, row band) is within 2e-3 of the reference's
+    fp32 y. (cols = 12288 with few row tiles: the K range is split, partial sums reduced.)"""
+    bands = [(160, 0.02), (96, 1e-5), (64, 1e5), (200, 0.02), (33, 3e-6)]
+    rows = sum(r for r, _ in bands)
+    cuts = np.cumsum([0] + [r for r, _ in bands])
+    q8 = _banded_q8(oracle, bands, cols, 161)
+    w = dev(cuda, oracle.repack_split(q8, rows, cols))
+    x = xs(oracle, t, cols, 162)
+    x[0, ::97] = 1e5
+    x[1, 5] = -1e5
+    x[2] *= 1e-6
+    x[3] *= 1e4
+    x[4, :] = 0.0
+    xd = dev(cuda, x)
+    y = cuda.full((t, rows), float("nan"), dtype=cuda.float32, device="cuda")
+    runtime.gemm(w.data_ptr(), rows, cols, xd.data_ptr(), t, y.data_ptr())
+    got = y.cpu().numpy()
+    want = oracle.gemm(q8, rows, cols, x, t)
+    assert np.isfinite(got).all()
+    assert np.array_equal(got[4], np.zeros(rows, dtype=np.float32))
+    assert _worst_block_err(got, want, cuts) < TC_TOL
+
+
+def test_tensor_core_swiglu_takes_any_fp32_range(cuda, runtime, rtb, oracle):
+    """The SwiGLU pair with gate and up rows of very different scales and x with outliers."""
+    t, cols = 16, 4096
+    gate_bands, up_bands = [(64, 0.02), (64, 1e-5)], [(64, 1e3), (64, 0.02)]
+    rows = 128
+    gq, uq = _banded_q8(oracle, gate_bands, cols, 171), _banded_q8(oracle, up_bands, cols, 172)
+    g, u = dev(cuda, oracle.repack_split(gq, rows, cols)), dev(cuda, oracle.repack_split(uq, rows, cols))
+    x = xs(oracle, t, cols, 173)
+    x[0, 11] = 3e4
+    x[1] *= 1e-6
+    xd = dev(cuda, x)
+    h = cuda.full((t, rows), float("nan"), dtype=cuda.float32, device="cuda")
+    runtime.gemm_silu(g.data_ptr(), u.data_ptr(), rows, cols, xd.data_ptr(), t, h.data_ptr())
+    yg = oracle.gemm(gq, rows, cols, x, t).astype(np.float64)
+    yu = oracle.gemm(uq, rows, cols, x, t).astype(np.float64)
+    got = h.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert _worst_block_err(got, yg / (1.0 + np.exp(-yg)) * yu, [0, 64, 128]) < 2 * TC_TOL
+
+
+# ---------------------------------------------------------------- BASELINE configs 3a and 4 at their own shapes
+
+CONFIG_SHAPES = {"qkv": (8192, 4096), "out": (4096, 4096), "down": (4096, 12288), "head": (151936, 4096)}
+
+
+def _row_sample(rows: int, n: int = 96, seed: int = 5) -> np.ndarray:
+    """A seeded sample of output rows plus both ends of the matrix (the first and last row tiles)."""
+    sel = set(np.random.default_rng(seed).choice(rows, n, replace=False).tolist()) | {0, 1, rows - 2, rows - 1}
+    return np.array(sorted(sel))
+
+
+def _sample_q8(oracle, sel, cols, stream):
+    return np.concatenate([oracle.synth_q8_0(1, cols, SEED, stream, row0=int(r)) for r in sel])
+
+
+@pytest.mark.parametrize("t", [2, 4, 16, 40])
+@pytest.mark.parametrize("shape", ["qkv", "out", "down", "head"])
+def test_config_shapes_on_a_row_sample(cuda, runtime, rtb, oracle, shape, t):
+    """The verify pass (M = 2, config 3a), M = 4, and the prompt products at M = 16 and 40 (config
+    4) on the full BASELINE matrices, the 151936 x 4096 head included: the sampled rows bit for bit
+    below 16 tokens, within 2e-3 from 16 (the two-CTA tensor-core shape)."""
+    rows, cols = CONFIG_SHAPES[shape]
+    m = Mat(cuda, rtb, oracle, rows, cols, 151, host=False)
+    x = xs(oracle, t, cols, 152)
+    xd = dev(cuda, x)
+    y = cuda.full((t, rows), float("nan"), dtype=cuda.float32, device="cuda")
+    runtime.gemm(m.ptr, rows, cols, xd.data_ptr(), t, y.data_ptr())
+    got = y.cpu().numpy()
+    assert np.isfinite(got).all()
+    sel = _row_sample(rows)
+    want = oracle.gemm(_sample_q8(oracle, sel, cols, 151), len(sel), cols, x, t)
+    if t < TC_MIN_T:
+        assert bits_equal(got[:, sel], want)
+    else:
+        assert rel_err(got[:, sel], want) < TC_TOL
+
+
+@pytest.mark.parametrize("t", [1, 2, 16, 40])
+def test_gate_up_config_shape_on_a_row_sample(cuda, runtime, rtb, oracle, t):
+    """The fused gate+up+SiLU pair at its BASELINE shape (2 x 12288 x 4096) on a row sample."""
+    rows, cols = 12288, 4096
+    g = Mat(cuda, rtb, oracle, rows, cols, 181, host=False)
+    u = Mat(cuda, rtb, oracle, rows, cols, 182, host=False)
+    x = xs(oracle, t, cols, 183)
+    xd = dev(cuda, x)
+    h = cuda.full((t, rows), float("nan"), dtype=cuda.float32, device="cuda")
+    runtime.gemm_silu(g.ptr, u.ptr, rows, cols, xd.data_ptr(), t, h.data_ptr())
+    sel = _row_sample(rows)
+    yg = oracle.gemm(_sample_q8(oracle, sel, cols, 181), len(sel), cols, x, t).astype(np.float64)
+    yu = oracle.gemm(_sample_q8(oracle, sel, cols, 182), len(sel), cols, x, t).astype(np.float64)
+    tol = 1e-5 if t < TC_MIN_T else 2 * TC_TOL
+    assert rel_err(h.cpu().numpy()[:, sel], yg / (1.0 + np.exp(-yg)) * yu) < tol

@@ -118,6 +118,24 @@ def test_file_sum_is_position_weighted(tmp_path):
     assert G.file_sum(str(p)) == 2 * 1 + 1 * 3  # the order counts
 
 
+def test_load_gguf_refuses_a_mis_tied_matrix(rtb, oracle, tmp_path):
+    """A tensor sharing a repacked Q8_0 matrix's bytes with other dims (a crafted or mis-tied file):
+    the in-place repack would rewrite bytes the other tensor reads, so the load refuses the file
+    before it reads anything or touches the arena (no GPU needed: the arena address is never used)."""
+    import ctypes as C
+    p = str(tmp_path / "mistied.gguf")
+    q8 = oracle.synth_q8_0(300, 4096, SEED, 86).tobytes()
+    G.write_gguf(p, [("token_embd.weight", G.GGML_Q8_0, [4096, 300], q8),
+                     ("output.weight", G.GGML_Q8_0, [4096, 200], b"")],
+                 shared={"output.weight": "token_embd.weight"})
+    lib = rtb.load()
+    arr = (rtb.Tensor * 2)()
+    n, st = C.c_int(0), rtb.LoadStats()
+    code = lib.rt_b200_load_gguf(None, p.encode(), 1 << 30, 1 << 40, arr, 2, C.byref(n), C.byref(st))
+    assert code == 1  # RTB_EINVAL
+    assert b"share bytes" in lib.rtb_load_error()
+
+
 @pytest.mark.gpu
 def test_load_gguf_into_hbm(cuda, rtb, oracle, synth_file):
     path, mats, norm, offs = synth_file

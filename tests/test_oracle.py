@@ -16,6 +16,7 @@ import os
 import numpy as np
 import pytest
 
+import oracle as O
 from conftest import GOLDEN
 
 
@@ -132,7 +133,7 @@ def test_gather_and_gemm_port(oracle):
     assert np.array_equal(Y[0].view(np.uint32), y.view(np.uint32))
 
 
-@pytest.mark.skipif(not os.path.exists("/root/reference/src/card/gemv.c"), reason="reference tree absent")
+@pytest.mark.skipif(not os.path.exists(os.path.join(O.REF_ROOT, "src/card/gemv.c")), reason="reference tree absent")
 def test_port_against_live_reference(oracle):
     """Where the reference tree is present: its compiled host model, live, on fresh shapes."""
     import subprocess

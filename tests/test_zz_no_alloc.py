@@ -4,8 +4,10 @@ Some engines reserve all of HBM up front or forbid allocation while serving, so 
 the library cudaMalloc the scratch its tensor-core path needs (the fp16 copy of x). rt_gemm_static
 runs the same kernel with that scratch in a fixed device array inside the library. These tests
 call it through the C ABI and hold it to the ordinary entry point (rt_gemm at t >= 16) within the
-tensor-core tolerance, on two calls in a row, and check that it refuses sizes beyond its limit.
-This file is collected last on purpose.
+tensor-core tolerance, on two calls in a row, and to the CPU oracle (the reference's rounding
+order in fp32) within the same tolerance; and check that it refuses sizes beyond its limits.
+This file is collected last on purpose: if it fails, a run that stops at the first failure has
+already run every other test.
 """
 from __future__ import annotations
 
@@ -17,6 +19,7 @@ pytestmark = pytest.mark.gpu
 SEED = 20261201
 TC_TOL = 2e-3
 STATIC_LIMIT = 4 * 1024 * 1024  # t * cols: the 8 MiB fp16 copy of x
+STATIC_ROWS = 1024 * 1024       # rows: one scale exponent byte per row
 
 
 def rel_err(y, ref) -> float:
@@ -54,6 +57,21 @@ def test_static_gemm_matches_rt_gemm_two_calls(cuda, runtime, rtb):
         assert rel_err(got, want) < TC_TOL
 
 
+def test_static_gemm_matches_the_oracle(cuda, rtb, oracle):
+    """Against the CPU oracle (the reference's fp32 rounding order) rather than the library itself."""
+    lib = rtb.load()
+    rows, cols, t = 1024, 4096, 48
+    q8 = oracle.synth_q8_0(rows, cols, SEED, 211)
+    w = cuda.from_numpy(oracle.repack_split(q8, rows, cols)).cuda()
+    x = np.stack([oracle.synth_f32(cols, SEED, 212 + k) for k in range(t)]).astype(np.float32)
+    xd = cuda.from_numpy(x).cuda()
+    for _ in range(2):
+        y = cuda.full((t, rows), float("nan"), dtype=cuda.float32, device="cuda")
+        cuda.cuda.synchronize()
+        assert lib.rt_gemm_static(w.data_ptr(), rows, cols, xd.data_ptr(), t, y.data_ptr(), None) == 0
+        assert rel_err(y.cpu().numpy(), oracle.gemm(q8, rows, cols, x, t)) < TC_TOL
+
+
 def test_static_gemm_refuses_what_it_cannot_hold(cuda, runtime, rtb):
     lib = rtb.load()
     rows, cols = 256, 8192
@@ -64,6 +82,8 @@ def test_static_gemm_refuses_what_it_cannot_hold(cuda, runtime, rtb):
     assert lib.rt_gemm_static(w.data_ptr(), rows, cols, x.data_ptr(), t_over, y.data_ptr(), None) == 1
     assert lib.rt_gemm_static(w.data_ptr(), rows, cols, x.data_ptr(), 8, y.data_ptr(), None) == 1  # t < 16
     assert lib.rt_gemm_static(w.data_ptr(), rows, 33, x.data_ptr(), 16, y.data_ptr(), None) == 1
+    # more rows than the exponent bytes hold (checked before anything is read)
+    assert lib.rt_gemm_static(w.data_ptr(), STATIC_ROWS + 1, cols, x.data_ptr(), 16, y.data_ptr(), None) == 1
     # at the limit it runs
     t_max = STATIC_LIMIT // cols
     assert lib.rt_gemm_static(w.data_ptr(), rows, cols, x.data_ptr(), t_max, y.data_ptr(), None) == 0
