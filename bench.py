@@ -373,7 +373,8 @@ class Bench:
         import ctypes as C
         torch, rt = self.torch, self.rt
         rt.set_async(True)
-        rt.set_stream(torch.cuda.current_stream().cuda_stream)
+        rt.set_stream(None)  # the runtime's own stream, as a C engine uses it
+        torch.cuda.synchronize()
         hx = {k: v.cpu().pin_memory() for k, v in self.x.items() if k[1] == 1}
         hy = {k: torch.empty(v.numel(), dtype=torch.float32).pin_memory() for k, v in self.y.items() if k[1] == 1}
         xd, xf = self.x[("d", 1)], self.x[("ff", 1)]

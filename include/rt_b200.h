@@ -102,6 +102,23 @@ RTB_API long gemv_s_bytes(long rows, long cols);
  * Returns 0 or an RTB_E* code. Replaces gemv_i_repack (src/card/gemv.h:55). */
 RTB_API int gemv_s_repack(const void *q8, long rows, long cols, void *out);
 
+/* The reference's load-side names (src/card/gemv.h:51-67), so the engine's load site
+ * (src/card/engine.c:295-316) links unchanged: they produce this library's row-split layout
+ * under the old names. gemv_i_bytes = gemv_s_bytes. gemv_i_repack = gemv_s_repack (void, as in
+ * the reference; a failure is recorded for rt_b200_last_error(NULL)). gemv_i_repack_thread is a
+ * team body, as the engine runs it (team_run(R.team, gemv_i_repack_thread, &job) on n threads):
+ * thread 0 repacks the whole matrix in place on the GPU (job->w a device pointer, cols % 256 == 0,
+ * so a row keeps its length) and returns when it is done; the other threads return at once, and
+ * job->tmp (the reference's per-thread scratch) is not used. */
+struct gemv_repack_job {
+    void *w;
+    long rows, cols;
+    void *tmp;
+};
+RTB_API long gemv_i_bytes(long rows, long cols);
+RTB_API void gemv_i_repack(const uint8_t *q8, long rows, long cols, void *out);
+RTB_API void gemv_i_repack_thread(void *arg, int tid, int n);
+
 /* ---------------------------------------------------------------- fused products
  * The reference runs these as separate queued gemvs plus host work (src/apl/qwen35.apl:124-126,
  * 170-172; src/apl/compiler/em.apl:820-840). Here each is one pass in the queued round. */
@@ -197,6 +214,11 @@ RTB_API void rt_b200_free(struct rt *R);
 RTB_API int rt_b200_nccl_id(void *out128);
 RTB_API int rt_b200_shard(struct rt *R, int rank, int world, const void *nccl_id);
 RTB_API int rt_b200_peer_gather(struct rt *R);
+
+/* The rows of a rows-row matrix that rank `rank` of `world` holds and computes, as the products
+ * split them: *row0 and *n (rows / world consecutive rows, rank-major). Host only, no device: an
+ * engine loads each matrix's shard with it. 0, or RTB_EINVAL (rows % world != 0, bad rank). */
+RTB_API int rt_b200_shard_rows(long rows, int rank, int world, long *row0, long *n);
 
 /* A self-test of the failure path: one kernel on R's stream waits, bounded, on a device counter
  * that nothing advances and then on an mbarrier that nothing arrives on, the two kinds of wait the

@@ -99,9 +99,15 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
 __device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void grid_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// The error word: err[0] the bits; at err + 2 (8-byte aligned) a pointer, or null, to a word in
+// mapped host memory that is set to 1 as well, so the host learns of an error without a copy.
 __device__ __forceinline__ void report(unsigned *err, unsigned bits) {
-    if (err)
+    if (err) {
         atomicOr(err, bits);
+        unsigned *mirror = *reinterpret_cast<unsigned *const volatile *>(err + 2);
+        if (mirror)
+            *reinterpret_cast<volatile unsigned *>(mirror) = 1u;
+    }
 }
 
 }  // namespace q8

@@ -81,7 +81,9 @@ struct Ctx {
     cudaStream_t own_stream = nullptr, stream = nullptr;
     bool async = false;
     bool overlap = false; // weights are read-only between products: prefetch them early (PDL)
-    unsigned *d_err = nullptr;
+    unsigned *d_err = nullptr;        // the error word (q8_ptx.cuh: bits, then the mirror's address)
+    volatile unsigned *h_err = nullptr; // its mirror in mapped host memory: nonzero once a kernel reported
+    bool synced = true;               // own stream, nothing enqueued on it since its last synchronize
     int status = RTB_OK;
     char msg[256] = {0};
     std::vector<Item> queue;
@@ -212,17 +214,24 @@ void error_word_text(unsigned h, char *out, size_t n) {
         }
 }
 
+// Waits for R's stream and reads the kernels' error word: its host mirror first (no copy), the
+// bits only when it is set.
 bool read_error_word(Ctx *c) {
-    unsigned h = 0;
-    if (!cuda_ok(c, cudaMemcpyAsync(&h, c->d_err, sizeof h, cudaMemcpyDeviceToHost, c->stream), "read error word"))
-        return false;
     if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "synchronize"))
         return false;
+    c->synced = c->stream == c->own_stream;
+    if (!*c->h_err)
+        return true;
+    unsigned h = 0;
+    if (!cuda_ok(c, cudaMemcpy(&h, c->d_err, sizeof h, cudaMemcpyDeviceToHost), "read error word"))
+        return false;
+    *c->h_err = 0;
     if (h) {
         char what[200];
         error_word_text(h, what, sizeof what);
         ctx_err(c, RTB_EKERNEL, "kernel error word 0x%x: %s", h, what);
         cuda_ok(c, cudaMemsetAsync(c->d_err, 0, sizeof(unsigned), c->stream), "clear error word");
+        c->synced = false;
         return false;
     }
     return true;
@@ -234,11 +243,14 @@ bool finish(Ctx *c) {
     return read_error_word(c);
 }
 
-// The output rows this rank computes of a product with `rows` rows, and where they start.
-void shard_rows(const Ctx *c, long long rows, long long *lr, long long *r0) {
-    *lr = rows / c->world;
-    *r0 = (long long)c->rank * *lr;
+// The output rows rank `rank` of `world` computes of a product with `rows` rows, and where they
+// start: rows / world consecutive rows, rank-major (rows % world == 0, checked by the callers).
+void split_rows(long long rows, int rank, int world, long long *lr, long long *r0) {
+    *lr = rows / world;
+    *r0 = (long long)rank * *lr;
 }
+
+void shard_rows(const Ctx *c, long long rows, long long *lr, long long *r0) { split_rows(rows, c->rank, c->world, lr, r0); }
 
 // One CUDA-core launch per group of jobs with the same token count.
 bool flush_gemv(Ctx *c, std::vector<q8::GemvJob> &jobs) {
@@ -338,6 +350,7 @@ bool run_peer_gathered(Ctx *c, const Item &it) {
 // Splits the items into kernel jobs (t >= 16: one tensor-core job; else passes of <= 4 tokens on
 // CUDA cores), launches them, then all-gathers the sharded outputs.
 bool run_items(Ctx *c, const std::vector<Item> &items) {
+    c->synced = false;
     if (peer_gatherable(c, items))
         return run_peer_gathered(c, items[0]);
     std::vector<q8::GemvJob> jobs;
@@ -467,6 +480,7 @@ bool round_conflict(const std::vector<Item> &a, const std::vector<Item> &b) {
 // MAX_WAITS waits starts a new launch. Rounds in different launches are ordered by the stream.
 bool run_chain(Ctx *c, bool serial) {
     using Bits = std::bitset<q8::MAX_CHAIN_JOBS>;
+    c->synced = false;
     const size_t nr = c->chain.size();
     size_t r = 0;
     while (r < nr) {
@@ -600,9 +614,11 @@ void open_round(Ctx *c) {
     }
     if (jobs.empty())
         return;
-    if (!cuda_ok(c, cudaEventRecord(c->ev_before, c->stream), "open: event") ||
-        !cuda_ok(c, cudaStreamWaitEvent(c->link, c->ev_before, 0), "open: link stream wait"))
+    // (R's own stream, synchronized since its last work: nothing there can still read an x)
+    if (!c->synced && (!cuda_ok(c, cudaEventRecord(c->ev_before, c->stream), "open: event") ||
+                       !cuda_ok(c, cudaStreamWaitEvent(c->link, c->ev_before, 0), "open: link stream wait")))
         return;
+    c->synced = false;
     const unsigned value = c->gate_seq + 1;
     while (!jobs.empty()) { // one gated launch per token count, as flush_gemv groups them
         const int m = jobs[0].m;
@@ -635,7 +651,7 @@ void open_round(Ctx *c) {
 // rt_gemv_go of an opened round: after the round's pulls on the link stream, the gate takes the
 // round's number (the write is fenced after the copies); R's stream then also waits for the link
 // stream, so whatever follows on it sees the pulled data.
-bool release_gate(Ctx *c) {
+bool release_gate(Ctx *c, bool more) {
     c->round_open = false;
     const CUresult r = write_value32()(reinterpret_cast<CUstream>(c->link), reinterpret_cast<CUdeviceptr>(c->d_gate),
                                        c->gate_seq, 0);
@@ -643,8 +659,10 @@ bool release_gate(Ctx *c) {
         ctx_err(c, RTB_ECUDA, "rt_gemv_go: cuStreamWriteValue32 failed (%d)", int(r));
         return false;
     }
-    return cuda_ok(c, cudaEventRecord(c->ev_link, c->link), "go: event") &&
-           cuda_ok(c, cudaStreamWaitEvent(c->stream, c->ev_link, 0), "go: stream wait");
+    // With nothing more to launch, what follows on R's stream comes after the gated kernel, which
+    // read x only after the gate, itself written after the pulls: R needs no wait of its own.
+    return !more || (cuda_ok(c, cudaEventRecord(c->ev_link, c->link), "go: event") &&
+                     cuda_ok(c, cudaStreamWaitEvent(c->stream, c->ev_link, 0), "go: stream wait"));
 }
 
 } // namespace
@@ -733,7 +751,19 @@ int rt_init(struct rt *R, int threads) {
         return -1;
     }
     c->stream = c->own_stream;
-    if (cudaMalloc(&c->d_err, sizeof(unsigned)) != cudaSuccess || cudaMemset(c->d_err, 0, sizeof(unsigned)) != cudaSuccess ||
+    unsigned *h_err = nullptr, *h_err_dev = nullptr;
+    if (cudaHostAlloc(&h_err, sizeof(unsigned), cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostGetDevicePointer(&h_err_dev, h_err, 0) != cudaSuccess) {
+        if (h_err)
+            cudaFreeHost(h_err);
+        cudaStreamDestroy(c->own_stream);
+        delete c;
+        return -1;
+    }
+    *h_err = 0;
+    c->h_err = h_err;
+    if (cudaMalloc(&c->d_err, 16) != cudaSuccess || cudaMemset(c->d_err, 0, 16) != cudaSuccess ||
+        cudaMemcpy(c->d_err + 2, &h_err_dev, sizeof h_err_dev, cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMalloc(&c->d_round, sizeof(unsigned) * q8::ROUND_CTR_STRIDE * q8::MAX_CHAIN_JOBS) != cudaSuccess ||
         cudaMalloc(&c->d_gate, sizeof(unsigned)) != cudaSuccess || cudaMemset(c->d_gate, 0, sizeof(unsigned)) != cudaSuccess ||
         cudaStreamCreateWithFlags(&c->link, cudaStreamNonBlocking) != cudaSuccess ||
@@ -749,6 +779,7 @@ int rt_init(struct rt *R, int threads) {
             cudaEventDestroy(c->ev_before);
         if (c->ev_link)
             cudaEventDestroy(c->ev_link);
+        cudaFreeHost(h_err);
         cudaStreamDestroy(c->own_stream);
         delete c;
         return -1;
@@ -766,7 +797,7 @@ void rt_b200_free(struct rt *R) {
         return;
     Ctx *c = static_cast<Ctx *>(R->chain);
     if (c->round_open) // release the pre-launched kernel: its results are not wanted
-        release_gate(c);
+        release_gate(c, false);
     cudaStreamSynchronize(c->stream);
     cudaStreamSynchronize(c->link);
     drop_peers(c);
@@ -780,6 +811,7 @@ void rt_b200_free(struct rt *R) {
     cudaEventDestroy(c->ev_link);
     cudaStreamDestroy(c->link);
     cudaStreamDestroy(c->own_stream);
+    cudaFreeHost(const_cast<unsigned *>(c->h_err));
     delete c;
     R->chain = nullptr;
 }
@@ -822,7 +854,7 @@ void rt_gemv_go(struct rt *R) {
     items.swap(c->queue);
     bool ok = true;
     if (c->round_open) {
-        ok = release_gate(c);
+        ok = release_gate(c, !items.empty());
     } else if (items.empty()) {
         return;
     }
@@ -963,6 +995,22 @@ int gemv_s_repack(const void *q8, long rows, long cols, void *out) {
     return RTB_OK;
 }
 
+long gemv_i_bytes(long rows, long cols) { return gemv_s_bytes(rows, cols); }
+
+void gemv_i_repack(const uint8_t *q8, long rows, long cols, void *out) { (void)gemv_s_repack(q8, rows, cols, out); }
+
+void gemv_i_repack_thread(void *arg, int tid, int n) {
+    (void)n;
+    if (tid != 0)
+        return;
+    const gemv_repack_job *j = static_cast<const gemv_repack_job *>(arg);
+    if (!j) {
+        thread_err(RTB_EINVAL, "gemv_i_repack_thread: null job");
+        return;
+    }
+    (void)gemv_s_repack(j->w, j->rows, j->cols, j->w);
+}
+
 int rt_b200_last_error(struct rt *R, char *msg, size_t n) {
     int *status = &t_status;
     char *m = t_msg;
@@ -1016,6 +1064,8 @@ int rt_b200_pull(struct rt *R, void *dev, const void *host, size_t bytes) {
     // while a round is open its kernel is already on R's stream, waiting for this x: the copy goes
     // on the link stream, which rt_gemv_go then orders before the gate's release
     cudaStream_t s = c->round_open ? c->link : c->stream;
+    if (!c->round_open)
+        c->synced = false;
     if (bytes && !cuda_ok(c, cudaMemcpyAsync(dev, host, bytes, cudaMemcpyHostToDevice, s), "rt_b200_pull"))
         return c->status;
     return RTB_OK;
@@ -1042,8 +1092,10 @@ void *rt_b200_stream(struct rt *R) {
 
 void rt_b200_set_stream(struct rt *R, void *stream) {
     Ctx *c = ctx_of(R);
-    if (c)
+    if (c) {
         c->stream = stream ? static_cast<cudaStream_t>(stream) : c->own_stream;
+        c->synced = false;
+    }
 }
 
 int rt_b200_nccl_id(void *out128) {
@@ -1151,6 +1203,18 @@ int rt_b200_wait_probe(struct rt *R) {
     cudaStreamSynchronize(c->stream);
     cudaFree(ctr);
     return c->status;
+}
+
+int rt_b200_shard_rows(long rows, int rank, int world, long *row0, long *n) {
+    if (!row0 || !n || world < 1 || rank < 0 || rank >= world || rows < 1 || rows % world) {
+        thread_err(RTB_EINVAL, "rt_b200_shard_rows: rows %ld rank %d world %d", rows, rank, world);
+        return RTB_EINVAL;
+    }
+    long long lr, r0;
+    split_rows(rows, rank, world, &lr, &r0);
+    *row0 = long(r0);
+    *n = long(lr);
+    return RTB_OK;
 }
 
 int rt_b200_peer_gather(struct rt *R) {

@@ -28,7 +28,8 @@ EXPORTS = ("rt_init", "rt_gemv", "rt_gemv_q", "rt_gemv_open", "rt_gemv_go", "rt_
            "rt_b200_last_error", "rt_b200_set_overlap", "rt_b200_set_async", "rt_b200_sync", "rt_b200_stream", "rt_b200_set_stream",
            "rt_b200_free", "rt_b200_nccl_id", "rt_b200_shard", "rt_b200_peer_gather", "rt_b200_chain_begin",
            "rt_b200_chain_end", "rtb_gguf_info", "rt_b200_load_gguf", "rtb_load_error", "rtb_synth_q8_0",
-           "rtb_synth_f32", "rt_gemm_static", "rt_b200_pull", "rt_b200_push", "rt_b200_wait_probe")
+           "rtb_synth_f32", "rt_gemm_static", "rt_b200_pull", "rt_b200_push", "rt_b200_wait_probe", "gemv_i_bytes",
+           "gemv_i_repack", "gemv_i_repack_thread", "rt_b200_shard_rows")
 
 
 class RtError(RuntimeError):
@@ -81,6 +82,9 @@ def load() -> C.CDLL:
         "rt_q8_row": ([_P, _L, _L, _P], None),
         "gemv_s_bytes": ([_L, _L], _L),
         "gemv_s_repack": ([_P, _L, _L, _P], C.c_int),
+        "gemv_i_bytes": ([_L, _L], _L),
+        "gemv_i_repack": ([_P, _L, _L, _P], None),
+        "gemv_i_repack_thread": ([_P, C.c_int, C.c_int], None),
         "rt_gemm_silu_q": ([R, _P, _P, _L, _L, _P, _L, _P], None),
         "rt_gemm_silu": ([R, _P, _P, _L, _L, _P, _L, _P], None),
         "rt_gemv_rows_q": ([R, _P, _L, _P, _L, _L, _P, _P], None),
@@ -97,6 +101,7 @@ def load() -> C.CDLL:
         "rt_b200_nccl_id": ([_P], C.c_int),
         "rt_b200_shard": ([R, C.c_int, C.c_int, _P], C.c_int),
         "rt_b200_peer_gather": ([R], C.c_int),
+        "rt_b200_shard_rows": ([_L, C.c_int, C.c_int, C.POINTER(_L), C.POINTER(_L)], C.c_int),
         "rt_b200_wait_probe": ([R], C.c_int),
         "rt_b200_chain_begin": ([R], C.c_int),
         "rt_b200_chain_end": ([R, C.c_int], C.c_int),
@@ -115,6 +120,15 @@ def load() -> C.CDLL:
         f.restype = res
     _lib = lib
     return lib
+
+
+def shard_rows(rows: int, rank: int, world: int) -> tuple[int, int]:
+    """rt_b200_shard_rows: (first row, row count) of rank's shard, as the library splits products."""
+    r0, n = C.c_long(0), C.c_long(0)
+    code = load().rt_b200_shard_rows(rows, rank, world, C.byref(r0), C.byref(n))
+    if code:
+        raise RtError(code, last_error(None)[1])
+    return r0.value, n.value
 
 
 def last_error(rt: "Runtime | None" = None) -> tuple[int, str]:

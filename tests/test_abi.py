@@ -115,3 +115,54 @@ def test_generated_style_c_code_compiles_and_links(rtb, tmp_path):
     codes, sizes = run.stdout.strip().split("|")
     assert codes.split() == ["5"] * 6  # RTB_ENOTINIT for every product: nothing reached a device
     assert sizes.split() == [str(4096 * 4096 * 34 // 32), "40"]
+
+
+# The engine's load site (src/card/engine.c:295-316 of the reference): scratch sized by
+# gemv_i_bytes, one struct gemv_repack_job per matrix, run as a team body on every thread. It must
+# compile and link against the library under the reference's names. Run on the host: threads other
+# than 0 return at once, and thread 0 refuses an in-place repack whose rows would change length
+# (cols % 256 != 0) before touching a device.
+LOAD_SITE_C = r"""
+#include <stdio.h>
+#include <stdint.h>
+#include "rt_b200.h"
+
+static void team_run(void (*fn)(void *, int, int), void *arg, int n)
+{
+    for (int tid = n - 1; tid >= 0; tid--)  /* tid 0 is the caller's thread, as in the engine */
+        fn(arg, tid, n);
+}
+
+int main(void)
+{
+    long max_cols = 12288;
+    long scratch = gemv_i_bytes(16, max_cols) * 4;
+    struct gemv_repack_job rj = {.w = (void *)0x1000, .rows = 64, .cols = 4128, .tmp = 0};
+    gemv_i_repack_thread(&rj, 3, 4);
+    int other = rt_b200_last_error(NULL, NULL, 0);
+    team_run(gemv_i_repack_thread, &rj, 4);
+    int refused = rt_b200_last_error(NULL, NULL, 0);
+    gemv_i_repack((const uint8_t *)0, 64, 4096, (void *)0x1000);
+    int null_arg = rt_b200_last_error(NULL, NULL, 0);
+    printf("%ld %ld %d %d %d\n", scratch, gemv_i_bytes(4096, 4096), other, refused, null_arg);
+    return 0;
+}
+"""
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="no C compiler")
+def test_engine_load_site_links_under_the_reference_names(rtb, tmp_path):
+    rtb.load()
+    src = tmp_path / "load_site.c"
+    src.write_text(LOAD_SITE_C)
+    exe = tmp_path / "load_site"
+    pkg = os.path.dirname(rtb.LIB_PATH)
+    cc = subprocess.run(["gcc", "-std=gnu11", "-O2", "-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include"),
+                         str(src), "-o", str(exe), f"-L{pkg}", "-l:librt_b200.so", f"-Wl,-rpath,{pkg}"],
+                        capture_output=True, text=True)
+    assert cc.returncode == 0, cc.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0, run.stderr
+    scratch, full, other, refused, null_arg = run.stdout.split()
+    assert int(scratch) == 4 * 16 * 12288 * 34 // 32 and int(full) == 4096 * 4096 * 34 // 32
+    assert (other, refused, null_arg) == ("0", "1", "1")  # RTB_EINVAL, before any device call

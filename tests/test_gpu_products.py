@@ -87,6 +87,32 @@ def test_repack(cuda, rtb, oracle, rows, cols, in_place):
     assert np.array_equal(got.cpu().numpy(), want)
 
 
+def test_reference_load_names_repack(cuda, rtb, oracle):
+    """gemv_i_repack_thread as the engine's load site runs it (a team body; thread 0 repacks in
+    place on the GPU) and gemv_i_repack out of place: the row-split layout under the reference's
+    names (src/card/gemv.h:51-67)."""
+    import ctypes as C
+    lib = rtb.load()
+    rows, cols = 300, 4096
+    q8 = oracle.synth_q8_0(rows, cols, SEED, 4)
+    want = oracle.repack_split(q8, rows, cols)
+    w = dev(cuda, q8)
+
+    class Job(C.Structure):
+        _fields_ = [("w", C.c_void_p), ("rows", C.c_long), ("cols", C.c_long), ("tmp", C.c_void_p)]
+
+    job = Job(w.data_ptr(), rows, cols, None)
+    for tid in (2, 1, 0):
+        lib.gemv_i_repack_thread(C.cast(C.byref(job), C.c_void_p), tid, 3)
+    assert rtb.last_error(None)[0] == 0
+    assert np.array_equal(w.cpu().numpy(), want)
+    src = dev(cuda, q8)
+    out = cuda.empty(lib.gemv_i_bytes(rows, cols), dtype=cuda.uint8, device="cuda")
+    lib.gemv_i_repack(src.data_ptr(), rows, cols, out.data_ptr())
+    assert rtb.last_error(None)[0] == 0
+    assert np.array_equal(out.cpu().numpy(), want)
+
+
 # ---------------------------------------------------------------- the reference's golden y
 
 def _golden():
@@ -385,6 +411,50 @@ def test_async_mode_and_stream(cuda, rtb, oracle):
             assert bits_equal(ys[k].cpu().numpy(), want[k])
     finally:
         rt.close()
+
+
+def test_back_to_back_launches(cuda, rtb, oracle):
+    """24 products back to back, overlapping (programmatic launch: each streams its weights while
+    the previous one finishes), of sizes around the one/two-CTA-per-SM switch and with rows of one
+    to three 4096-column chunks; then the same sequence replayed as a CUDA graph three times:
+    every y bit for bit."""
+    shapes = [(4096, 4096), (2368, 4096), (2360, 4096), (8192, 4096), (512, 12288), (12288, 4096)]
+    mats = [Mat(cuda, rtb, oracle, r, c, 211 + i) for i, (r, c) in enumerate(shapes)]
+    xs_ = {c: xs(oracle, 1, c, 217 + c) for c in {c for _, c in shapes}}
+    xd = {c: dev(cuda, x) for c, x in xs_.items()}
+    want = [oracle.gemv(m.q8, m.rows, m.cols, xs_[m.cols][0]) for m in mats]
+    ys = [cuda.full((mats[k % len(mats)].rows,), float("nan"), dtype=cuda.float32, device="cuda") for k in range(24)]
+    with rtb.Runtime() as rt:
+        rt.set_async(True)
+        rt.set_overlap(True)
+
+        def run():
+            for k in range(24):
+                m = mats[k % len(mats)]
+                rt.gemv(m.ptr, m.rows, m.cols, xd[m.cols].data_ptr(), ys[k].data_ptr())
+
+        run()
+        rt.sync()
+        for k in range(24):
+            assert bits_equal(ys[k].cpu().numpy(), want[k % len(mats)]), k
+        g = cuda.cuda.CUDAGraph()
+        st = cuda.cuda.Stream()
+        st.wait_stream(cuda.cuda.current_stream())
+        with cuda.cuda.stream(st):
+            with cuda.cuda.graph(g, stream=st):
+                rt.set_stream(cuda.cuda.current_stream().cuda_stream)
+                run()
+        cuda.cuda.current_stream().wait_stream(st)
+        rt.set_stream(cuda.cuda.current_stream().cuda_stream)
+        for _ in range(3):
+            for y in ys:
+                y.fill_(float("nan"))
+            g.replay()
+            cuda.cuda.synchronize()
+            for k in range(24):
+                assert bits_equal(ys[k].cpu().numpy(), want[k % len(mats)]), k
+        rt.sync()
+        del g
 
 
 def test_bad_arguments_raise_and_leave_the_gpu_usable(cuda, runtime, rtb, oracle):

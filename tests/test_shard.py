@@ -3,8 +3,9 @@
 The library's multi-GPU contract (include/rt_b200.h, rt_b200_shard): with `world` ranks, rank k
 holds rows [k*rows/world, (k+1)*rows/world) of every matrix, computes those outputs, and an
 all-gather in rank order rebuilds the whole y on every rank. These tests run that contract on CPU
-ranks with the oracle as the per-rank product and gloo as the collective, and check the rebuilt y
-is the unsharded product bit for bit; bench.py shards the same way (workload.shard_rows).
+ranks: each rank asks the library for its shard (rt_b200_shard_rows, the split its products use),
+loads those rows with the oracle's generator, computes them with the oracle, and gloo all-gathers;
+the rebuilt y must be the unsharded product bit for bit. bench.py shards the same way.
 """
 from __future__ import annotations
 
@@ -31,13 +32,15 @@ def _rank_main(rank: int, world: int, port: int, case: dict, out) -> None:
     sys.path.insert(0, ORACLE)
     sys.path.insert(0, PKG)
     import oracle as O
+    import rtb200
     import workload as WL
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         rows, cols, t = case["rows"], case["cols"], case["t"]
-        r0, n = WL.shard_rows(rows, rank, world)
+        r0, n = rtb200.shard_rows(rows, rank, world)  # the library's split
+        assert (r0, n) == WL.shard_rows(rows, rank, world)  # the bench's allocation agrees
         q8 = O.synth_q8_0(n, cols, 7, 3, row0=r0)  # this rank's shard only
         x = np.stack([O.synth_f32(cols, 7, 4 + k) for k in range(t)])
         y_local = O.gemm(q8, n, cols, x, t, threads=2)  # [t][n]
@@ -69,14 +72,18 @@ def test_row_shards_all_gather_rebuild_the_product(case, oracle):
     assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
 
 
-def test_shard_rows_partition():
+def test_shard_rows_partition(rtb):
     import workload as WL
     for rows, world in [(4096, 1), (4096, 2), (151936, 8), (12288, 4)]:
-        parts = [WL.shard_rows(rows, k, world) for k in range(world)]
+        parts = [rtb.shard_rows(rows, k, world) for k in range(world)]
+        assert parts == [WL.shard_rows(rows, k, world) for k in range(world)]
         assert parts[0][0] == 0 and sum(n for _, n in parts) == rows
         assert all(parts[k][0] + parts[k][1] == parts[k + 1][0] for k in range(world - 1))
     with pytest.raises(ValueError):
         WL.shard_rows(100, 0, 8)
+    for bad in [(100, 0, 8), (64, 2, 2), (64, -1, 2), (64, 0, 0)]:
+        with pytest.raises(rtb.RtError):
+            rtb.shard_rows(*bad)
 
 
 def test_every_baseline_shape_shards_over_8():
