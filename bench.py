@@ -54,7 +54,7 @@ SEED = 20261201
 METRIC = "Q8_0 weight-product GB/s, 9B decode step (M=1)"
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 TRAFFIC_PATH = os.path.join(ROOT, "profiles", "gemv_exact_head_151936x4096.md")
-STEP_TRAFFIC_PATH = os.path.join(ROOT, "profiles", "launches_bench_decode_step_m1.md")
+STEP_TRAFFIC_PATH = os.path.join(ROOT, "profiles", "gemv_exact_down_gateup_m1.md")
 
 
 def log(*a):
@@ -364,12 +364,13 @@ class Bench:
     def e2e(self, steps: int, warmup: int) -> dict:
         """The reference-facing path with host buffers, one round at a time as the reference engine
         runs them, driven from C (intel-phi-apl_b200/engine_rounds.c, eng_run_rounds) against the C
-        ABI: per round the product is queued (rt_gemv_q / rt_gemm_silu_q), the round is opened
-        (rt_gemv_open: its kernel is launched and streams its weights while x is still on the
-        host), x goes host->device from pinned memory (rt_b200_pull, the engine's link_pull), the
-        round runs (rt_gemv_go) and y comes back device->host (rt_b200_push, the engine's
-        link_push), which returns once y is on the host. Wall-clock time of whole steps, after
-        `warmup` steps. Also timed: the same rounds without rt_gemv_open."""
+        ABI on the runtime's own stream: per round the product is queued (rt_gemv_q /
+        rt_gemm_silu_q), x goes host->device from pinned memory (rt_b200_pull, the engine's
+        link_pull), the round runs (rt_gemv_go) and y comes back device->host (rt_b200_push, the
+        engine's link_push), which returns once y is on the host. Wall-clock time of whole steps,
+        after `warmup` steps. Also timed: the same rounds opened before x is pulled (rt_gemv_open:
+        the round's kernel is launched at once and streams its weights, gated on the GPU until go),
+        which measures slower in this loop, where no host work sits between the rounds to hide."""
         import ctypes as C
         torch, rt = self.torch, self.rt
         rt.set_async(True)
@@ -386,7 +387,7 @@ class Bench:
                         ("x_host", C.c_void_p), ("x_bytes", C.c_size_t), ("y_dev", C.c_void_p),
                         ("y_host", C.c_void_p), ("y_bytes", C.c_size_t)]
 
-        spec = []
+        spec = []  # (kind, w, w2, rows, cols, x name, y name); every round opened until the plain run
         for L in self.w:
             spec += [(0, L["qkv"], None, WL.QKV, WL.D, "d", "qkv"), (0, L["out"], None, WL.D, WL.D, "d", "out"),
                      (1, L["gate"], L["up"], WL.FF, WL.D, "d", "h"), (0, L["down"], None, WL.D, WL.FF, "ff", "down")]
@@ -414,16 +415,17 @@ class Bench:
             torch.cuda.synchronize()
             return self.max_over_ranks((time.perf_counter() - t0) / n)
 
-        dt = timed(steps)
+        dt_open = timed(steps)
         for r in rounds:
             r.open = 0
-        dt_plain = timed(steps)
+        dt = timed(steps)
         total = WL.step_bytes(1, self.layers)
         return {"value": round(total / dt / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(dt * 1e3, 3), "tok_s": round(1.0 / dt, 1),
-                "path": "per round, from C (engine_rounds.c): rt_gemv_q / rt_gemm_silu_q, rt_gemv_open, rt_b200_pull "
-                        "of x, rt_gemv_go, rt_b200_push of y (pinned host buffers)",
-                "without_open": {"ms_per_step": round(dt_plain * 1e3, 3), "value": round(total / dt_plain / 1e9, 1)}}
+                "path": "per round, from C (engine_rounds.c): rt_gemv_q / rt_gemm_silu_q, rt_b200_pull of x, "
+                        "rt_gemv_go, rt_b200_push of y (pinned host buffers)",
+                "opened_rounds": {"ms_per_step": round(dt_open * 1e3, 3), "value": round(total / dt_open / 1e9, 1),
+                                  "path": "the same with rt_gemv_open before the pull"}}
 
     def _graph(self, fns):
         """The calls captured as one CUDA graph on a side stream (the runtime follows the stream)."""
@@ -676,7 +678,7 @@ def step_roofline(total: int, ms1: float, world: int, res: dict, layers: int = W
     """The roofline of the decode step, the metric's own workload: its 129 gemv_exact_kernel
     launches (each rank streams its row shard) against one GPU's measured HBM copy bandwidth.
     achieved = the step's algorithmic bytes per GPU / the step time. traffic = ncu DRAM read+write
-    bytes of one step's launches (profiles/launches_bench_decode_step_m1.md, 1 GPU), per step.
+    bytes of one step's launches (profiles/gemv_exact_down_gateup_m1.md, 1 GPU), per step.
     per_shape (1 GPU): each shape's launch alone (the sweep's graph of 32 copies), its fraction of
     the peak and its share of the step (launches per step x time / step time)."""
     peak, how = peaks()

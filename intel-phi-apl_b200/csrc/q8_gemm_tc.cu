@@ -737,6 +737,13 @@ size_t tokf_bytes(const GemmJob &G) { return (size_t(G.t) * sizeof(float) + 255)
 size_t rexp_bytes(const GemmJob &G) { return (size_t(G.rows) * (G.w2 ? 2 : 1) + 255) / 256 * 256; }
 size_t x_bytes(const GemmJob &G) { return xh_bytes(G) + tokf_bytes(G) + rexp_bytes(G); }
 
+// The shape's kernel on the current device: loaded, and its shared-memory limit set to the SM's
+// per-CTA limit (preload_gemm_tc does it for both shapes at rt_init).
+template <int CPS>
+cudaError_t setup_shape() {
+    return cudaFuncSetAttribute(gemm_tc_kernel<CPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+}
+
 // One launch of the CPS-per-SM shape. With CPS = 1 the CTA allocates all 512 TMEM columns, so a
 // second CTA on the SM would only wait in its allocation: more than half the SM's shared memory
 // keeps it off. With CPS = 2 two CTAs fit (256 columns and at most ~113 KB each).
@@ -748,8 +755,7 @@ cudaError_t launch_shape(const TcParams &p, size_t smem, int units, int num_sms,
         return cudaErrorInvalidValue;
     static bool attr = false;
     if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<CPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             227 * 1024); // the SM's limit per CTA
+        cudaError_t e = setup_shape<CPS>();
         if (e != cudaSuccess)
             return e;
         attr = true;
@@ -771,6 +777,16 @@ cudaError_t launch_shape(const TcParams &p, size_t smem, int units, int num_sms,
 }
 
 } // namespace
+
+cudaError_t preload_gemm_tc() {
+    cudaError_t e;
+    if ((e = setup_shape<1>()) != cudaSuccess || (e = setup_shape<2>()) != cudaSuccess)
+        return e;
+    cudaFuncAttributes a;
+    if ((e = cudaFuncGetAttributes(&a, tc_prep_kernel)) != cudaSuccess)
+        return e;
+    return cudaFuncGetAttributes(&a, splitk_reduce_kernel);
+}
 
 size_t gemm_tc_scratch_bytes(const GemmJob *jobs, int n, int num_sms, bool split_k) {
     if (n < 1 || n > 8)

@@ -613,12 +613,16 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
     }
 }
 
-template <int MT, int CTAS, class P = GemvParams>
-cudaError_t launch_mt(const P &p, int num_sms, int grid_limit, cudaStream_t stream, bool pdl, bool coop = false) {
+// One kernel instance's set-up on the current device: its shared-memory attribute and the CTAs
+// that fit on an SM (kept per process). Done for every instance by preload_gemv at rt_init, so no
+// launch loads a kernel or sets an attribute first (that can wait for the GPU, which an opened
+// round's gated kernel holds).
+template <int MT, int CTAS, class P>
+cudaError_t setup_mt(int *per_sm_out) {
     using C = Cfg<MT, CTAS>;
     const size_t smem = smem_bytes<MT, CTAS>();
-    static int per_sm = 0; // CTAs that fit on one SM (per process; the attribute is per function)
-    if (per_sm == 0) {
+    static int per_sm = 0;
+    if (per_sm == 0 || !per_sm_out) {
         cudaError_t e = cudaFuncSetAttribute(gemv_exact_kernel<MT, CTAS, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              int(smem));
         if (e != cudaSuccess)
@@ -631,6 +635,19 @@ cudaError_t launch_mt(const P &p, int num_sms, int grid_limit, cudaStream_t stre
             return cudaErrorInvalidConfiguration;
         per_sm = n < CTAS ? n : CTAS;
     }
+    if (per_sm_out)
+        *per_sm_out = per_sm;
+    return cudaSuccess;
+}
+
+template <int MT, int CTAS, class P = GemvParams>
+cudaError_t launch_mt(const P &p, int num_sms, int grid_limit, cudaStream_t stream, bool pdl, bool coop = false) {
+    using C = Cfg<MT, CTAS>;
+    const size_t smem = smem_bytes<MT, CTAS>();
+    int per_sm = 0;
+    cudaError_t es = setup_mt<MT, CTAS, P>(&per_sm);
+    if (es != cudaSuccess)
+        return es;
     int grid = per_sm * (num_sms > 0 ? num_sms : 148);
     if (grid_limit > 0 && grid > grid_limit)
         grid = grid_limit;
@@ -693,6 +710,18 @@ cudaError_t launch_gemv(GemvParams &p, int num_sms, int grid_limit, cudaStream_t
     case 3: return launch_mt<3, 1>(p, num_sms, grid_limit, stream, pdl);
     default: return launch_mt<4, 1>(p, num_sms, grid_limit, stream, pdl);
     }
+}
+
+cudaError_t preload_gemv() {
+    cudaError_t e;
+    if ((e = setup_mt<1, 1, GemvParams>(nullptr)) != cudaSuccess || (e = setup_mt<1, 2, GemvParams>(nullptr)) != cudaSuccess ||
+        (e = setup_mt<2, 1, GemvParams>(nullptr)) != cudaSuccess || (e = setup_mt<3, 1, GemvParams>(nullptr)) != cudaSuccess ||
+        (e = setup_mt<4, 1, GemvParams>(nullptr)) != cudaSuccess || (e = setup_mt<1, 1, ChainParams>(nullptr)) != cudaSuccess ||
+        (e = setup_mt<2, 1, ChainParams>(nullptr)) != cudaSuccess || (e = setup_mt<3, 1, ChainParams>(nullptr)) != cudaSuccess ||
+        (e = setup_mt<4, 1, ChainParams>(nullptr)) != cudaSuccess)
+        return e;
+    cudaFuncAttributes a;
+    return cudaFuncGetAttributes(&a, wait_probe_kernel);
 }
 
 cudaError_t launch_wait_probe(const unsigned *ctr, unsigned *err, cudaStream_t stream) {

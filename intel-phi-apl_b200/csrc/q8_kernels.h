@@ -121,6 +121,13 @@ size_t gemm_tc_scratch_bytes(const GemmJob *jobs, int n, int num_sms, bool split
 cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scratch_bytes, int num_sms,
                            unsigned *err, cudaStream_t stream, bool pdl, bool split_k);
 
+// Each kernel file's kernels loaded and their attributes set on the current device (rt_init calls
+// these, so that no later launch does it first: under lazy module loading the first launch of a
+// kernel may have to wait for the GPU, which a gated kernel of an opened round holds until go).
+cudaError_t preload_gemv();
+cudaError_t preload_gemm_tc();
+cudaError_t preload_peer();
+
 // ---- utilities
 // The repack stages a whole GGUF row in shared memory (what makes it safe in place): rows of at
 // most this many GGUF bytes, i.e. cols <= 192,736.

@@ -56,6 +56,11 @@ __global__ void peer_finish_kernel(const PeerOut po, float *y, long long ldy, in
 
 } // namespace
 
+cudaError_t preload_peer() {
+    cudaFuncAttributes a;
+    return cudaFuncGetAttributes(&a, peer_finish_kernel);
+}
+
 cudaError_t launch_peer_finish(const PeerOut &po, float *y, long long ldy, int t, unsigned *err, cudaStream_t stream,
                                bool pdl) {
     if (!po.on || po.world < 2 || po.world > MAX_PEERS || t < 1 ||

@@ -614,6 +614,33 @@ void open_round(Ctx *c) {
     }
     if (jobs.empty())
         return;
+    // The tensor-core products left for go get their scratch now: growing it at go would allocate
+    // (and may synchronize) while the gated kernel holds the GPU waiting for go.
+    if (!rest.empty()) {
+        size_t need = 0;
+        std::vector<q8::GemmJob> tc;
+        for (const Item &it : rest) {
+            q8::GemmJob g;
+            memset(&g, 0, sizeof g);
+            g.w = it.w;
+            g.w2 = it.kind == K_SILU ? it.w2 : nullptr;
+            g.x = it.x;
+            g.ldx = it.cols;
+            g.y = it.y;
+            g.ldy = it.rows;
+            g.rows = it.rows;
+            g.cols = int(it.cols);
+            g.t = int(it.t);
+            tc.push_back(g);
+        }
+        for (size_t i = 0; i < tc.size(); i += 8) {
+            const int n = int(tc.size() - i < 8 ? tc.size() - i : 8);
+            const size_t b = q8::gemm_tc_scratch_bytes(&tc[i], n, c->num_sms, true);
+            need = b > need ? b : need;
+        }
+        if (!ensure_scratch(c, need))
+            return;
+    }
     // (R's own stream, synchronized since its last work: nothing there can still read an x)
     if (!c->synced && (!cuda_ok(c, cudaEventRecord(c->ev_before, c->stream), "open: event") ||
                        !cuda_ok(c, cudaStreamWaitEvent(c->link, c->ev_before, 0), "open: link stream wait")))
@@ -752,7 +779,8 @@ int rt_init(struct rt *R, int threads) {
     }
     c->stream = c->own_stream;
     unsigned *h_err = nullptr, *h_err_dev = nullptr;
-    if (cudaHostAlloc(&h_err, sizeof(unsigned), cudaHostAllocMapped) != cudaSuccess ||
+    if (q8::preload_gemv() != cudaSuccess || q8::preload_gemm_tc() != cudaSuccess || q8::preload_peer() != cudaSuccess ||
+        cudaHostAlloc(&h_err, sizeof(unsigned), cudaHostAllocMapped) != cudaSuccess ||
         cudaHostGetDevicePointer(&h_err_dev, h_err, 0) != cudaSuccess) {
         if (h_err)
             cudaFreeHost(h_err);
