@@ -202,10 +202,15 @@ RTB_API void rt_b200_free(struct rt *R);
  * One process per GPU. With world > 1, every product's w is this rank's row shard (rows/world
  * consecutive rows, rank-major, rows % world == 0) while rows, y and t keep the whole product's
  * meaning: each rank computes its rows and y is filled on every rank over NVLink.
- * - A single product of <= 4 tokens (rt_gemv, rt_gemm, rt_gemm_silu) gathers y in its own kernel:
- *   every output is also stored into each peer's staging buffer (CUDA IPC mappings set up by
- *   rt_b200_shard), the last CTA raises a flag on every peer, and a small kernel on each rank waits
- *   for the peers' flags and copies their rows into y.
+ * - A single product of <= 4 tokens (rt_gemv, rt_gemm, rt_gemm_silu) gathers y over NVLink
+ *   without NCCL: every output is also stored into each peer's staging buffer (CUDA IPC mappings
+ *   set up by rt_b200_shard) and the last CTA raises a flag on every peer. The peers' rows are then
+ *   copied into y by the next such product's own kernel (after it has waited, bounded, for the
+ *   flags; its weights stream meanwhile), or, before anything else is run, pulled or pushed, or
+ *   when R is synchronized or flushed, by a small kernel of their own. So in async mode y is
+ *   whole once the next call on R has been made; blocking calls return with y whole. A sequence
+ *   captured into a CUDA graph must end with rt_b200_flush, so that the graph finishes its last
+ *   gather itself.
  * - Queued rounds, t > 4 and the tensor-core path all-gather y with NCCL.
  * All ranks must issue the same products in the same order. nccl_id is the 128-byte ncclUniqueId
  * from rt_b200_nccl_id on rank 0, passed to every rank by the caller. 0 or an RTB_E* code.
@@ -214,6 +219,10 @@ RTB_API void rt_b200_free(struct rt *R);
 RTB_API int rt_b200_nccl_id(void *out128);
 RTB_API int rt_b200_shard(struct rt *R, int rank, int world, const void *nccl_id);
 RTB_API int rt_b200_peer_gather(struct rt *R);
+
+/* Enqueues the kernel that finishes a row-sharded product's pending gather, if one is pending (a
+ * no-op otherwise, and with one GPU). Can be captured into a graph. 0 or an RTB_E* code. */
+RTB_API int rt_b200_flush(struct rt *R);
 
 /* The rows of a rows-row matrix that rank `rank` of `world` holds and computes, as the products
  * split them: *row0 and *n (rows / world consecutive rows, rank-major). Host only, no device: an

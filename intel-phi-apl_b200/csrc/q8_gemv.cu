@@ -57,6 +57,9 @@ struct Cfg {
     static constexpr int NCHAIN = CTAS == 2 ? 1 : 2;                  // tile i of the CTA -> chain warp i % NCHAIN
     static constexpr int COPY_WARP = CHAIN_WARP + NCHAIN;
     static constexpr int NT = NC + 32 * NCHAIN + 32;                  // threads
+    // tiles visited chunk-major together in a launch with rows of several chunks (one at a time in
+    // the two-CTA form: its register budget has no room for the group's running sums)
+    static constexpr int GROUP = CTAS == 2 ? 1 : 4;
 };
 // One-token launches with at least this many stages per SM run two CTAs per SM.
 constexpr int TWO_CTA_MIN_STAGES_PER_SM = 12;
@@ -95,7 +98,7 @@ struct JobView {
     int nwait; // the waits themselves stay in the kernel parameters (read once per job)
     int x_written;
     long long rows, src_rows, ldx, ldy, rb;
-    int cols, m, tile0, rpt, nchunk;
+    int cols, m, tile0, tiles, rpt, nchunk;
     __device__ __forceinline__ void load(const GemvJob &J) {
         done_ctr = J.done_ctr;
         nwait = J.nwait;
@@ -112,24 +115,35 @@ struct JobView {
         cols = J.cols;
         m = J.m;
         tile0 = J.tile0;
+        tiles = J.tiles;
         rb = q8s_row_bytes(cols);
         rpt = w2 ? R / 2 : R; // output rows per tile
         nchunk = (cols + KC - 1) / KC;
     }
 };
 
-// The CTA's sequence of stages: tiles blockIdx.x, +gridDim.x, ..., each in ceil(cols/KC) chunks.
-// Every role walks its own copy; tiles only grow, so the job index only moves forward.
+// The CTA's sequence of stages. Its tiles are blockIdx.x, +gridDim.x, ..., each ceil(cols/KC)
+// chunks long. A row of several chunks is visited chunk-major over a group of up to GROUP tiles
+// of the CTA (chunk 0 of each tile of the group, then chunk 1, ...): the compute warps then load
+// each x chunk once per group instead of once per stage, and each row still runs its blocks in
+// order (the chain warps keep a running sum per tile of the group). A gather's tiles go one at a
+// time (its row index is loaded per tile). Every role walks its own copy; tiles only grow, so the
+// job index only moves forward. k: the CTA's count of the current tile (its chain warp is
+// k % NCHAIN); i: the tile's place in its group (its running-sum slot is i / NCHAIN).
+template <int GROUP>
 struct StageIter {
     int g, c, job;
+    int gfirst, gsize, i, kbase, k;
     JobView J;
     template <class P>
     __device__ __forceinline__ void start(const P &p) {
-        g = blockIdx.x;
-        c = 0;
         job = -1;
-        if (g < p.total_tiles)
-            set(p);
+        kbase = 0;
+        gfirst = blockIdx.x;
+        if (gfirst < p.total_tiles)
+            group(p);
+        else
+            g = gfirst;
     }
     template <class P>
     __device__ __forceinline__ void set(const P &p) {
@@ -141,23 +155,43 @@ struct StageIter {
             J.load(p.job[j]);
         }
     }
+    // a new group from tile gfirst
+    template <class P>
+    __device__ __forceinline__ void group(const P &p) {
+        g = gfirst;
+        set(p);
+        gsize = 1;
+        if (GROUP > 1 && J.nchunk > 1 && !J.idx) {
+            const int left = 1 + (J.tile0 + J.tiles - 1 - gfirst) / int(gridDim.x); // this CTA's tiles left in the job
+            gsize = left < GROUP ? left : GROUP;
+        }
+        i = 0;
+        c = 0;
+        k = kbase;
+    }
     template <class P>
     __device__ __forceinline__ bool valid(const P &p) const { return g < p.total_tiles; }
     template <class P>
     __device__ __forceinline__ void next(const P &p) {
-        if (++c == J.nchunk) {
-            c = 0;
-            g += gridDim.x;
-            if (g < p.total_tiles)
-                set(p);
+        if (++i == gsize) {
+            i = 0;
+            if (++c == J.nchunk) {
+                kbase += gsize;
+                gfirst += gsize * int(gridDim.x);
+                if (gfirst < p.total_tiles)
+                    group(p);
+                else
+                    g = gfirst;
+                return;
+            }
         }
+        g = gfirst + i * int(gridDim.x);
+        k = kbase + i;
     }
     // stage row r: the output index and the matrix it reads
     __device__ __forceinline__ long long out_row(int r) const { return (long long)(g - J.tile0) * J.rpt + (r % J.rpt); }
     __device__ __forceinline__ const uint8_t *matrix(int r) const { return (J.w2 && r >= J.rpt) ? J.w2 : J.w; }
 };
-
-
 
 // Rows processed side by side by one compute thread. Two at a time for one token: the second
 // pair's shared-memory reads then overlap the first pair's chains in the other warps (all eight
@@ -237,6 +271,52 @@ __device__ __noinline__ bool wait_gate(const unsigned *gate, unsigned value) {
     }
 }
 
+// Waits until *flag >= value, read at system scope (a peer GPU raises it over NVLink), bounded.
+__device__ __noinline__ bool wait_flag64(const unsigned long long *flag, unsigned long long value) {
+    const long long t0 = clock64();
+    for (;;) {
+        unsigned long long v;
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
+        if (v >= value)
+            return true;
+        const long long dt = clock64() - t0;
+        if (dt > WAIT_LIMIT_CYCLES)
+            return false;
+        if (dt > 20000)
+            __nanosleep(100);
+    }
+}
+
+// The previous product's gather, run by the compute threads of a row-sharded launch before they
+// read x: wait for the peers' flags of that product's round (compute thread 0, bounded; the others
+// through the CTA barrier's first phase), then copy this CTA's share of the peers' rows from this
+// GPU's staging image into the product's y. The previous product has completed (the grid wait),
+// so the local round counter is final. Kept out of line: the product loop's registers stay its own.
+__device__ __noinline__ void peer_finish_prologue(const PeerOut &po, uint64_t *depbar, unsigned *err, int tid, int lane) {
+    const unsigned char *mine = po.region[po.rank];
+    const unsigned long long round = *reinterpret_cast<const volatile unsigned long long *>(mine + 72);
+    if (tid == 0) {
+        bool ok = true;
+        for (int w = 0; w < po.world && ok; ++w)
+            if (w != po.rank)
+                ok = wait_flag64(reinterpret_cast<const unsigned long long *>(mine) + w, round);
+        if (!ok)
+            report(err, ERR_TIMEOUT_PEER);
+        mbar_arrive(depbar);
+    } else if (lane == 0 && !mbar_wait(depbar, 0)) {
+        report(err, ERR_TIMEOUT_PEER);
+    }
+    __syncwarp();
+    const float *stage = reinterpret_cast<const float *>(mine + PEER_HDR + (round & 1) * PEER_STAGE_BYTES);
+    const long long rows = po.fin_rows, lr = rows / po.world, own0 = (long long)po.rank * lr;
+    const long long n = (long long)po.fin_t * rows;
+    for (long long e = (long long)blockIdx.x * NC + tid; e < n; e += (long long)gridDim.x * NC) {
+        const long long tok = e / rows, row = e - tok * rows;
+        if (row < own0 || row >= own0 + lr)
+            po.fin_y[tok * rows + row] = __ldcg(stage + e);
+    }
+}
+
 // The failure path's self-test: one thread waits on a device counter that nothing advances, then
 // on an mbarrier that nothing arrives on. Each wait gives up after WAIT_LIMIT_CYCLES (about a
 // second) and reports its bit, as a stuck wait in a product kernel does; the kernel then returns.
@@ -251,9 +331,12 @@ __global__ void wait_probe_kernel(const unsigned *ctr, unsigned *err) {
         report(err, ERR_TIMEOUT_FULL);
 }
 
-template <int MT, int CTAS, class P>
+// GROUPED: some job of the launch has rows of several chunks (the instance without it carries no
+// group bookkeeping, which the one-chunk rows would pay for in every stage).
+template <int MT, int CTAS, class P, bool GROUPED>
 __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(const __grid_constant__ P p) {
     using C = Cfg<MT, CTAS>;
+    constexpr int GROUP = GROUPED ? C::GROUP : 1;
     constexpr int STAGES = C::STAGES, TBUF = C::TBUF, NCHAIN = C::NCHAIN, COPY_WARP = C::COPY_WARP;
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t *slots = smem;
@@ -287,9 +370,12 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
         // ---------------------------------------------------------------- compute threads
         float xr[MT][Q8_QK];
         int xjob = -1, xc = -1, wjob = -1, ndep = 0;
-        int ctile = 0; // the CTA's tiles so far: tile i's partial sums go to chain warp i % NCHAIN
         const int b = tid % NBK, half = tid / NBK;
         grid_wait(); // x comes from the previous kernel on the stream
+        if (p.peer.fin_on) {
+            peer_finish_prologue(p.peer, depbar, p.err, tid, lane);
+            ndep = 1;
+        }
         if (p.gate) {
             // an opened round: x lands after the launch. Compute thread 0 polls the gate and
             // passes it on through the CTA barrier (its first phase), as for a chained round.
@@ -303,7 +389,7 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
             ndep = 1;
             __syncwarp();
         }
-        StageIter it;
+        StageIter<GROUP> it;
         it.start(p);
         for (int s = 0; it.valid(p); it.next(p), ++s) {
             const int slot = s % STAGES, tb = s % TBUF;
@@ -409,14 +495,16 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
             }
             if (!ok)
                 break;
-            mbar_arrive(&tfull[(ctile % NCHAIN) * TBUF + tb]);
-            if (it.c == it.J.nchunk - 1)
-                ++ctile;
+            mbar_arrive(&tfull[(it.k % NCHAIN) * TBUF + tb]); // the tile's chain warp
         }
     } else if (warp < COPY_WARP) {
         // ---------------------------------------------------------------- chain warps
         const int mt = lane / R, r = lane % R, cw = warp - CHAIN_WARP;
-        float acc = 0.0f;
+        constexpr int ACCS = (GROUP + NCHAIN - 1) / NCHAIN;
+        float accs[ACCS]; // the running sums of this warp's tiles of the current group
+#pragma unroll
+        for (int a = 0; a < ACCS; ++a)
+            accs[a] = 0.0f;
         // A row-sharded launch also stores each output into every peer's staging image of this
         // round ([t][rows_total], parity of the round being produced).
         const PeerOut &po = p.peer;
@@ -444,10 +532,10 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
         // warp has its own TBUF barriers, which advance only on its own stages, and keeps their
         // parities here (bit b: buffer b).
         uint32_t tpar = 0;
-        StageIter it;
+        StageIter<GROUP> it;
         it.start(p);
-        for (int s = 0, tile = 0; it.valid(p); ++s) {
-            const bool own = tile % NCHAIN == cw;
+        for (int s = 0; it.valid(p); ++s) {
+            const bool own = it.k % NCHAIN == cw;
             const int tb = s % TBUF;
             const bool last_chunk = it.c == it.J.nchunk - 1;
             if (own) {
@@ -461,8 +549,12 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
                 const bool valid = o < it.J.rows;
                 const bool loaded = rowflag[(s % FRING) * R + r] != 0;
                 const bool mine = mt < it.J.m && loaded;
-                if (it.c == 0)
-                    acc = 0.0f;
+                const int slot = it.i / NCHAIN;
+                float acc = 0.0f; // (selected from registers: no local-memory indexing)
+#pragma unroll
+                for (int a = 0; a < ACCS; ++a)
+                    if (a == slot && it.c > 0)
+                        acc = accs[a];
                 if (mine) {
                     const float *tp = T + tb * MT * R * TPAD + (mt * R + r) * TPAD;
                     const float *dp = TD + tb * R * TPAD + r * TPAD;
@@ -485,6 +577,10 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
                     for (; b < nbk; ++b)
                         acc = __fmaf_rn(tp[b], dp[b], acc);
                 }
+#pragma unroll
+                for (int a = 0; a < ACCS; ++a)
+                    if (a == slot)
+                        accs[a] = acc;
                 __syncwarp();
                 if (lane == 0)
                     mbar_arrive(&tempty[tb]);
@@ -509,8 +605,6 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
                     }
                 }
             }
-            if (last_chunk)
-                ++tile;
             it.next(p);
         }
     } else {
@@ -527,7 +621,7 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
                 report(p.err, ERR_TIMEOUT_GATE);
             __syncwarp();
         }
-        StageIter it;
+        StageIter<GROUP> it;
         it.start(p);
         long long src = -1; // this lane's source row for the current stage (gathers: prefetched)
         if (it.valid(p) && lane < R && it.J.idx) {
@@ -617,18 +711,18 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
 // that fit on an SM (kept per process). Done for every instance by preload_gemv at rt_init, so no
 // launch loads a kernel or sets an attribute first (that can wait for the GPU, which an opened
 // round's gated kernel holds).
-template <int MT, int CTAS, class P>
+template <int MT, int CTAS, class P, bool GROUPED>
 cudaError_t setup_mt(int *per_sm_out) {
     using C = Cfg<MT, CTAS>;
     const size_t smem = smem_bytes<MT, CTAS>();
     static int per_sm = 0;
     if (per_sm == 0 || !per_sm_out) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_exact_kernel<MT, CTAS, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(gemv_exact_kernel<MT, CTAS, P, GROUPED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              int(smem));
         if (e != cudaSuccess)
             return e;
         int n = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_exact_kernel<MT, CTAS, P>, C::NT, smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_exact_kernel<MT, CTAS, P, GROUPED>, C::NT, smem);
         if (e != cudaSuccess)
             return e;
         if (n < 1)
@@ -640,12 +734,12 @@ cudaError_t setup_mt(int *per_sm_out) {
     return cudaSuccess;
 }
 
-template <int MT, int CTAS, class P = GemvParams>
-cudaError_t launch_mt(const P &p, int num_sms, int grid_limit, cudaStream_t stream, bool pdl, bool coop = false) {
+template <int MT, int CTAS, class P, bool GROUPED>
+cudaError_t launch_mt_g(const P &p, int num_sms, int grid_limit, cudaStream_t stream, bool pdl, bool coop) {
     using C = Cfg<MT, CTAS>;
     const size_t smem = smem_bytes<MT, CTAS>();
     int per_sm = 0;
-    cudaError_t es = setup_mt<MT, CTAS, P>(&per_sm);
+    cudaError_t es = setup_mt<MT, CTAS, P, GROUPED>(&per_sm);
     if (es != cudaSuccess)
         return es;
     int grid = per_sm * (num_sms > 0 ? num_sms : 148);
@@ -669,7 +763,33 @@ cudaError_t launch_mt(const P &p, int num_sms, int grid_limit, cudaStream_t stre
     }
     cfg.attrs = attr;
     cfg.numAttrs = (pdl || coop) ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_exact_kernel<MT, CTAS, P>, p);
+    return cudaLaunchKernelEx(&cfg, gemv_exact_kernel<MT, CTAS, P, GROUPED>, p);
+}
+
+// rows of several chunks (not gathered) somewhere in the launch
+template <class P>
+bool any_grouped(const P &p) {
+    for (int j = 0; j < p.njobs; ++j)
+        if (p.job[j].cols > KC && !p.job[j].idx)
+            return true;
+    return false;
+}
+
+template <int MT, int CTAS, class P = GemvParams>
+cudaError_t launch_mt(const P &p, int num_sms, int grid_limit, cudaStream_t stream, bool pdl, bool coop = false) {
+    if constexpr (CTAS == 1)
+        if (any_grouped(p))
+            return launch_mt_g<MT, CTAS, P, true>(p, num_sms, grid_limit, stream, pdl, coop);
+    return launch_mt_g<MT, CTAS, P, false>(p, num_sms, grid_limit, stream, pdl, coop);
+}
+
+template <int MT, int CTAS, class P>
+cudaError_t setup_both() {
+    cudaError_t e = setup_mt<MT, CTAS, P, false>(nullptr);
+    if constexpr (CTAS == 1)
+        if (e == cudaSuccess)
+            e = setup_mt<MT, CTAS, P, true>(nullptr);
+    return e;
 }
 
 } // namespace
@@ -714,11 +834,11 @@ cudaError_t launch_gemv(GemvParams &p, int num_sms, int grid_limit, cudaStream_t
 
 cudaError_t preload_gemv() {
     cudaError_t e;
-    if ((e = setup_mt<1, 1, GemvParams>(nullptr)) != cudaSuccess || (e = setup_mt<1, 2, GemvParams>(nullptr)) != cudaSuccess ||
-        (e = setup_mt<2, 1, GemvParams>(nullptr)) != cudaSuccess || (e = setup_mt<3, 1, GemvParams>(nullptr)) != cudaSuccess ||
-        (e = setup_mt<4, 1, GemvParams>(nullptr)) != cudaSuccess || (e = setup_mt<1, 1, ChainParams>(nullptr)) != cudaSuccess ||
-        (e = setup_mt<2, 1, ChainParams>(nullptr)) != cudaSuccess || (e = setup_mt<3, 1, ChainParams>(nullptr)) != cudaSuccess ||
-        (e = setup_mt<4, 1, ChainParams>(nullptr)) != cudaSuccess)
+    if ((e = setup_both<1, 1, GemvParams>()) != cudaSuccess || (e = setup_both<1, 2, GemvParams>()) != cudaSuccess ||
+        (e = setup_both<2, 1, GemvParams>()) != cudaSuccess || (e = setup_both<3, 1, GemvParams>()) != cudaSuccess ||
+        (e = setup_both<4, 1, GemvParams>()) != cudaSuccess || (e = setup_both<1, 1, ChainParams>()) != cudaSuccess ||
+        (e = setup_both<2, 1, ChainParams>()) != cudaSuccess || (e = setup_both<3, 1, ChainParams>()) != cudaSuccess ||
+        (e = setup_both<4, 1, ChainParams>()) != cudaSuccess)
         return e;
     cudaFuncAttributes a;
     return cudaFuncGetAttributes(&a, wait_probe_kernel);

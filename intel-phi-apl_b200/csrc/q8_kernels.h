@@ -60,6 +60,14 @@ struct PeerOut {
     unsigned char *region[MAX_PEERS]; // every rank's region as mapped on this GPU (own: local)
     long long row0, rows_total;       // this rank's first output row; the product's rows
     int rank, world, on;              // on = 0: an unsharded launch
+    // The previous row-sharded product's gather, finished by this launch (fin_on): its y[t][rows]
+    // still lacks the peers' rows, which sit in this rank's staging image of the latest round.
+    // The compute warps wait (bounded) for every peer's flag of that round, then the CTAs copy
+    // those rows into fin_y, each CTA a share, before or while this product runs (this product's
+    // x does not overlap fin_y: the host finishes the gather with its own kernel otherwise).
+    float *fin_y;
+    long long fin_rows;
+    int fin_t, fin_on;
 };
 
 template <int NJ>

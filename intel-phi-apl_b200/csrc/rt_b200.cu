@@ -94,6 +94,11 @@ struct Ctx {
     unsigned char *peer_local = nullptr;
     unsigned char *peer_map[q8::MAX_PEERS] = {};
     bool peer_ok = false;
+    // the last row-sharded product whose peers' rows are not in its y yet (its gather is finished
+    // by the next such product's kernel, or by the finish kernel at the next anything else)
+    bool pending = false;
+    float *pending_y = nullptr;
+    long long pending_rows = 0, pending_t = 0;
     void *scratch = nullptr; // grows on demand (the tensor-core path's fp16 x)
     size_t scratch_bytes = 0;
     // chains (rt_b200_chain_begin .. rt_b200_chain_end): recorded rounds, and the device counters
@@ -127,6 +132,9 @@ WriteValue32 write_value32() {
     });
     return fn;
 }
+
+bool flush_pending(Ctx *c);
+bool overlaps(const void *a, size_t na, const void *b, size_t nb);
 
 // Errors of the calls that take no struct rt.
 thread_local int t_status = RTB_OK;
@@ -240,7 +248,7 @@ bool read_error_word(Ctx *c) {
 bool finish(Ctx *c) {
     if (c->async)
         return true;
-    return read_error_word(c);
+    return flush_pending(c) && read_error_word(c); // a blocking call returns with y whole
 }
 
 // The output rows rank `rank` of `world` computes of a product with `rows` rows, and where they
@@ -314,9 +322,44 @@ bool peer_gatherable(const Ctx *c, const std::vector<Item> &items) {
            size_t(it.t) * size_t(it.rows) * sizeof(float) <= q8::PEER_STAGE_BYTES;
 }
 
+q8::PeerOut peer_out(const Ctx *c) {
+    q8::PeerOut po;
+    memset(&po, 0, sizeof po);
+    for (int w = 0; w < c->world; ++w)
+        po.region[w] = c->peer_map[w];
+    po.rank = c->rank;
+    po.world = c->world;
+    return po;
+}
+
+// Finishes the pending gather with its own kernel (waits for the peers' flags, copies their rows).
+bool flush_pending(Ctx *c) {
+    if (!c->pending)
+        return true;
+    c->pending = false;
+    q8::PeerOut po = peer_out(c);
+    po.on = 1;
+    po.rows_total = c->pending_rows;
+    return cuda_ok(c, q8::launch_peer_finish(po, c->pending_y, c->pending_rows, int(c->pending_t), c->d_err, c->stream,
+                                             c->overlap),
+                   "peer gather");
+}
+
 bool run_peer_gathered(Ctx *c, const Item &it) {
     long long lr, r0;
     shard_rows(c, it.rows, &lr, &r0);
+    // The pending gather is finished inside this launch unless this product's x or y touches the
+    // pending y (then it must be complete first).
+    bool fin = c->pending;
+    if (fin) {
+        const size_t pb = size_t(c->pending_t * c->pending_rows) * 4;
+        if (overlaps(it.x, size_t(it.t * it.cols) * 4, c->pending_y, pb) ||
+            overlaps(it.y, size_t(it.t * it.rows) * 4, c->pending_y, pb)) {
+            if (!flush_pending(c))
+                return false;
+            fin = false;
+        }
+    }
     q8::GemvParams p;
     memset(&p, 0, sizeof p);
     p.err = c->d_err;
@@ -334,17 +377,24 @@ bool run_peer_gathered(Ctx *c, const Item &it) {
     j.cols = int(it.cols);
     j.m = int(it.t);
     q8::PeerOut &po = p.peer;
-    for (int w = 0; w < c->world; ++w)
-        po.region[w] = c->peer_map[w];
+    po = peer_out(c);
     po.row0 = r0;
     po.rows_total = it.rows;
-    po.rank = c->rank;
-    po.world = c->world;
     po.on = 1;
+    if (fin) {
+        po.fin_on = 1;
+        po.fin_y = c->pending_y;
+        po.fin_rows = c->pending_rows;
+        po.fin_t = int(c->pending_t);
+        c->pending = false;
+    }
     if (!cuda_ok(c, q8::launch_gemv(p, c->num_sms, 0, c->stream, c->overlap), "gemv launch"))
         return false;
-    return cuda_ok(c, q8::launch_peer_finish(po, it.y, it.rows, int(it.t), c->d_err, c->stream, c->overlap),
-                   "peer gather");
+    c->pending = true; // this product's gather: finished by whatever runs next
+    c->pending_y = it.y;
+    c->pending_rows = it.rows;
+    c->pending_t = it.t;
+    return true;
 }
 
 // Splits the items into kernel jobs (t >= 16: one tensor-core job; else passes of <= 4 tokens on
@@ -353,6 +403,8 @@ bool run_items(Ctx *c, const std::vector<Item> &items) {
     c->synced = false;
     if (peer_gatherable(c, items))
         return run_peer_gathered(c, items[0]);
+    if (!flush_pending(c))
+        return false;
     std::vector<q8::GemvJob> jobs;
     std::vector<q8::GemmJob> tc;
     for (const Item &it : items) {
@@ -826,6 +878,7 @@ void rt_b200_free(struct rt *R) {
     Ctx *c = static_cast<Ctx *>(R->chain);
     if (c->round_open) // release the pre-launched kernel: its results are not wanted
         release_gate(c, false);
+    flush_pending(c);
     cudaStreamSynchronize(c->stream);
     cudaStreamSynchronize(c->link);
     drop_peers(c);
@@ -1076,6 +1129,7 @@ int rt_b200_sync(struct rt *R) {
     // An open round whose go never came: its kernel gives up on the gate (about a second) and
     // reports it through the error word; the round is closed either way.
     c->round_open = false;
+    flush_pending(c);
     read_error_word(c);
     cuda_ok(c, cudaStreamSynchronize(c->link), "synchronize the link stream");
     return c->status;
@@ -1091,6 +1145,8 @@ int rt_b200_pull(struct rt *R, void *dev, const void *host, size_t bytes) {
     }
     // while a round is open its kernel is already on R's stream, waiting for this x: the copy goes
     // on the link stream, which rt_gemv_go then orders before the gate's release
+    if (!c->round_open && !flush_pending(c)) // (a pending gather must not land on what this copies)
+        return c->status;
     cudaStream_t s = c->round_open ? c->link : c->stream;
     if (!c->round_open)
         c->synced = false;
@@ -1107,6 +1163,8 @@ int rt_b200_push(struct rt *R, void *host, const void *dev, size_t bytes) {
         ctx_err(c, RTB_EINVAL, "rt_b200_push: null pointer");
         return RTB_EINVAL;
     }
+    if (!flush_pending(c)) // y whole before it crosses
+        return c->status;
     if (bytes && !cuda_ok(c, cudaMemcpyAsync(host, dev, bytes, cudaMemcpyDeviceToHost, c->stream), "rt_b200_push"))
         return c->status;
     read_error_word(c); // waits for the stream: the bytes have landed, kernel errors surface here
@@ -1121,9 +1179,18 @@ void *rt_b200_stream(struct rt *R) {
 void rt_b200_set_stream(struct rt *R, void *stream) {
     Ctx *c = ctx_of(R);
     if (c) {
+        flush_pending(c); // on the stream it was left on
         c->stream = stream ? static_cast<cudaStream_t>(stream) : c->own_stream;
         c->synced = false;
     }
+}
+
+int rt_b200_flush(struct rt *R) {
+    Ctx *c = ctx_of(R);
+    if (!c)
+        return RTB_ENOTINIT;
+    flush_pending(c);
+    return c->status;
 }
 
 int rt_b200_nccl_id(void *out128) {
@@ -1145,6 +1212,7 @@ int rt_b200_shard(struct rt *R, int rank, int world, const void *nccl_id) {
         ctx_err(c, RTB_EINVAL, "rt_b200_shard: rank %d world %d", rank, world);
         return RTB_EINVAL;
     }
+    flush_pending(c);
     cudaStreamSynchronize(c->stream);
     drop_peers(c);
     if (c->comm) {

@@ -29,7 +29,7 @@ EXPORTS = ("rt_init", "rt_gemv", "rt_gemv_q", "rt_gemv_open", "rt_gemv_go", "rt_
            "rt_b200_free", "rt_b200_nccl_id", "rt_b200_shard", "rt_b200_peer_gather", "rt_b200_chain_begin",
            "rt_b200_chain_end", "rtb_gguf_info", "rt_b200_load_gguf", "rtb_load_error", "rtb_synth_q8_0",
            "rtb_synth_f32", "rt_gemm_static", "rt_b200_pull", "rt_b200_push", "rt_b200_wait_probe", "gemv_i_bytes",
-           "gemv_i_repack", "gemv_i_repack_thread", "rt_b200_shard_rows")
+           "gemv_i_repack", "gemv_i_repack_thread", "rt_b200_shard_rows", "rt_b200_flush")
 
 
 class RtError(RuntimeError):
@@ -101,6 +101,7 @@ def load() -> C.CDLL:
         "rt_b200_nccl_id": ([_P], C.c_int),
         "rt_b200_shard": ([R, C.c_int, C.c_int, _P], C.c_int),
         "rt_b200_peer_gather": ([R], C.c_int),
+        "rt_b200_flush": ([R], C.c_int),
         "rt_b200_shard_rows": ([_L, C.c_int, C.c_int, C.POINTER(_L), C.POINTER(_L)], C.c_int),
         "rt_b200_wait_probe": ([R], C.c_int),
         "rt_b200_chain_begin": ([R], C.c_int),
@@ -331,6 +332,13 @@ class Runtime:
             raise RtError(code, self.lib.rtb_load_error().decode(errors="replace"))
         stats = {k: getattr(st, k) for k, _ in LoadStats._fields_}
         return [_tensor_dict(arr[i]) for i in range(n.value)], stats
+
+    def flush(self) -> None:
+        """rt_b200_flush: enqueue the finish of a pending row-sharded gather (capturable)."""
+        code = self.lib.rt_b200_flush(self._ref)
+        if code:
+            _check(self)
+            raise RtError(code, "rt_b200_flush")
 
     def peer_gather(self) -> bool:
         """True when single products gather y in their own kernel (else through NCCL)."""

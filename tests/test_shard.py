@@ -120,11 +120,22 @@ def _gpu_rank_main(rank: int, world: int, nid: bytes, out) -> None:
         rt.gemv(w.data_ptr(), rows, cols, x.data_ptr(), y1.data_ptr())
         rt.gemm_silu(w.data_ptr(), w2.data_ptr(), rows, cols, x.data_ptr(), 1, ys.data_ptr())
         rt.gemm(w.data_ptr(), rows, cols, x.data_ptr(), 16, y16.data_ptr())  # tensor cores, NCCL gather
-        # rounds back to back (alternating staging images), each on its own x row
+        # rounds back to back (alternating staging images), each on its own x row, blocking
         for k in range(5):
             yk = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
             rt.gemv(w.data_ptr(), rows, cols, x[k].data_ptr(), yk.data_ptr())
             rounds.append(yk)
+        # and async: each product finishes the previous one's gather in its own kernel; a chain
+        # whose x is the previous y (x overlaps the pending y: finished by its own kernel first)
+        rt.set_async(True)
+        for k in range(5):
+            yk = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
+            rt.gemv(w.data_ptr(), rows, cols, x[7 + k].data_ptr(), yk.data_ptr())
+            rounds.append(yk)
+        ya = torch.full((rows // 2,), float("nan"), dtype=torch.float32, device="cuda")
+        rt.gemv(w.data_ptr(), rows // 2, cols, rounds[-1].data_ptr(), ya.data_ptr())  # x: part of the pending y
+        rt.sync()
+        rt.set_async(False)
         # one round captured as a CUDA graph and replayed twice: the round count lives on the GPU
         yg = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
         rt.set_async(True)
@@ -135,6 +146,7 @@ def _gpu_rank_main(rank: int, world: int, nid: bytes, out) -> None:
             with torch.cuda.graph(g, stream=s):
                 rt.set_stream(torch.cuda.current_stream().cuda_stream)
                 rt.gemv(w.data_ptr(), rows, cols, x[6].data_ptr(), yg.data_ptr())
+                rt.flush()  # the graph finishes its own last gather
         torch.cuda.current_stream().wait_stream(s)
         rt.set_stream(torch.cuda.current_stream().cuda_stream)
         for _ in range(2):
@@ -144,7 +156,7 @@ def _gpu_rank_main(rank: int, world: int, nid: bytes, out) -> None:
         rt.sync()
         del g
     out.put((rank, peer, y.cpu().numpy(), y1.cpu().numpy(), ys.cpu().numpy(), y16.cpu().numpy(),
-             [r.cpu().numpy() for r in rounds], yg.cpu().numpy()))
+             [r.cpu().numpy() for r in rounds], yg.cpu().numpy(), ya.cpu().numpy()))
 
 
 @pytest.mark.gpu
@@ -175,7 +187,7 @@ def test_row_shards_on_two_gpus(cuda, rtb, oracle):
     u = oracle.gemv(q8u, rows, cols, x[0])
     want_silu = (g / (1.0 + np.exp(-g.astype(np.float64))) * u).astype(np.float32)
     want16 = oracle.gemm_f64(q8, rows, cols, x, 16)
-    for _, peer, y, y1, ys, y16, rounds, yg in res:
+    for _, peer, y, y1, ys, y16, rounds, yg, ya in res:
         assert peer, "the in-kernel gather was not set up"
         assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
         assert np.array_equal(y1.view(np.uint32), want[0].view(np.uint32))
@@ -183,5 +195,13 @@ def test_row_shards_on_two_gpus(cuda, rtb, oracle):
         rms = np.sqrt(np.mean(want16 ** 2))
         assert np.max(np.abs(y16 - want16)) / rms < 2e-3
         for k, yk in enumerate(rounds):
-            assert np.array_equal(yk.view(np.uint32), oracle.gemv(q8, rows, cols, x[k]).view(np.uint32))
+            xk = x[k] if k < 5 else x[7 + k - 5]
+            assert np.array_equal(yk.view(np.uint32), oracle.gemv(q8, rows, cols, xk).view(np.uint32)), k
+        # the product of rows // 2 rows over each rank's first rows // 4 shard rows, its x the first
+        # cols entries of the last async round's y: every rank's product is the big matrix's rows
+        # [k * rows/2, k * rows/2 + rows/4) for rank k
+        xa = rounds[-1][:cols]
+        want_a = np.concatenate([oracle.gemv(oracle.synth_q8_0(rows // 4, cols, 11, 5, row0=k * rows // 2), rows // 4,
+                                             cols, xa) for k in range(2)])
+        assert np.array_equal(ya.view(np.uint32), want_a.view(np.uint32))
         assert np.array_equal(yg.view(np.uint32), oracle.gemv(q8, rows, cols, x[6]).view(np.uint32))
