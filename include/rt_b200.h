@@ -205,9 +205,9 @@ RTB_API void rt_b200_free(struct rt *R);
  * - A single product of <= 4 tokens (rt_gemv, rt_gemm, rt_gemm_silu) gathers y over NVLink
  *   without NCCL: every output is also stored into each peer's staging buffer (CUDA IPC mappings
  *   set up by rt_b200_shard) and the last CTA raises a flag on every peer. The peers' rows are then
- *   copied into y by the next such product's own kernel (after it has waited, bounded, for the
- *   flags; its weights stream meanwhile), or, before anything else is run, pulled or pushed, or
- *   when R is synchronized or flushed, by a small kernel of their own. So in async mode y is
+ *   copied into y by the next such product's own kernel, after its own rows (by then the peers'
+ *   flags are normally up; the wait is bounded), or, before anything else is run, pulled or
+ *   pushed, or when R is synchronized or flushed, by a small kernel of their own. So in async mode y is
  *   whole once the next call on R has been made; blocking calls return with y whole. A sequence
  *   captured into a CUDA graph must end with rt_b200_flush, so that the graph finishes its last
  *   gather itself.

@@ -287,30 +287,31 @@ __device__ __noinline__ bool wait_flag64(const unsigned long long *flag, unsigne
     }
 }
 
-// The previous product's gather, run by the compute threads of a row-sharded launch before they
-// read x: wait for the peers' flags of that product's round (compute thread 0, bounded; the others
-// through the CTA barrier's first phase), then copy this CTA's share of the peers' rows from this
-// GPU's staging image into the product's y. The previous product has completed (the grid wait),
-// so the local round counter is final. Kept out of line: the product loop's registers stay its own.
-__device__ __noinline__ void peer_finish_prologue(const PeerOut &po, uint64_t *depbar, unsigned *err, int tid, int lane) {
+// The previous row-sharded product's gather, run by every thread of a CTA after the CTA's own
+// tiles: thread 0 waits, bounded, for the peers' flags of that product's round (they are normally
+// long up: the peers are past that round too), then the CTA copies its share of the peers' rows
+// from this GPU's staging image of the round into that product's y. This launch's own round is
+// not published yet, so the local round counter still names that product's round.
+__device__ __noinline__ void peer_finish_epilogue(const PeerOut &po, unsigned *err, int nthreads) {
+    __shared__ int ok;
     const unsigned char *mine = po.region[po.rank];
     const unsigned long long round = *reinterpret_cast<const volatile unsigned long long *>(mine + 72);
-    if (tid == 0) {
-        bool ok = true;
-        for (int w = 0; w < po.world && ok; ++w)
+    if (threadIdx.x == 0) {
+        bool good = true;
+        for (int w = 0; w < po.world && good; ++w)
             if (w != po.rank)
-                ok = wait_flag64(reinterpret_cast<const unsigned long long *>(mine) + w, round);
-        if (!ok)
+                good = wait_flag64(reinterpret_cast<const unsigned long long *>(mine) + w, round);
+        if (!good)
             report(err, ERR_TIMEOUT_PEER);
-        mbar_arrive(depbar);
-    } else if (lane == 0 && !mbar_wait(depbar, 0)) {
-        report(err, ERR_TIMEOUT_PEER);
+        ok = good;
     }
-    __syncwarp();
-    const float *stage = reinterpret_cast<const float *>(mine + PEER_HDR + (round & 1) * PEER_STAGE_BYTES);
+    __syncthreads();
+    if (!ok)
+        return;
+    const float *stage = reinterpret_cast<const float *>(mine + peer_image(round));
     const long long rows = po.fin_rows, lr = rows / po.world, own0 = (long long)po.rank * lr;
     const long long n = (long long)po.fin_t * rows;
-    for (long long e = (long long)blockIdx.x * NC + tid; e < n; e += (long long)gridDim.x * NC) {
+    for (long long e = (long long)blockIdx.x * nthreads + threadIdx.x; e < n; e += (long long)gridDim.x * nthreads) {
         const long long tok = e / rows, row = e - tok * rows;
         if (row < own0 || row >= own0 + lr)
             po.fin_y[tok * rows + row] = __ldcg(stage + e);
@@ -372,10 +373,6 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
         int xjob = -1, xc = -1, wjob = -1, ndep = 0;
         const int b = tid % NBK, half = tid / NBK;
         grid_wait(); // x comes from the previous kernel on the stream
-        if (p.peer.fin_on) {
-            peer_finish_prologue(p.peer, depbar, p.err, tid, lane);
-            ndep = 1;
-        }
         if (p.gate) {
             // an opened round: x lands after the launch. Compute thread 0 polls the gate and
             // passes it on through the CTA barrier (its first phase), as for a chained round.
@@ -505,8 +502,8 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
 #pragma unroll
         for (int a = 0; a < ACCS; ++a)
             accs[a] = 0.0f;
-        // A row-sharded launch also stores each output into every peer's staging image of this
-        // round ([t][rows_total], parity of the round being produced).
+        // A row-sharded launch also stores each output into every peer's staging image of the
+        // round being produced ([t][rows_total]).
         const PeerOut &po = p.peer;
         unsigned long long stage_off = 0;
         if (po.on) {
@@ -515,7 +512,7 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
             grid_wait();
             const unsigned long long round0 =
                 *reinterpret_cast<const volatile unsigned long long *>(po.region[po.rank] + 72);
-            stage_off = PEER_HDR + ((round0 + 1) & 1) * PEER_STAGE_BYTES;
+            stage_off = peer_image(round0 + 1);
         }
         auto put = [&](float *y, long long ldy, long long o, float v) {
             y[mt * ldy + o] = v;
@@ -684,9 +681,14 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
     }
 
     if (p.peer.on) {
-        // The last CTA to finish publishes the round: the CTA's peer stores are ordered (barrier,
-        // then one system-scope fence) before its count, the last count before the flags.
+        // The previous product's gather first (its rows land before this round is published),
+        // then the last CTA to finish publishes the round: the CTA's peer stores are ordered
+        // (barrier, then one system-scope fence) before its count, the last count before the flags.
         __syncthreads();
+        if (p.peer.fin_on) {
+            peer_finish_epilogue(p.peer, p.err, C::NT);
+            __syncthreads();
+        }
         if (tid == 0) {
             unsigned char *mine = p.peer.region[p.peer.rank];
             unsigned *done = reinterpret_cast<unsigned *>(mine + 64);

@@ -47,24 +47,33 @@ constexpr int ROUND_CTR_STRIDE = 32;
 //   [64, 68)           uint32 completion counter of the product kernel's CTAs (local use)
 //   [72, 80)           uint64 round: products completed by this rank (advanced on the device, so
 //                      CUDA-graph replays keep counting)
-//   [PEER_HDR, +2*PEER_STAGE_BYTES)  two staging images of y, [t][rows] fp32, by round parity.
-// The product kernel stores every output into its local y and into the current staging image of
-// every peer; its last CTA advances `round` and raises its flag on every peer. launch_peer_finish
-// then waits (bounded) for all peers' flags and copies their rows from staging into y.
+//   [PEER_HDR, +PEER_IMAGES*PEER_STAGE_BYTES)  staging images of y, [t][rows] fp32, round r in
+//                      image r % PEER_IMAGES.
+// The product kernel of round r stores every output into its local y and into image r of every
+// peer; its last CTA advances `round` and raises its flag on every peer. Round r's gather is
+// finished by the next row-sharded product (at its end, after its own rows: by then the peers are
+// done with round r) or by launch_peer_finish: both wait (bounded) for all peers' flags of round r
+// and copy the peers' rows from image r into y. Three images: a rank's round r+1 ends only after
+// it has seen every peer's flag of round r, which that peer raised after copying out its round
+// r-1 rows, so no peer writes round r+2 into an image that is still being read.
 constexpr int MAX_PEERS = 8;
 constexpr size_t PEER_HDR = 256;
+constexpr int PEER_IMAGES = 3;
 constexpr size_t PEER_STAGE_BYTES = size_t(16) << 20;
-constexpr size_t PEER_REGION_BYTES = PEER_HDR + 2 * PEER_STAGE_BYTES;
+constexpr size_t PEER_REGION_BYTES = PEER_HDR + PEER_IMAGES * PEER_STAGE_BYTES;
+__host__ __device__ constexpr size_t peer_image(unsigned long long round) {
+    return PEER_HDR + size_t(round % PEER_IMAGES) * PEER_STAGE_BYTES;
+}
 
 struct PeerOut {
     unsigned char *region[MAX_PEERS]; // every rank's region as mapped on this GPU (own: local)
     long long row0, rows_total;       // this rank's first output row; the product's rows
     int rank, world, on;              // on = 0: an unsharded launch
     // The previous row-sharded product's gather, finished by this launch (fin_on): its y[t][rows]
-    // still lacks the peers' rows, which sit in this rank's staging image of the latest round.
-    // The compute warps wait (bounded) for every peer's flag of that round, then the CTAs copy
-    // those rows into fin_y, each CTA a share, before or while this product runs (this product's
-    // x does not overlap fin_y: the host finishes the gather with its own kernel otherwise).
+    // still lacks the peers' rows, which sit in this rank's staging image of that round. After its
+    // own tiles each CTA waits (bounded) for every peer's flag of that round and copies a share of
+    // those rows into fin_y, before the launch publishes its own round (this product's x and y do
+    // not overlap fin_y: the host finishes the gather with its own kernel otherwise).
     float *fin_y;
     long long fin_rows;
     int fin_t, fin_on;

@@ -44,7 +44,7 @@ __global__ void peer_finish_kernel(const PeerOut po, float *y, long long ldy, in
     __syncthreads();
     if (!ok)
         return;
-    const float *stage = reinterpret_cast<const float *>(mine + PEER_HDR + (round & 1) * PEER_STAGE_BYTES);
+    const float *stage = reinterpret_cast<const float *>(mine + peer_image(round));
     const long long rows = po.rows_total, lr = rows / po.world, own0 = (long long)po.rank * lr;
     const long long n = (long long)t * rows;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
