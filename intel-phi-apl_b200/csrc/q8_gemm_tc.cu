@@ -545,13 +545,22 @@ __global__ void __launch_bounds__(TcShape<CPS>::NT, CPS) gemm_tc_kernel(const __
 
 // The pre-pass of a job, before its product on the stream. Blocks [0, t): one token each: the
 // largest |x| of the token gives s_t (|x| * 2^s_t <= 2^15 at that entry; s_t <= 126), then
-// xh = fp16(x * 2^s_t) and tokf[t] = 2^-s_t. Blocks from t: one warp per matrix row (W's rows, then
-// a pair's up rows): the row's largest scale gives r_o (row_exponent) into rexp.
+// xh = fp16(x * 2^s_t) and tokf[t] = 2^-s_t. Blocks from t: the matrix rows (W's rows, then a
+// pair's up rows), a half-warp per row: the row's largest scale gives r_o (row_exponent) into rexp.
 constexpr int PREP_THREADS = 256;
 
+// RPB rows per half-warp and batch: 8 where the matrix has rows enough to give every SM a block
+// of 16-row warps, else 1 (a few deep blocks on a small matrix leave most SMs idle).
+template <int RPB>
 __global__ void __launch_bounds__(PREP_THREADS) tc_prep_kernel(const float *x, long long ldx, int cols, int t,
                                                                __half *xh, float *tokf, const uint8_t *w,
                                                                const uint8_t *w2, long long rows, int8_t *rexp) {
+    // Under programmatic launch the product may start its prologue now; this pass waits for the
+    // kernel before it (x is its output, and the scratch written here may still be read by the
+    // previous product).
+    if (threadIdx.x == 0)
+        grid_launch_dependents();
+    grid_wait();
     if (blockIdx.x < unsigned(t)) {
         __shared__ float part[PREP_THREADS / 32];
         __shared__ int s_sh;
@@ -585,24 +594,45 @@ __global__ void __launch_bounds__(PREP_THREADS) tc_prep_kernel(const float *x, l
             ht[c] = __float2half_rn(xt[c] * f);
         return;
     }
+    // The row exponents: a half-warp per row, 16-byte chunks of the row's scales, RPB rows per
+    // half-warp at a time so that RPB loads per lane are in flight (a warp per row with one load
+    // in flight left this pass latency-bound on large matrices: 28 us on the 151936-row head).
     const long long nrows = w2 ? 2 * rows : rows;
     const long long rb = q8s_row_bytes(cols), nsc16 = q8s_scale_stride(cols) / 8; // 16-byte scale chunks
-    const int lane = threadIdx.x % 32;
-    const long long wstep = (long long)(gridDim.x - t) * (PREP_THREADS / 32);
-    for (long long o = (long long)(blockIdx.x - t) * (PREP_THREADS / 32) + threadIdx.x / 32; o < nrows; o += wstep) {
-        const uint8_t *row = (o < rows ? w + o * rb : w2 + (o - rows) * rb) + cols;
-        unsigned mb = 0;
-        for (long long k = lane; k < nsc16; k += 32) {
-            const uint4 v = __ldg(reinterpret_cast<const uint4 *>(row) + k);
-            const unsigned a[4] = {v.x, v.y, v.z, v.w};
+    const int lane = threadIdx.x % 32, half = lane >> 4, hl = lane & 15;
+    const long long wstep = (long long)(gridDim.x - t) * (PREP_THREADS / 32) * (2 * RPB);
+    for (long long base = ((long long)(blockIdx.x - t) * (PREP_THREADS / 32) + threadIdx.x / 32) * (2 * RPB); base < nrows;
+         base += wstep) {
+        unsigned mb[RPB];
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                mb = max(mb, max(a[j] & 0x7fffu, (a[j] >> 16) & 0x7fffu));
+        for (int j = 0; j < RPB; ++j)
+            mb[j] = 0;
+#pragma unroll 4
+        for (long long k = hl; k < nsc16; k += 16) {
+            uint4 v[RPB];
+#pragma unroll
+            for (int j = 0; j < RPB; ++j) {
+                const long long o = base + 2 * j + half;
+                v[j] = make_uint4(0, 0, 0, 0);
+                if (o < nrows)
+                    v[j] = __ldg(reinterpret_cast<const uint4 *>((o < rows ? w + o * rb : w2 + (o - rows) * rb) + cols) + k);
+            }
+#pragma unroll
+            for (int j = 0; j < RPB; ++j) {
+                const unsigned a4[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    mb[j] = max(mb[j], max(a4[q] & 0x7fffu, (a4[q] >> 16) & 0x7fffu));
+            }
         }
-        for (int off = 16; off; off >>= 1)
-            mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, off));
-        if (lane == 0)
-            rexp[o] = int8_t(row_exponent(mb));
+#pragma unroll
+        for (int j = 0; j < RPB; ++j) {
+            for (int off = 8; off; off >>= 1)
+                mb[j] = max(mb[j], __shfl_xor_sync(0xffffffffu, mb[j], off));
+            const long long o = base + 2 * j + half;
+            if (hl == 0 && o < nrows)
+                rexp[o] = int8_t(row_exponent(mb[j]));
+        }
     }
 }
 
@@ -610,6 +640,9 @@ __global__ void __launch_bounds__(PREP_THREADS) tc_prep_kernel(const float *x, l
 // planes come first, then the up planes, and y = silu(gate sum) * (up sum).
 __global__ void splitk_reduce_kernel(const float *part, int ks, int pair, long long rows, int t, float *y,
                                      long long ldy) {
+    if (threadIdx.x == 0)
+        grid_launch_dependents();
+    grid_wait(); // the product's partial planes
     const long long n = (long long)t * rows, plane = n;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
         const long long tok = i / rows, row = i - tok * rows;
@@ -624,6 +657,22 @@ __global__ void splitk_reduce_kernel(const float *part, int ks, int pair, long l
         }
         y[tok * ldy + row] = g;
     }
+}
+
+// A small kernel of the product's launch sequence, with programmatic dependent launch when pdl.
+template <class... KArgs, class... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, cudaStream_t stream, bool pdl,
+                       Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
 // ---------------------------------------------------------------- host: tensor maps
@@ -783,7 +832,8 @@ cudaError_t preload_gemm_tc() {
     if ((e = setup_shape<1>()) != cudaSuccess || (e = setup_shape<2>()) != cudaSuccess)
         return e;
     cudaFuncAttributes a;
-    if ((e = cudaFuncGetAttributes(&a, tc_prep_kernel)) != cudaSuccess)
+    if ((e = cudaFuncGetAttributes(&a, tc_prep_kernel<1>)) != cudaSuccess ||
+        (e = cudaFuncGetAttributes(&a, tc_prep_kernel<8>)) != cudaSuccess)
         return e;
     return cudaFuncGetAttributes(&a, splitk_reduce_kernel);
 }
@@ -840,11 +890,15 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
         sc += x_bytes(G);
         {
             const long long nrows = G.rows * (G.w2 ? 2 : 1);
-            long long rblocks = (nrows + PREP_THREADS / 32 - 1) / (PREP_THREADS / 32);
+            const int sms = num_sms > 0 ? num_sms : 148;
+            const bool deep = nrows >= (long long)sms * (PREP_THREADS / 32) * 16;
+            const long long rows_per_block = (PREP_THREADS / 32) * 2 * (deep ? 8 : 1);
+            long long rblocks = (nrows + rows_per_block - 1) / rows_per_block;
             rblocks = rblocks > 1184 ? 1184 : rblocks;
-            tc_prep_kernel<<<unsigned(G.t + rblocks), PREP_THREADS, 0, stream>>>(G.x, G.ldx, G.cols, G.t, xh, tokf, G.w,
-                                                                               G.w2, G.rows, rexp);
-            cudaError_t e = cudaGetLastError();
+            cudaError_t e = deep ? launch_pdl(tc_prep_kernel<8>, unsigned(G.t + rblocks), PREP_THREADS, stream, pdl, G.x,
+                                              G.ldx, G.cols, G.t, xh, tokf, G.w, G.w2, G.rows, rexp)
+                                 : launch_pdl(tc_prep_kernel<1>, unsigned(G.t + rblocks), PREP_THREADS, stream, pdl, G.x,
+                                              G.ldx, G.cols, G.t, xh, tokf, G.w, G.w2, G.rows, rexp);
             if (e != cudaSuccess)
                 return e;
         }
@@ -890,8 +944,8 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
         const long long outs = (long long)J.t * J.rows;
         int g = int((outs + 255) / 256);
         g = g > 8192 ? 8192 : g;
-        splitk_reduce_kernel<<<g, 256, 0, stream>>>(J.part, J.ks, J.pair, J.rows, J.t, J.y, J.ldy);
-        if ((e = cudaGetLastError()) != cudaSuccess)
+        if ((e = launch_pdl(splitk_reduce_kernel, unsigned(g), 256, stream, pdl, static_cast<const float *>(J.part), J.ks,
+                            int(J.pair), J.rows, J.t, J.y, J.ldy)) != cudaSuccess)
             return e;
     }
     return cudaSuccess;
