@@ -190,6 +190,20 @@ RTB_API int rt_b200_push(struct rt *R, void *host, const void *dev, size_t bytes
  * products start after the previous kernel completes, as plain stream order. */
 RTB_API void rt_b200_set_overlap(struct rt *R, int on);
 
+/* No counterpart in the reference (its link_push is a DMA copy, src/card/link.c:105-118). 1: a
+ * round's y may come back from its own product kernel. In async mode rt_gemv_go then holds back a
+ * round of one CUDA-core product (t <= 4, one GPU, no chain, R's stream not being captured)
+ * instead of launching it, and the next call on R launches it. When that call is rt_b200_push of
+ * exactly that product's y (dev = y, bytes = t * rows * 4) into pinned host memory the GPU can
+ * write (cudaHostAlloc, or cudaHostRegister'd and mapped: on 64-bit systems with unified
+ * addressing any pinned memory), the kernel also stores each output there and its last CTA raises
+ * a flag in mapped host memory; push returns once the host sees the flag (y is then whole on the
+ * host) with the round's error status, without a device-to-host copy or a stream synchronization.
+ * Any other call on R, or a push of anything else, launches the held round first as rt_gemv_go
+ * would have. The caller vouches that between rt_gemv_go and its next call on R it enqueues
+ * nothing of its own on R's stream that needs the held product. 0 (default): go launches at once. */
+RTB_API void rt_b200_set_push_direct(struct rt *R, int on);
+
 /* R's CUDA stream (a cudaStream_t); set_stream makes R use the caller's stream instead (NULL:
  * back to R's own; the legacy default stream is cudaStreamLegacy, not NULL). */
 RTB_API void *rt_b200_stream(struct rt *R);

@@ -514,8 +514,11 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
                 *reinterpret_cast<const volatile unsigned long long *>(po.region[po.rank] + 72);
             stage_off = peer_image(round0 + 1);
         }
+        float *const yh = p.y_host;
         auto put = [&](float *y, long long ldy, long long o, float v) {
             y[mt * ldy + o] = v;
+            if (yh)
+                yh[mt * ldy + o] = v; // the round's only job: y's own layout, in host memory
             if (po.on) {
                 const long long gi = mt * po.rows_total + po.row0 + o;
                 for (int w = 0; w < po.world; ++w)
@@ -704,6 +707,19 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
                         unsigned long long *flag = reinterpret_cast<unsigned long long *>(p.peer.region[w]) + p.peer.rank;
                         asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(flag), "l"(e) : "memory");
                     }
+            }
+        }
+    }
+    if (p.y_host) {
+        // The last CTA to finish tells the host: each CTA's host stores are ordered (barrier, then
+        // one system-scope fence) before its count, the last count before the flag.
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence_system();
+            if (atomicAdd(p.host_ctr, 1u) == gridDim.x - 1) {
+                *p.host_ctr = 0;
+                __threadfence_system();
+                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.host_flag), "r"(p.host_seq) : "memory");
             }
         }
     }

@@ -7,6 +7,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <atomic>
 #include <bitset>
 #include <cstdarg>
 #include <cstdio>
@@ -114,6 +115,17 @@ struct Ctx {
     cudaStream_t link = nullptr;
     cudaEvent_t ev_before = nullptr, ev_link = nullptr;
     bool round_open = false;
+    // direct pushes (rt_b200_set_push_direct): a round of one CUDA-core product that rt_gemv_go
+    // held back instead of launching, its launch left to the next call on R; the host word the
+    // product's last CTA raises (mapped, beside the error mirror), its device address, the CTA
+    // counter behind it and the rounds pushed so far
+    bool direct = false;
+    bool held = false;
+    Item held_item;
+    volatile unsigned *h_flag = nullptr;
+    unsigned *h_flag_dev = nullptr;
+    unsigned *d_hctr = nullptr;
+    unsigned host_seq = 0;
 };
 
 // cuStreamWriteValue32 (the driver's stream memory operation: executed by the GPU's front end in
@@ -135,6 +147,7 @@ WriteValue32 write_value32() {
 
 bool flush_pending(Ctx *c);
 bool overlaps(const void *a, size_t na, const void *b, size_t nb);
+bool launch_held(Ctx *c);
 
 // Errors of the calls that take no struct rt.
 thread_local int t_status = RTB_OK;
@@ -161,12 +174,21 @@ void thread_err(int code, const char *fmt, ...) {
     va_end(ap);
 }
 
-Ctx *ctx_of(struct rt *R) {
+Ctx *ctx_raw(struct rt *R) {
     if (!R || !R->chain) {
         thread_err(RTB_ENOTINIT, "struct rt not initialised by rt_init");
         return nullptr;
     }
     return static_cast<Ctx *>(R->chain);
+}
+
+// R's context for an entry point, after launching a round rt_gemv_go held back (every call on R but
+// rt_b200_push, which may launch it with y going straight to the host, comes after that launch).
+Ctx *ctx_of(struct rt *R) {
+    Ctx *c = ctx_raw(R);
+    if (c && c->held)
+        launch_held(c);
+    return c;
 }
 
 bool cuda_ok(Ctx *c, cudaError_t e, const char *what) {
@@ -397,6 +419,24 @@ bool run_peer_gathered(Ctx *c, const Item &it) {
     return true;
 }
 
+// The CUDA-core job of tokens [k, k + 4) of a product (rows lr from r0 on this rank).
+q8::GemvJob cuda_core_job(const Item &it, long long k, long long lr, long long r0) {
+    q8::GemvJob j;
+    memset(&j, 0, sizeof j);
+    j.w = it.w;
+    j.w2 = it.kind == K_SILU ? it.w2 : nullptr;
+    j.idx = it.kind == K_ROWS ? it.idx : nullptr;
+    j.x = it.x + k * it.cols;
+    j.ldx = it.cols;
+    j.ldy = it.rows;
+    j.y = it.y + k * it.rows + r0;
+    j.rows = lr;
+    j.src_rows = it.kind == K_ROWS ? it.src_rows : lr;
+    j.cols = int(it.cols);
+    j.m = int(it.t - k < q8::GEMV_MAX_T ? it.t - k : q8::GEMV_MAX_T);
+    return j;
+}
+
 // Splits the items into kernel jobs (t >= 16: one tensor-core job; else passes of <= 4 tokens on
 // CUDA cores), launches them, then all-gathers the sharded outputs.
 bool run_items(Ctx *c, const std::vector<Item> &items) {
@@ -426,22 +466,8 @@ bool run_items(Ctx *c, const std::vector<Item> &items) {
             tc.push_back(g);
             continue;
         }
-        for (long long k = 0; k < it.t; k += q8::GEMV_MAX_T) {
-            q8::GemvJob j;
-            memset(&j, 0, sizeof j);
-            j.w = it.w;
-            j.w2 = it.kind == K_SILU ? it.w2 : nullptr;
-            j.idx = it.kind == K_ROWS ? it.idx : nullptr;
-            j.x = it.x + k * it.cols;
-            j.ldx = it.cols;
-            j.ldy = it.rows;
-            j.y = it.y + k * it.rows + r0;
-            j.rows = lr;
-            j.src_rows = it.kind == K_ROWS ? it.src_rows : lr;
-            j.cols = int(it.cols);
-            j.m = int(it.t - k < q8::GEMV_MAX_T ? it.t - k : q8::GEMV_MAX_T);
-            jobs.push_back(j);
-        }
+        for (long long k = 0; k < it.t; k += q8::GEMV_MAX_T)
+            jobs.push_back(cuda_core_job(it, k, lr, r0));
     }
     if (!flush_gemv(c, jobs) || !flush_tc(c, tc))
         return false;
@@ -481,6 +507,82 @@ bool run_now(Ctx *c, const Item &it) {
         return true;
     }
     return run_items(c, one) && finish(c);
+}
+
+// ---------------------------------------------------------------- direct pushes
+
+// A round rt_gemv_go may hold back for a direct push: direct pushes on, async, one GPU, no chain,
+// and one CUDA-core product of one pass (<= 4 tokens); never while the stream is being captured
+// (a held launch could then miss the graph).
+bool holdable(Ctx *c, const std::vector<Item> &items) {
+    if (!c->direct || !c->async || c->chaining || c->world > 1 || items.size() != 1 || items[0].t > q8::GEMV_MAX_T)
+        return false;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    return cudaStreamIsCapturing(c->stream, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusNone;
+}
+
+bool launch_held(Ctx *c) {
+    if (!c->held)
+        return true;
+    c->held = false;
+    std::vector<Item> one(1, c->held_item);
+    return run_items(c, one);
+}
+
+// The device's address of host memory the GPU can write (pinned and mapped), else null.
+float *mapped(void *host) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, host) != cudaSuccess) {
+        cudaGetLastError(); // (an unregistered pointer: not an error of R's)
+        return nullptr;
+    }
+    return a.type == cudaMemoryTypeHost ? static_cast<float *>(a.devicePointer) : nullptr;
+}
+
+// The held round, launched with its y also stored into host memory (the device address yh) and a
+// host flag raised by its last CTA; returns once the flag is up (y is on the host) or the launch
+// ended without it. The host polls the flag and, now and then, whether the stream has finished: a
+// kernel that faulted raises no flag, and the wait then ends through the stream's error.
+int push_direct(Ctx *c, const Item &it, float *yh) {
+    q8::GemvParams p;
+    memset(&p, 0, sizeof p);
+    p.err = c->d_err;
+    p.early = c->overlap ? 1 : 0;
+    p.njobs = 1;
+    p.job[0] = cuda_core_job(it, 0, it.rows, 0);
+    unsigned seq = ++c->host_seq;
+    if (seq == 0) // (0 is the flag's initial value)
+        seq = c->host_seq = 1;
+    p.y_host = yh;
+    p.host_flag = c->h_flag_dev;
+    p.host_ctr = c->d_hctr;
+    p.host_seq = seq;
+    c->synced = false;
+    if (!cuda_ok(c, q8::launch_gemv(p, c->num_sms, 0, c->stream, c->overlap), "gemv launch"))
+        return c->status;
+    bool up = false;
+    for (unsigned long i = 1;; ++i) {
+        if (*c->h_flag == seq) {
+            up = true;
+            break;
+        }
+        if ((i & 4095) == 0) {
+            const cudaError_t q = cudaStreamQuery(c->stream);
+            if (q != cudaErrorNotReady) {
+                up = *c->h_flag == seq;
+                break;
+            }
+        }
+#if defined(__x86_64__)
+        __builtin_ia32_pause();
+#endif
+    }
+    std::atomic_thread_fence(std::memory_order_acquire);
+    if (*c->h_err || !up) { // a kernel reported (or the launch failed): synchronize and read why
+        if (read_error_word(c) && !up)
+            ctx_err(c, RTB_ECUDA, "rt_b200_push: the product ended without its completion flag");
+    }
+    return c->status;
 }
 
 // ---------------------------------------------------------------- chains
@@ -830,9 +932,10 @@ int rt_init(struct rt *R, int threads) {
         return -1;
     }
     c->stream = c->own_stream;
+    // mapped host words: the error mirror at 0, the direct pushes' flag 128 bytes on
     unsigned *h_err = nullptr, *h_err_dev = nullptr;
     if (q8::preload_gemv() != cudaSuccess || q8::preload_gemm_tc() != cudaSuccess || q8::preload_peer() != cudaSuccess ||
-        cudaHostAlloc(&h_err, sizeof(unsigned), cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostAlloc(&h_err, 256, cudaHostAllocMapped) != cudaSuccess ||
         cudaHostGetDevicePointer(&h_err_dev, h_err, 0) != cudaSuccess) {
         if (h_err)
             cudaFreeHost(h_err);
@@ -840,12 +943,15 @@ int rt_init(struct rt *R, int threads) {
         delete c;
         return -1;
     }
-    *h_err = 0;
+    memset(h_err, 0, 256);
     c->h_err = h_err;
+    c->h_flag = h_err + 32;
+    c->h_flag_dev = h_err_dev + 32;
     if (cudaMalloc(&c->d_err, 16) != cudaSuccess || cudaMemset(c->d_err, 0, 16) != cudaSuccess ||
         cudaMemcpy(c->d_err + 2, &h_err_dev, sizeof h_err_dev, cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMalloc(&c->d_round, sizeof(unsigned) * q8::ROUND_CTR_STRIDE * q8::MAX_CHAIN_JOBS) != cudaSuccess ||
         cudaMalloc(&c->d_gate, sizeof(unsigned)) != cudaSuccess || cudaMemset(c->d_gate, 0, sizeof(unsigned)) != cudaSuccess ||
+        cudaMalloc(&c->d_hctr, sizeof(unsigned)) != cudaSuccess || cudaMemset(c->d_hctr, 0, sizeof(unsigned)) != cudaSuccess ||
         cudaStreamCreateWithFlags(&c->link, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&c->ev_before, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&c->ev_link, cudaEventDisableTiming) != cudaSuccess) {
@@ -853,6 +959,7 @@ int rt_init(struct rt *R, int threads) {
         cudaFree(c->d_err);
         cudaFree(c->d_round);
         cudaFree(c->d_gate);
+        cudaFree(c->d_hctr);
         if (c->link)
             cudaStreamDestroy(c->link);
         if (c->ev_before)
@@ -876,6 +983,7 @@ void rt_b200_free(struct rt *R) {
     if (!R || !R->chain)
         return;
     Ctx *c = static_cast<Ctx *>(R->chain);
+    launch_held(c);
     if (c->round_open) // release the pre-launched kernel: its results are not wanted
         release_gate(c, false);
     flush_pending(c);
@@ -886,6 +994,7 @@ void rt_b200_free(struct rt *R) {
         nccl().CommDestroy(c->comm);
     cudaFree(c->d_round);
     cudaFree(c->d_gate);
+    cudaFree(c->d_hctr);
     cudaFree(c->scratch);
     cudaFree(c->d_err);
     cudaEventDestroy(c->ev_before);
@@ -934,6 +1043,7 @@ void rt_gemv_go(struct rt *R) {
     std::vector<Item> items;
     items.swap(c->queue);
     bool ok = true;
+    const bool was_open = c->round_open;
     if (c->round_open) {
         ok = release_gate(c, !items.empty());
     } else if (items.empty()) {
@@ -942,6 +1052,11 @@ void rt_gemv_go(struct rt *R) {
     if (c->chaining) {
         if (!items.empty())
             c->chain.push_back(items);
+        return;
+    }
+    if (ok && !items.empty() && !was_open && holdable(c, items)) {
+        c->held = true; // launched by the next call on R: a direct push, or any other call
+        c->held_item = items[0];
         return;
     }
     if (ok && (items.empty() || run_items(c, items)))
@@ -1156,12 +1271,26 @@ int rt_b200_pull(struct rt *R, void *dev, const void *host, size_t bytes) {
 }
 
 int rt_b200_push(struct rt *R, void *host, const void *dev, size_t bytes) {
-    Ctx *c = ctx_of(R);
+    Ctx *c = ctx_raw(R);
     if (!c)
         return RTB_ENOTINIT;
     if ((!dev || !host) && bytes) {
+        launch_held(c);
         ctx_err(c, RTB_EINVAL, "rt_b200_push: null pointer");
         return RTB_EINVAL;
+    }
+    if (c->held) {
+        // the held round's y, whole, into host memory the GPU can write: the product stores it
+        // there itself and raises the host flag; anything else launches the round as usual
+        const Item it = c->held_item;
+        c->held = false;
+        float *yh = nullptr;
+        if (dev == it.y && bytes == size_t(it.t * it.rows) * sizeof(float) && aligned(host, 4) &&
+            (yh = mapped(host)) != nullptr)
+            return push_direct(c, it, yh);
+        std::vector<Item> one(1, it);
+        if (!run_items(c, one))
+            return c->status;
     }
     if (!flush_pending(c)) // y whole before it crosses
         return c->status;
@@ -1183,6 +1312,12 @@ void rt_b200_set_stream(struct rt *R, void *stream) {
         c->stream = stream ? static_cast<cudaStream_t>(stream) : c->own_stream;
         c->synced = false;
     }
+}
+
+void rt_b200_set_push_direct(struct rt *R, int on) {
+    Ctx *c = ctx_of(R);
+    if (c)
+        c->direct = on != 0;
 }
 
 int rt_b200_flush(struct rt *R) {

@@ -29,7 +29,8 @@ EXPORTS = ("rt_init", "rt_gemv", "rt_gemv_q", "rt_gemv_open", "rt_gemv_go", "rt_
            "rt_b200_free", "rt_b200_nccl_id", "rt_b200_shard", "rt_b200_peer_gather", "rt_b200_chain_begin",
            "rt_b200_chain_end", "rtb_gguf_info", "rt_b200_load_gguf", "rtb_load_error", "rtb_synth_q8_0",
            "rtb_synth_f32", "rt_gemm_static", "rt_b200_pull", "rt_b200_push", "rt_b200_wait_probe", "gemv_i_bytes",
-           "gemv_i_repack", "gemv_i_repack_thread", "rt_b200_shard_rows", "rt_b200_flush")
+           "gemv_i_repack", "gemv_i_repack_thread", "rt_b200_shard_rows", "rt_b200_flush",
+           "rt_b200_set_push_direct")
 
 
 class RtError(RuntimeError):
@@ -102,6 +103,7 @@ def load() -> C.CDLL:
         "rt_b200_shard": ([R, C.c_int, C.c_int, _P], C.c_int),
         "rt_b200_peer_gather": ([R], C.c_int),
         "rt_b200_flush": ([R], C.c_int),
+        "rt_b200_set_push_direct": ([R, C.c_int], None),
         "rt_b200_shard_rows": ([_L, C.c_int, C.c_int, C.POINTER(_L), C.POINTER(_L)], C.c_int),
         "rt_b200_wait_probe": ([R], C.c_int),
         "rt_b200_chain_begin": ([R], C.c_int),
@@ -268,6 +270,11 @@ class Runtime:
     def set_overlap(self, on: bool) -> None:
         """Weights are read-only between products: launch products so they overlap (PDL)."""
         self.lib.rt_b200_set_overlap(self._ref, 1 if on else 0)
+
+    def set_push_direct(self, on: bool) -> None:
+        """rt_b200_set_push_direct: go holds a one-product round back for push, which then takes y
+        straight from the product kernel into mapped pinned host memory."""
+        self.lib.rt_b200_set_push_direct(self._ref, 1 if on else 0)
 
     def sync(self) -> None:
         code = self.lib.rt_b200_sync(self._ref)

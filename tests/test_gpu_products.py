@@ -264,6 +264,104 @@ def test_opened_round_without_go_gives_up_and_recovers(cuda, rtb, oracle):
         assert bits_equal(y.cpu().numpy(), oracle.gemv(m.q8, rows, cols, x[0]))
 
 
+def test_direct_push(cuda, rtb, oracle):
+    """rt_b200_set_push_direct: a round of one product, held back by rt_gemv_go, then pushed into
+    mapped pinned host memory, writes y there from its own kernel and raises a host flag; push
+    returns with y whole on the host. Checked bit for bit on the host and in device memory over
+    back-to-back rounds (a gemv, a SwiGLU pair, a row gather, a 2-token product, the 151936-row
+    head), and the rounds that must take the usual path: a push of part of y, a push into
+    pageable memory, a held round followed by another call instead of a push, and a 16-token
+    tensor-core product (never held)."""
+    cols = 4096
+    a = Mat(cuda, rtb, oracle, 8192, cols, 211)
+    g = Mat(cuda, rtb, oracle, 512, cols, 212)
+    u = Mat(cuda, rtb, oracle, 512, cols, 213)
+    hd = Mat(cuda, rtb, oracle, 151936, cols, 214)
+    idx = np.array([8191, 0, 4000, 17, 17], dtype=np.int32)
+    idx_d = dev(cuda, idx)
+    xd = cuda.empty((16, cols), dtype=cuda.float32, device="cuda")
+    ya = cuda.full((8192,), float("nan"), dtype=cuda.float32, device="cuda")
+    y2 = cuda.full((2, 8192), float("nan"), dtype=cuda.float32, device="cuda")
+    h = cuda.full((512,), float("nan"), dtype=cuda.float32, device="cuda")
+    yr = cuda.full((5,), float("nan"), dtype=cuda.float32, device="cuda")
+    yh = cuda.full((151936,), float("nan"), dtype=cuda.float32, device="cuda")
+    y16 = cuda.full((16, 8192), float("nan"), dtype=cuda.float32, device="cuda")
+    host = cuda.full((2 * 151936,), float("nan"), dtype=cuda.float32).pin_memory()
+    pageable = np.full(8192, np.nan, dtype=np.float32)
+
+    def fresh():
+        host.fill_(float("nan"))
+
+    with rtb.Runtime() as rt:
+        rt.set_async(True)
+        rt.set_push_direct(True)
+        for k in range(3):
+            x = xs(oracle, 16, cols, 215 + k)
+            hx = cuda.from_numpy(x).pin_memory()
+            want = oracle.gemm(a.q8, 8192, cols, x, 2)
+            # a gemv, pushed whole into pinned memory: direct
+            fresh()
+            rt.gemv_q(a.ptr, 8192, cols, xd.data_ptr(), ya.data_ptr())
+            rt.pull(xd.data_ptr(), hx.data_ptr(), 4 * 16 * cols)
+            rt.gemv_go()
+            rt.push(host.data_ptr(), ya.data_ptr(), 4 * 8192)
+            assert bits_equal(host[:8192].numpy(), want[0]), k
+            assert bits_equal(ya.cpu().numpy(), want[0]), k
+            # 2 tokens
+            fresh()
+            rt.gemm_q(a.ptr, 8192, cols, xd.data_ptr(), 2, y2.data_ptr())
+            rt.gemv_go()
+            rt.push(host.data_ptr(), y2.data_ptr(), 4 * 2 * 8192)
+            assert bits_equal(host[:2 * 8192].numpy().reshape(2, 8192), want), k
+            # a SwiGLU pair
+            fresh()
+            rt.gemm_silu_q(g.ptr, u.ptr, 512, cols, xd.data_ptr(), 1, h.data_ptr())
+            rt.gemv_go()
+            rt.push(host.data_ptr(), h.data_ptr(), 4 * 512)
+            yg = oracle.gemv(g.q8, 512, cols, x[0]).astype(np.float64)
+            yu = oracle.gemv(u.q8, 512, cols, x[0]).astype(np.float64)
+            hs = host[:512].numpy()
+            assert np.allclose(hs, (yg / (1.0 + np.exp(-yg)) * yu).astype(np.float32), rtol=1e-6, atol=1e-30), k
+            assert bits_equal(h.cpu().numpy(), hs), k
+            # a row gather
+            fresh()
+            rt.gemv_rows_q(a.ptr, 8192, idx_d.data_ptr(), 5, cols, xd.data_ptr(), yr.data_ptr())
+            rt.gemv_go()
+            rt.push(host.data_ptr(), yr.data_ptr(), 4 * 5)
+            assert bits_equal(host[:5].numpy(), want[0][idx]), k
+            # the head: 607 KB of y from 296 CTAs
+            fresh()
+            rt.gemv_q(hd.ptr, 151936, cols, xd.data_ptr(), yh.data_ptr())
+            rt.gemv_go()
+            rt.push(host.data_ptr(), yh.data_ptr(), 4 * 151936)
+            assert bits_equal(host[:151936].numpy(), oracle.gemv(hd.q8, 151936, cols, x[0])), k
+        # the usual path: part of y; pageable memory; another call first; tensor cores
+        x = xs(oracle, 16, cols, 219)
+        xd.copy_(cuda.from_numpy(x))
+        want = oracle.gemm(a.q8, 8192, cols, x, 16)
+        fresh()
+        ya.fill_(float("nan"))
+        rt.gemv_q(a.ptr, 8192, cols, xd.data_ptr(), ya.data_ptr())
+        rt.gemv_go()
+        rt.push(host.data_ptr(), ya.data_ptr(), 4 * 4096)
+        assert bits_equal(host[:4096].numpy(), want[0][:4096])
+        assert np.isnan(host[4096:8192].numpy()).all()
+        assert bits_equal(ya.cpu().numpy(), want[0])
+        rt.gemv_q(a.ptr, 8192, cols, xd.data_ptr(), ya.data_ptr())
+        rt.gemv_go()
+        rt.push(pageable.ctypes.data, ya.data_ptr(), 4 * 8192)
+        assert bits_equal(pageable, want[0])
+        ya.fill_(float("nan"))
+        rt.gemv_q(a.ptr, 8192, cols, xd.data_ptr(), ya.data_ptr())
+        rt.gemv_go()
+        rt.sync()  # launches the held round, as any call on R does
+        assert bits_equal(ya.cpu().numpy(), want[0])
+        rt.gemm_q(a.ptr, 8192, cols, xd.data_ptr(), 16, y16.data_ptr())
+        rt.gemv_go()
+        rt.push(host.data_ptr(), y16.data_ptr(), 4 * 16 * 8192)
+        assert rel_err(host[:16 * 8192].numpy().reshape(16, 8192), want) < TC_TOL
+
+
 def test_gemv_output_head_full_size(cuda, runtime, rtb, oracle):
     """BASELINE config 2's output head, 151936 x 4096, every output bit for bit."""
     rows, cols = 151936, 4096
