@@ -321,6 +321,9 @@ class Bench:
                 clocks = ClockSampler([0])
                 res["prompt"] = self.prompt()
                 res["prompt"]["clocks"] = clocks.stop()
+            clocks = ClockSampler([0])
+            res["prims"] = self.prims()
+            res["prims"]["clocks"] = clocks.stop()
         return res
 
     def head_launch(self, steps: int) -> dict:
@@ -514,6 +517,86 @@ class Bench:
             out[f"m{m}"] = row
             del xd, xf, ys
         rt.sync()
+        return out
+
+    def prims(self) -> dict:
+        """The host-half primitives beside the products (rt_ip21_kv, rt_ip12_kv, rt_ip21,
+        rt_scale_outer; src/host/rt_host.c:128-279) at a 9B-class decode step's sizes: attention
+        over a 4096-token history (16 query heads on 4 kv heads, 256 columns: 16 MB of keys or
+        values per call) and the delta rule's state (32 heads of 128 x 128: 2 MB per call). Each
+        call reads its own buffer from a rotation larger than L2, 24 calls per CUDA graph; GB/s
+        of algorithmic bytes (inputs read once, outputs written once). Beside each, the
+        reference's own host code (oracle/_ref, src/host/rt_host.c, one thread) on one call."""
+        import numpy as np
+        torch, rt = self.torch, self.rt
+        rt.set_async(True)
+        rt.set_stream(torch.cuda.current_stream().cuda_stream)
+        hpeak, hkind = peaks()
+        h, n1, c, t = 16, 4, 256, 4096
+        hs, r, cs = 32, 128, 128
+        l = [q * n1 // h for q in range(h)]
+        kv_bytes = t * n1 * c * 4
+        nkv = 12  # 12 x 16 MB > L2
+        gen = torch.Generator(device="cuda").manual_seed(7)
+        kvs = [torch.randn(t * n1 * c, device="cuda", generator=gen) for _ in range(nkv)]
+        states = [torch.randn(hs * r * cs, device="cuda", generator=gen) for _ in range(96)]  # 96 x 2 MB
+        q = torch.randn(h * c, device="cuda", generator=gen)
+        p = torch.randn(h * t, device="cuda", generator=gen)
+        bs = torch.randn(hs * cs, device="cuda", generator=gen)
+        av = torch.randn(hs * r, device="cuda", generator=gen)
+        bv = torch.randn(hs * cs, device="cuda", generator=gen)
+        zs = torch.empty(h * t, device="cuda")
+        zo = torch.empty(h * c, device="cuda")
+        zd = torch.empty(hs * r, device="cuda")
+        zu = [torch.empty(hs * r * cs, device="cuda") for _ in range(2)]
+        n = 24
+        calls = {
+            "ip21_kv": (lambda i: rt.ip21_kv(zs.data_ptr(), kvs[i % nkv].data_ptr(), n1, c, l, h, t, q.data_ptr()),
+                        kv_bytes + h * c * 4 + h * t * 4),
+            "ip12_kv": (lambda i: rt.ip12_kv(zo.data_ptr(), p.data_ptr(), kvs[i % nkv].data_ptr(), n1, c, l, h, t),
+                        kv_bytes + h * t * 4 + h * c * 4),
+            "ip21": (lambda i: rt.ip21(zd.data_ptr(), states[i % 96].data_ptr(), hs, r, cs, bs.data_ptr()),
+                     hs * r * cs * 4 + hs * cs * 4 + hs * r * 4),
+            "scale_outer": (lambda i: rt.scale_outer(zu[i % 2].data_ptr(), states[i % 96].data_ptr(), 0.97, av.data_ptr(),
+                                                     bv.data_ptr(), hs * r, cs),
+                            2 * hs * r * cs * 4 + hs * r * 4 + cs * 4),
+        }
+        out = {"shapes": {"attention": {"h": h, "n1": n1, "c": c, "t": t}, "delta_rule": {"h": hs, "r": r, "c": cs}},
+               "peak_gbs": hpeak, "peak_kind": hkind}
+        for name, (f, nbytes) in calls.items():
+            fns = [(lambda i=i, f=f: f(i)) for i in range(n)]
+            for g in fns:
+                g()
+            torch.cuda.synchronize()
+            gr = self._graph(fns)
+            us = self._time_graph(gr, 3) * 1e3 / n
+            del gr
+            out[name] = {"us": round(us, 2), "GB_s": round(nbytes / us / 1e3, 1), "hbm_frac": round(nbytes / us / 1e3 / hpeak, 3),
+                         "bytes": nbytes}
+        rt.sync()
+        try:  # the reference's own host code, one call each (the CPU leg: the checker library)
+            sys.path.insert(0, os.path.join(ROOT, "oracle"))
+            import oracle as O
+            if O.hostref_available():
+                A = O._f32  # 64-byte aligned copies: the reference's AVX2 loads need 32
+                kvh, qh, ph = A(kvs[0].cpu().numpy()), A(q.cpu().numpy()), A(p.cpu().numpy())
+                sh, bsh, avh, bvh = A(states[0].cpu().numpy()), A(bs.cpu().numpy()), A(av.cpu().numpy()), A(bv.cpu().numpy())
+                la = np.array(l, dtype=np.int64)
+                zsh, zoh, zdh, zuh = O._aligned(h * t), O._aligned(h * c), O._aligned(hs * r), O._aligned(hs * r * cs)
+                lib, rref = O.hostref()
+                R = O.C.byref(rref)
+                refs = {"ip21_kv": lambda: lib.rt_ip21_kv(R, zsh, kvh, n1, c, la, h, t, qh),
+                        "ip12_kv": lambda: lib.rt_ip12_kv(R, zoh, ph, kvh, n1, c, la, h, t),
+                        "ip21": lambda: lib.rt_ip21(R, zdh, sh, hs, r, cs, bsh),
+                        "scale_outer": lambda: lib.rt_scale_outer(R, zuh, sh, 0.97, avh, bvh, hs * r, cs)}
+                for name, f in refs.items():
+                    f()
+                    t0 = time.perf_counter()
+                    f()
+                    out[name]["cpu_reference_us"] = round((time.perf_counter() - t0) * 1e6, 1)
+        except OSError:
+            pass
+        del kvs, states
         return out
 
     def sweep(self) -> dict:
@@ -792,6 +875,8 @@ def main() -> int:
             line["sweep"] = res["sweep"]
         if "prompt" in res:
             line["prompt"] = res["prompt"]
+        if "prims" in res:
+            line["prims"] = res["prims"]
         print(json.dumps(line), flush=True)
     b.rt.close()
     if world > 1:

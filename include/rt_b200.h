@@ -88,6 +88,28 @@ RTB_API void rt_gemm_q(struct rt *R, const void *w, long rows, long cols, const 
 /* src/card/rt.h:85 (rt.c:484-501). z[cols] = row `row` of W dequantised: z[i] = (float)q * d. */
 RTB_API void rt_q8_row(const void *w, long cols, long row, float *z);
 
+/* ---- The host-half primitives beside the products: the inner products over an attention head's
+ * history and the delta rule's state products, which the reference runs on its host worker
+ * (src/host/rt_host.c:128-279, prototypes src/card/rt.h:73-82). Here they run on the GPU, on R's
+ * stream (blocking unless async, as the products), with device pointers and the reference's
+ * rounding order bit for bit: a dot product is 8 lanes of fma chains over columns j, j+8, ...
+ * summed ((l0+l4)+(l2+l6))+((l1+l5)+(l3+l7)) (src/host/vec8.h:49-55). c is a multiple of 8;
+ * l (host memory, h <= 128 entries) gives each query head's kv head, in [0, n1); kv is
+ * [t][n1][c] and 16-byte aligned. Not inside a chain. */
+/* z[h*t + s] = dot(kv[s][l[h]][:], b[h][:]) (src/host/rt_host.c:135-162) */
+RTB_API void rt_ip21_kv(struct rt *R, float *z, const float *kv, long n1, long c, const long *l, long h, long t,
+                        const float *b);
+/* z[h][k] = fma(a[h][s], kv[s][l[h]][k], z[h][k]) over s = 0..t-1 in order, from 0
+ * (src/host/rt_host.c:164-189) */
+RTB_API void rt_ip12_kv(struct rt *R, float *z, const float *a, const float *kv, long n1, long c, const long *l, long h,
+                        long t);
+/* z[h][i] = dot(a[h][i][:], b[h][:]), a as [h][r][c] (src/host/rt_host.c:200-247) */
+RTB_API void rt_ip21(struct rt *R, float *z, const float *a, long h, long r, long c, const float *b);
+/* z[i][q] = fma(g, s[i][q], a[i] * b[q]), the product rounded first, m x k (src/host/rt_host.c:261-279;
+ * any k here, a multiple of 8 there) */
+RTB_API void rt_scale_outer(struct rt *R, float *z, const float *s, float g, const float *a, const float *b, long m,
+                            long k);
+
 /* ---------------------------------------------------------------- load side */
 
 /* Bytes of a rows x cols matrix in the row-split layout: each row holds its cols int8 quants

@@ -78,8 +78,10 @@ constexpr int A_COLS = BK / 2;
 //     and SiLU make it longer); accumulators in columns [0, 256) (two of 128 columns, double-
 //     buffered, for tiles of <= 128 tokens, else one of 256), up to 8 A slots from 256.
 //   CPS = 2 (tiles of up to 64 tokens): 10 warps, 4 dequant (each thread both blocks of its row),
-//     4 epilogue; accumulators at columns 0 and 64, the A slots from the next 32-column boundary
-//     (5 of them for tiles of <= 32 tokens, else 4). Two CTAs share an SM and
+//     4 epilogue; accumulators at columns 0 and 32 (tiles of <= 32 tokens) or 0 and 64, the A
+//     slots from the next 32-column boundary (6 of them for tiles of <= 32 tokens, else 4: the
+//     ring's depth is what bounds these small tiles, whose stages wait on DRAM latency). Two CTAs
+//     share an SM and
 //     its tensor core: at N <= 64 an MMA instruction takes ~46 cycles while each wait in the
 //     issuing thread stalls it ~200, so a second issuer keeps the pipe fed.
 constexpr int MAX_BN_TWO_CTAS = 64; // the two-CTA shape's tiles: two accumulators of up to 64 columns
@@ -117,7 +119,8 @@ struct TcParams {
     CUtensorMap tx[8];   // fp16 x per job
     TcJobDev job[8];
     int njobs, total_units, bn, stages;
-    int a_base; // TMEM column of the first A slot (after the accumulators)
+    int a_base;     // TMEM column of the first A slot (after the accumulators)
+    int acc_stride; // TMEM columns from the first accumulator to the second
     unsigned *err;
 };
 
@@ -246,7 +249,7 @@ __global__ void __launch_bounds__(TcShape<CPS>::NT, CPS) gemm_tc_kernel(const __
     const int A_BASE = p.a_base;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int S = p.stages, BN = p.bn, SB = stage_bytes(BN), NACC = n_acc(BN, CPS), ACC_STRIDE = Sh::ACC_COLS / NACC;
+    const int S = p.stages, BN = p.bn, SB = stage_bytes(BN), NACC = n_acc(BN, CPS), ACC_STRIDE = p.acc_stride;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + size_t(S) * SB); // [S]: TMA landed
     uint64_t *empty = full + MAX_STAGES;                                   // [S]: the stage's MMAs done
     uint64_t *afull = empty + MAX_STAGES;                                  // [S]: the stage's A slot in TMEM
@@ -865,9 +868,10 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
     p.err = err;
     const int sb = stage_bytes(bn), cps = cps_of(bn);
     const size_t smem_limit = cps == 1 ? SMEM_LIMIT : SMEM_LIMIT_2;
-    // the A slots follow the accumulators (at columns 0 and ACC_COLS / 2 when double-buffered),
-    // on a 32-column boundary: two CTAs per SM with tiles of <= 32 tokens fit a fifth stage
-    const int acc_stride = (cps == 1 ? TcShape<1>::ACC_COLS : TcShape<2>::ACC_COLS) / n_acc(bn, cps);
+    // the A slots follow the accumulators (at columns 0 and ACC_COLS / 2 when double-buffered; two
+    // CTAs per SM with tiles of <= 32 tokens: at 0 and 32), on a 32-column boundary
+    const int acc_stride = cps == 2 && bn <= 32 ? 32 : (cps == 1 ? TcShape<1>::ACC_COLS : TcShape<2>::ACC_COLS) / n_acc(bn, cps);
+    p.acc_stride = acc_stride;
     const int acc_end = (n_acc(bn, cps) - 1) * acc_stride + bn;
     p.a_base = cps == 1 ? TcShape<1>::ACC_COLS : (acc_end + A_COLS - 1) / A_COLS * A_COLS;
     const int tmem_cols = cps == 1 ? TcShape<1>::TMEM_COLS : TcShape<2>::TMEM_COLS;

@@ -117,6 +117,30 @@ cudaError_t launch_gemv_chain(ChainParams &p, int num_sms, cudaStream_t stream);
 // The bounded waits' self-test (rt_b200_wait_probe): *ctr must be 0 and stay 0.
 cudaError_t launch_wait_probe(const unsigned *ctr, unsigned *err, cudaStream_t stream);
 
+// ---- the host-half primitives beside the products (host_prims.cu)
+constexpr int MAX_PRIM_HEADS = 128; // query heads of one call
+constexpr int MAX_PRIM_GROUP = 16;  // query heads of one kv head in one ip12_kv CTA (a warp each)
+struct PrimHeads {
+    long long l[MAX_PRIM_HEADS]; // the kv head of each query head
+};
+// The query heads grouped by kv head, each group <= MAX_PRIM_GROUP heads: group g is heads
+// head[first[g] .. first[g+1]) of kv head kv[g].
+struct PrimGroups {
+    int n;
+    int first[MAX_PRIM_HEADS + 1];
+    int head[MAX_PRIM_HEADS];
+    long long kv[MAX_PRIM_HEADS];
+};
+cudaError_t launch_ip21(float *z, const float *a, long long h, long long r, long long c, const float *b,
+                        cudaStream_t stream);
+cudaError_t launch_ip21_kv(float *z, const float *kv, long long n1, long long c, const PrimHeads &heads, long long h,
+                           long long t, const float *b, cudaStream_t stream);
+cudaError_t launch_ip12_kv(float *z, const float *a, const float *kv, long long n1, long long c, const PrimGroups &groups,
+                           long long t, cudaStream_t stream);
+cudaError_t launch_scale_outer(float *z, const float *s, float g, const float *a, const float *b, long long m,
+                               long long k, cudaStream_t stream);
+cudaError_t preload_prims();
+
 // After a peer-gathered launch: wait for every peer's flag of this round, then copy their rows
 // of y ([t][ldy], ldy = rows_total) from the staging image.
 // pdl: launch with programmatic stream serialization (overlaps the product's tail).

@@ -935,6 +935,7 @@ int rt_init(struct rt *R, int threads) {
     // mapped host words: the error mirror at 0, the direct pushes' flag 128 bytes on
     unsigned *h_err = nullptr, *h_err_dev = nullptr;
     if (q8::preload_gemv() != cudaSuccess || q8::preload_gemm_tc() != cudaSuccess || q8::preload_peer() != cudaSuccess ||
+        q8::preload_prims() != cudaSuccess ||
         cudaHostAlloc(&h_err, 256, cudaHostAllocMapped) != cudaSuccess ||
         cudaHostGetDevicePointer(&h_err_dev, h_err, 0) != cudaSuccess) {
         if (h_err)
@@ -1135,6 +1136,139 @@ void rt_gemv_rows(struct rt *R, const void *w, long w_rows, const int32_t *idx, 
         it.src_rows = w_rows;
         run_now(c, it);
     }
+}
+
+// ---------------------------------------------------------------- host-half primitives
+// (src/host/rt_host.c:128-279; the kernels in host_prims.cu). On R's stream, device pointers;
+// blocking unless async, as the products.
+
+// The common checks; false (and R's error set) if the call cannot run.
+static bool prim_ok(Ctx *c, const char *fn, bool ptrs, long h, long c_cols) {
+    if (c->chaining) {
+        ctx_err(c, RTB_EINVAL, "%s: not inside a chain (rt_b200_chain_begin .. end)", fn);
+        return false;
+    }
+    if (!ptrs) {
+        ctx_err(c, RTB_EINVAL, "%s: null or misaligned pointer (4 bytes; kv 16)", fn);
+        return false;
+    }
+    if (h < 1 || h > q8::MAX_PRIM_HEADS) {
+        ctx_err(c, RTB_EINVAL, "%s: h = %ld outside [1, %d]", fn, h, q8::MAX_PRIM_HEADS);
+        return false;
+    }
+    if (c_cols < 8 || c_cols % 8) {
+        ctx_err(c, RTB_EINVAL, "%s: c = %ld is not a positive multiple of 8", fn, c_cols);
+        return false;
+    }
+    return flush_pending(c);
+}
+
+static bool heads_ok(Ctx *c, const char *fn, const long *l, long h, long n1) {
+    if (!l || n1 < 1) {
+        ctx_err(c, RTB_EINVAL, "%s: null l or n1 < 1", fn);
+        return false;
+    }
+    for (long i = 0; i < h; ++i)
+        if (l[i] < 0 || l[i] >= n1) {
+            ctx_err(c, RTB_EINVAL, "%s: l[%ld] = %ld outside [0, n1 = %ld)", fn, i, l[i], n1);
+            return false;
+        }
+    return true;
+}
+
+void rt_ip21(struct rt *R, float *z, const float *a, long h, long r, long c_cols, const float *b) {
+    Ctx *c = ctx_of(R);
+    if (!c || !prim_ok(c, "rt_ip21", z && b && (r == 0 || a) && aligned(z, 4) && aligned(a, 4) && aligned(b, 4), h, c_cols))
+        return;
+    if (r < 0) {
+        ctx_err(c, RTB_EINVAL, "rt_ip21: r < 0");
+        return;
+    }
+    c->synced = false;
+    if (cuda_ok(c, q8::launch_ip21(z, a, h, r, c_cols, b, c->stream), "rt_ip21"))
+        finish(c);
+}
+
+void rt_ip21_kv(struct rt *R, float *z, const float *kv, long n1, long c_cols, const long *l, long h, long t,
+                const float *b) {
+    Ctx *c = ctx_of(R);
+    // (an empty history reads no kv: a null kv is then fine)
+    const bool kv_ok = t == 0 || (kv && aligned(kv, 16));
+    if (!c || !prim_ok(c, "rt_ip21_kv", z && b && kv_ok && aligned(z, 4) && aligned(b, 4), h, c_cols) ||
+        !heads_ok(c, "rt_ip21_kv", l, h, n1))
+        return;
+    if (t < 0) {
+        ctx_err(c, RTB_EINVAL, "rt_ip21_kv: t < 0");
+        return;
+    }
+    q8::PrimHeads heads;
+    memset(&heads, 0, sizeof heads);
+    for (long i = 0; i < h; ++i)
+        heads.l[i] = l[i];
+    c->synced = false;
+    if (cuda_ok(c, q8::launch_ip21_kv(z, kv, n1, c_cols, heads, h, t, b, c->stream), "rt_ip21_kv"))
+        finish(c);
+}
+
+void rt_ip12_kv(struct rt *R, float *z, const float *a, const float *kv, long n1, long c_cols, const long *l, long h,
+                long t) {
+    Ctx *c = ctx_of(R);
+    const bool in_ok = t == 0 || (a && kv && aligned(a, 4) && aligned(kv, 16)); // (t = 0: z = 0, nothing read)
+    if (!c || !prim_ok(c, "rt_ip12_kv", z && in_ok && aligned(z, 4), h, c_cols) ||
+        !heads_ok(c, "rt_ip12_kv", l, h, n1))
+        return;
+    if (t < 0) {
+        ctx_err(c, RTB_EINVAL, "rt_ip12_kv: t < 0");
+        return;
+    }
+    // the query heads grouped by kv head (the groups share each streamed history slice), split
+    // into groups of at most MAX_PRIM_GROUP
+    q8::PrimGroups g;
+    memset(&g, 0, sizeof g);
+    std::vector<char> done(size_t(h), 0);
+    int nh = 0;
+    for (long i = 0; i < h; ++i) {
+        if (done[size_t(i)])
+            continue;
+        g.first[g.n] = nh;
+        g.kv[g.n] = l[i];
+        for (long j = i; j < h; ++j)
+            if (!done[size_t(j)] && l[j] == l[i]) {
+                if (nh - g.first[g.n] == q8::MAX_PRIM_GROUP) { // a full group: the next one, same kv head
+                    ++g.n;
+                    g.first[g.n] = nh;
+                    g.kv[g.n] = l[i];
+                }
+                g.head[nh++] = int(j);
+                done[size_t(j)] = 1;
+            }
+        ++g.n;
+    }
+    g.first[g.n] = nh;
+    c->synced = false;
+    if (cuda_ok(c, q8::launch_ip12_kv(z, a, kv, n1, c_cols, g, t, c->stream), "rt_ip12_kv"))
+        finish(c);
+}
+
+void rt_scale_outer(struct rt *R, float *z, const float *s, float g, const float *a, const float *b, long m, long k) {
+    Ctx *c = ctx_of(R);
+    if (!c)
+        return;
+    if (c->chaining) {
+        ctx_err(c, RTB_EINVAL, "rt_scale_outer: not inside a chain (rt_b200_chain_begin .. end)");
+        return;
+    }
+    if (!z || !s || !a || !b || !aligned(z, 4) || !aligned(s, 4) || !aligned(a, 4) || !aligned(b, 4) || m < 0 || k < 0) {
+        ctx_err(c, RTB_EINVAL, "rt_scale_outer: null or misaligned pointer, or m, k < 0");
+        return;
+    }
+    if (!flush_pending(c))
+        return;
+    if (m == 0 || k == 0)
+        return;
+    c->synced = false;
+    if (cuda_ok(c, q8::launch_scale_outer(z, s, g, a, b, m, k, c->stream), "rt_scale_outer"))
+        finish(c);
 }
 
 void rt_q8_row(const void *w, long cols, long row, float *z) {

@@ -30,7 +30,7 @@ EXPORTS = ("rt_init", "rt_gemv", "rt_gemv_q", "rt_gemv_open", "rt_gemv_go", "rt_
            "rt_b200_chain_end", "rtb_gguf_info", "rt_b200_load_gguf", "rtb_load_error", "rtb_synth_q8_0",
            "rtb_synth_f32", "rt_gemm_static", "rt_b200_pull", "rt_b200_push", "rt_b200_wait_probe", "gemv_i_bytes",
            "gemv_i_repack", "gemv_i_repack_thread", "rt_b200_shard_rows", "rt_b200_flush",
-           "rt_b200_set_push_direct")
+           "rt_b200_set_push_direct", "rt_ip21", "rt_ip21_kv", "rt_ip12_kv", "rt_scale_outer")
 
 
 class RtError(RuntimeError):
@@ -81,6 +81,10 @@ def load() -> C.CDLL:
         "rt_gemm": ([R, _P, _L, _L, _P, _L, _P], None),
         "rt_gemm_q": ([R, _P, _L, _L, _P, _L, _P], None),
         "rt_q8_row": ([_P, _L, _L, _P], None),
+        "rt_ip21": ([R, _P, _P, _L, _L, _L, _P], None),
+        "rt_ip21_kv": ([R, _P, _P, _L, _L, _P, _L, _L, _P], None),
+        "rt_ip12_kv": ([R, _P, _P, _P, _L, _L, _P, _L, _L], None),
+        "rt_scale_outer": ([R, _P, _P, C.c_float, _P, _P, _L, _L], None),
         "gemv_s_bytes": ([_L, _L], _L),
         "gemv_s_repack": ([_P, _L, _L, _P], C.c_int),
         "gemv_i_bytes": ([_L, _L], _L),
@@ -270,6 +274,29 @@ class Runtime:
     def set_overlap(self, on: bool) -> None:
         """Weights are read-only between products: launch products so they overlap (PDL)."""
         self.lib.rt_b200_set_overlap(self._ref, 1 if on else 0)
+
+    # ---- the host-half primitives (device pointers; l: the kv head of each query head, host ints)
+    def ip21(self, z: int, a: int, h: int, r: int, c: int, b: int) -> None:
+        """rt_ip21: z[h][i] = a[h][i][:] . b[h][:] (the delta rule's state product)."""
+        self.lib.rt_ip21(self._ref, z, a, h, r, c, b)
+        _check(self)
+
+    def ip21_kv(self, z: int, kv: int, n1: int, c: int, l, h: int, t: int, b: int) -> None:
+        """rt_ip21_kv: z[h][s] = kv[s][l[h]][:] . b[h][:] (scores over a head's history)."""
+        la = (C.c_long * h)(*[int(v) for v in l])
+        self.lib.rt_ip21_kv(self._ref, z, kv, n1, c, la, h, t, b)
+        _check(self)
+
+    def ip12_kv(self, z: int, a: int, kv: int, n1: int, c: int, l, h: int, t: int) -> None:
+        """rt_ip12_kv: z[h][:] = sum over s in order of a[h][s] * kv[s][l[h]][:]."""
+        la = (C.c_long * h)(*[int(v) for v in l])
+        self.lib.rt_ip12_kv(self._ref, z, a, kv, n1, c, la, h, t)
+        _check(self)
+
+    def scale_outer(self, z: int, s: int, g: float, a: int, b: int, m: int, k: int) -> None:
+        """rt_scale_outer: z[i][q] = g * s[i][q] + a[i] * b[q] (one fma, the product rounded first)."""
+        self.lib.rt_scale_outer(self._ref, z, s, g, a, b, m, k)
+        _check(self)
 
     def set_push_direct(self, on: bool) -> None:
         """rt_b200_set_push_direct: go holds a one-product round back for push, which then takes y

@@ -1,11 +1,12 @@
 """TEST INFRASTRUCTURE ONLY: ctypes access to the CPU oracles.
 
-Two libraries, both built by ``oracle/Makefile``:
+Three libraries, all built by ``oracle/Makefile``:
 
 * ``libq8oracle.so`` -- this repository's C restatement of the reference's Q8_0 products
   (``oracle/q8_oracle.c``; the header says which reference lines each function follows);
 * ``_ref/libq8ref.so`` -- the reference's own host-model kernels (src/card/gemv.c, gemm.c,
-  team.c) compiled from its sources, behind ``oracle/ref_harness.c``.
+  team.c) compiled from its sources, behind ``oracle/ref_harness.c``;
+* ``_ref/libhostref.so`` -- the reference's own host-half primitives (src/host/rt_host.c).
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg import this
 module; the product path never does.
@@ -28,6 +29,7 @@ _u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
 _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _f64p = np.ctypeslib.ndpointer(dtype=np.float64, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+_lp = np.ctypeslib.ndpointer(dtype=np.int64, flags="C_CONTIGUOUS")
 _L = C.c_long
 
 _port = None
@@ -60,12 +62,46 @@ def port() -> C.CDLL:
         lib.q8o_gemm_f64.argtypes = [_u8p, _L, _L, _f32p, _L, _f64p, C.c_int]
         lib.q8o_gate21_hashes.argtypes = [np.ctypeslib.ndpointer(dtype=np.uint64, flags="C_CONTIGUOUS")]
         lib.q8o_gate_a.argtypes = [C.POINTER(C.c_uint64), np.ctypeslib.ndpointer(dtype=np.uint32, flags="C_CONTIGUOUS")]
+        lib.q8o_ip21_kv.argtypes = [_f32p, _f32p, _L, _L, _lp, _L, _L, _f32p]
+        lib.q8o_ip12_kv.argtypes = [_f32p, _f32p, _f32p, _L, _L, _lp, _L, _L]
+        lib.q8o_ip21.argtypes = [_f32p, _f32p, _L, _L, _L, _f32p]
+        lib.q8o_scale_outer.argtypes = [_f32p, _f32p, C.c_float, _f32p, _f32p, _L, _L]
         _port = lib
     return _port
 
 
 def ref_available() -> bool:
     return os.path.exists(REF_PATH)
+
+
+HOSTREF_PATH = os.path.join(HERE, "_ref", "libhostref.so")
+_hostref = None
+
+
+class _StructRt(C.Structure):
+    # the reference's struct rt (src/card/rt.h:19-26); team = NULL: the one-thread path
+    _fields_ = [("team", C.c_void_p), ("frame", C.c_char_p), ("chain", C.c_void_p), ("gemm_chain", C.c_void_p),
+                ("threads", C.c_int), ("last", C.c_int)]
+
+
+def hostref_available() -> bool:
+    return os.path.exists(HOSTREF_PATH)
+
+
+def hostref() -> tuple[C.CDLL, C.c_void_p]:
+    """The reference's own host-half primitives (src/host/rt_host.c), and a struct rt without a
+    team for them (its one-thread path: the same arithmetic per output)."""
+    global _hostref
+    if _hostref is None:
+        lib = C.CDLL(HOSTREF_PATH)
+        R = C.POINTER(_StructRt)
+        lib.rt_ip21_kv.argtypes = [R, _f32p, _f32p, _L, _L, _lp, _L, _L, _f32p]
+        lib.rt_ip12_kv.argtypes = [R, _f32p, _f32p, _f32p, _L, _L, _lp, _L, _L]
+        lib.rt_ip21.argtypes = [R, _f32p, _f32p, _L, _L, _L, _f32p]
+        lib.rt_scale_outer.argtypes = [R, _f32p, _f32p, C.c_float, _f32p, _f32p, _L, _L]
+        rt = _StructRt()
+        _hostref = (lib, rt)
+    return _hostref
 
 
 def ref() -> C.CDLL:
@@ -201,3 +237,64 @@ class RefMatrix:
         ref().refh_gemm(self.form_i, self.rows, self.cols, np.ascontiguousarray(x, dtype=np.float32).reshape(-1), t,
                         y.reshape(-1))
         return y
+
+
+# ---------------------------------------------------------------- host-half primitives
+# (prims_oracle.c restates src/host/rt_host.c:128-279; the same calls on the reference itself
+# through hostref())
+
+def _f32(a):
+    """A float32 copy on a 64-byte boundary: the reference's AVX2 code uses aligned loads and
+    stores (_mm256_load_ps / _mm256_store_ps), which fault on less."""
+    a = np.asarray(a, dtype=np.float32).ravel()
+    out = _aligned(a.size)
+    out[:] = a
+    return out
+
+
+def _aligned(n: int) -> np.ndarray:
+    buf = np.empty(n + 16, dtype=np.float32)
+    off = (-buf.ctypes.data % 64) // 4
+    return buf[off:off + n]
+
+
+def ip21_kv(kv: np.ndarray, n1: int, c: int, l: np.ndarray, h: int, t: int, b: np.ndarray, use_ref: bool = False) -> np.ndarray:
+    z = _aligned(h * t)
+    l64 = np.ascontiguousarray(l, dtype=np.int64)
+    if use_ref:
+        lib, rt = hostref()
+        lib.rt_ip21_kv(C.byref(rt), z, _f32(kv), n1, c, l64, h, t, _f32(b))
+    else:
+        port().q8o_ip21_kv(z, _f32(kv), n1, c, l64, h, t, _f32(b))
+    return z
+
+
+def ip12_kv(a: np.ndarray, kv: np.ndarray, n1: int, c: int, l: np.ndarray, h: int, t: int, use_ref: bool = False) -> np.ndarray:
+    z = _aligned(h * c)
+    l64 = np.ascontiguousarray(l, dtype=np.int64)
+    if use_ref:
+        lib, rt = hostref()
+        lib.rt_ip12_kv(C.byref(rt), z, _f32(a), _f32(kv), n1, c, l64, h, t)
+    else:
+        port().q8o_ip12_kv(z, _f32(a), _f32(kv), n1, c, l64, h, t)
+    return z
+
+
+def ip21(a: np.ndarray, h: int, r: int, c: int, b: np.ndarray, use_ref: bool = False) -> np.ndarray:
+    z = _aligned(h * r)
+    if use_ref:
+        lib, rt = hostref()
+        lib.rt_ip21(C.byref(rt), z, _f32(a), h, r, c, _f32(b))
+    else:
+        port().q8o_ip21(z, _f32(a), h, r, c, _f32(b))
+    return z
+
+
+def scale_outer(s: np.ndarray, g: float, a: np.ndarray, b: np.ndarray, m: int, k: int, use_ref: bool = False) -> np.ndarray:
+    z = _aligned(m * k)
+    if use_ref:
+        lib, rt = hostref()
+        lib.rt_scale_outer(C.byref(rt), z, _f32(s), g, _f32(a), _f32(b), m, k)
+    else:
+        port().q8o_scale_outer(z, _f32(s), g, _f32(a), _f32(b), m, k)
+    return z

@@ -62,6 +62,13 @@ void q8o_gemm_f64(const uint8_t *q8, long rows, long cols, const float *x, long 
 void q8o_gate21_hashes(uint64_t out[7]);
 void q8o_gate_a(uint64_t *hash, uint32_t words[3]);
 
+/* ---- the host-half primitives beside the products (prims_oracle.c; src/host/rt_host.c:128-279),
+ * in the reference's rounding order. l: h entries, the kv head of each query head. c % 8 == 0. */
+void q8o_ip21_kv(float *z, const float *kv, long n1, long c, const long *l, long h, long t, const float *b);
+void q8o_ip12_kv(float *z, const float *a, const float *kv, long n1, long c, const long *l, long h, long t);
+void q8o_ip21(float *z, const float *a, long h, long r, long c, const float *b);
+void q8o_scale_outer(float *z, const float *s, float g, const float *a, const float *b, long m, long k);
+
 #ifdef __cplusplus
 }
 #endif

@@ -28,7 +28,8 @@ def pytest_configure(config):
 
 def _ensure_oracle_built() -> None:
     lib = os.path.join(ORACLE, "libq8oracle.so")
-    if not os.path.exists(lib):
+    srcs = [os.path.join(ORACLE, f) for f in ("q8_oracle.c", "prims_oracle.c", "q8_oracle.h")]
+    if not os.path.exists(lib) or any(os.path.exists(f) and os.path.getmtime(f) > os.path.getmtime(lib) for f in srcs):
         subprocess.run(["make", "-C", ORACLE, "port"], check=True, capture_output=True)
 
 

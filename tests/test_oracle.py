@@ -146,3 +146,53 @@ def test_port_against_live_reference(oracle):
         want = ref.gemm(x, t) if t > 1 else ref.gemv(x[0])[None]
         got = oracle.gemm(q8, rows, cols, x, t)
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+PRIM_SHAPES = [  # h, n1, c, t (history), r (state rows), m, k
+    (8, 2, 64, 37, 19, 24, 40),
+    (16, 4, 256, 300, 128, 128, 128),
+    (3, 3, 8, 1, 1, 1, 8),
+    (40, 1, 72, 130, 5, 9, 16),
+]
+
+
+def _prim_inputs(shape, seed):
+    h, n1, c, t, r, m, k = shape
+    rng = np.random.default_rng(seed)
+    f = lambda n: rng.standard_normal(n).astype(np.float32)
+    l = np.array([(7 * q + 1) % n1 for q in range(h)], dtype=np.int64)
+    return dict(kv=f(t * n1 * c), b=f(h * c), l=l, a=f(h * t), A=f(h * r * c), s=f(m * k), av=f(m), bv=f(k))
+
+
+@pytest.mark.skipif(not O.hostref_available(), reason="oracle/_ref/libhostref.so not built (reference tree absent)")
+@pytest.mark.parametrize("shape", PRIM_SHAPES)
+def test_prims_port_matches_reference(oracle, shape):
+    """The C restatement of the host-half primitives (prims_oracle.c) against the reference's own
+    src/host/rt_host.c compiled from its sources: every output bit for bit."""
+    h, n1, c, t, r, m, k = shape
+    d = _prim_inputs(shape, 5)
+    cases = [
+        (lambda u: oracle.ip21_kv(d["kv"], n1, c, d["l"], h, t, d["b"], use_ref=u)),
+        (lambda u: oracle.ip12_kv(d["a"], d["kv"], n1, c, d["l"], h, t, use_ref=u)),
+        (lambda u: oracle.ip21(d["A"], h, r, c, d["b"], use_ref=u)),
+        (lambda u: oracle.scale_outer(d["s"], 0.9375, d["av"], d["bv"], m, k, use_ref=u)),
+    ]
+    for f in cases:
+        assert np.array_equal(f(False).view(np.uint32), f(True).view(np.uint32))
+
+
+def test_prims_port_order(oracle):
+    """The restatement's lane order, on inputs where it shows: 8-lane sums differ from a plain
+    left-to-right sum, and ip12_kv is one ordered chain."""
+    c = 16
+    row = np.array([1e8, 1, -1e8, 1, 3, 0, 0, 0, 0.5, 0, 0, 0, 0, 0, 0, 0], dtype=np.float32)
+    b = np.ones(c, dtype=np.float32)
+    z = oracle.ip21(row, 1, 1, c, b)
+    lanes = [float(np.float32(row[j]) + np.float32(row[j + 8])) for j in range(8)]
+    want = np.float32((np.float32(lanes[0] + lanes[4]) + np.float32(lanes[2] + lanes[6])) +
+                      np.float32(np.float32(lanes[1] + lanes[5]) + np.float32(lanes[3] + lanes[7])))
+    assert z[0] == want
+    a = np.array([1e8, 1.0, -1e8], dtype=np.float32)
+    kv = np.ones(3 * 8, dtype=np.float32)
+    z = oracle.ip12_kv(a, kv, 1, 8, np.zeros(1, dtype=np.int64), 1, 3)
+    assert z[0] == np.float32(np.float32(np.float32(1e8) + 1.0) - np.float32(1e8))
