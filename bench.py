@@ -372,12 +372,12 @@ class Bench:
         rt_gemm_silu_q), x goes host->device from pinned memory (rt_b200_pull, the engine's
         link_pull), the round runs (rt_gemv_go) and y comes back device->host (rt_b200_push, the
         engine's link_push), which returns once y is on the host. Wall-clock time of whole steps,
-        after `warmup` steps. The headline runs with direct pushes (rt_b200_set_push_direct: the
-        product kernel stores y into the pinned host buffer itself and raises a host flag, which
-        push polls; the step's rounds are all single products of one token). Also timed: the same
-        rounds with push as a device-to-host copy and a stream synchronization, and opened before
-        x is pulled (rt_gemv_open: the round's kernel is launched at once and streams its weights,
-        gated on the GPU until go)."""
+        after `warmup` steps. Also timed: the same rounds with direct pushes
+        (rt_b200_set_push_direct: the product kernel stores y into the pinned host buffer itself
+        and raises a host flag, which push polls), and opened before x is pulled (rt_gemv_open:
+        the round's kernel is launched at once and streams its weights, gated on the GPU until
+        go). Both measure slower in this loop, where each round's pull follows the previous
+        round at once."""
         import ctypes as C
         torch, rt = self.torch, self.rt
         rt.set_async(True)
@@ -425,20 +425,20 @@ class Bench:
         dt_open = timed(steps)
         for r in rounds:
             r.open = 0
-        dt_copy = timed(steps)
-        rt.set_push_direct(True)
         dt = timed(steps)
+        rt.set_push_direct(True)
+        dt_direct = timed(steps)
         rt.set_push_direct(False)
         total = WL.step_bytes(1, self.layers)
         return {"value": round(total / dt / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(dt * 1e3, 3), "tok_s": round(1.0 / dt, 1),
                 "path": "per round, from C (engine_rounds.c): rt_gemv_q / rt_gemm_silu_q, rt_b200_pull of x, "
-                        "rt_gemv_go, rt_b200_push of y (pinned host buffers; direct pushes: the product kernel "
-                        "writes y to the host buffer and raises a host flag)",
-                "copy_pushes": {"ms_per_step": round(dt_copy * 1e3, 3), "value": round(total / dt_copy / 1e9, 1),
-                                "path": "the same with push as a device-to-host copy and a stream synchronization"},
+                        "rt_gemv_go, rt_b200_push of y (pinned host buffers)",
+                "direct_pushes": {"ms_per_step": round(dt_direct * 1e3, 3), "value": round(total / dt_direct / 1e9, 1),
+                                  "path": "the same with rt_b200_set_push_direct: y written to the host buffer by the "
+                                          "product kernel, push polls its host flag"},
                 "opened_rounds": {"ms_per_step": round(dt_open * 1e3, 3), "value": round(total / dt_open / 1e9, 1),
-                                  "path": "copy pushes, with rt_gemv_open before the pull"}}
+                                  "path": "the same with rt_gemv_open before the pull"}}
 
     def _graph(self, fns):
         """The calls captured as one CUDA graph on a side stream (the runtime follows the stream)."""

@@ -222,8 +222,11 @@ RTB_API void rt_b200_set_overlap(struct rt *R, int on);
  * a flag in mapped host memory; push returns once the host sees the flag (y is then whole on the
  * host) with the round's error status, without a device-to-host copy or a stream synchronization.
  * Any other call on R, or a push of anything else, launches the held round first as rt_gemv_go
- * would have. The caller vouches that between rt_gemv_go and its next call on R it enqueues
- * nothing of its own on R's stream that needs the held product. 0 (default): go launches at once. */
+ * would have. The held product runs as a CUDA graph, captured the first time that round (same
+ * product, same y) comes and launched as it is when it comes again (an engine's rounds repeat
+ * every token; at most 4096 graphs are kept). The caller vouches that between rt_gemv_go and its
+ * next call on R it enqueues nothing of its own on R's stream that needs the held product.
+ * 0 (default): go launches at once. */
 RTB_API void rt_b200_set_push_direct(struct rt *R, int on);
 
 /* R's CUDA stream (a cudaStream_t); set_stream makes R use the caller's stream instead (NULL:

@@ -718,8 +718,10 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
             __threadfence_system();
             if (atomicAdd(p.host_ctr, 1u) == gridDim.x - 1) {
                 *p.host_ctr = 0;
+                const unsigned seq = p.host_ctr[1] + 1; // (only this CTA writes it)
+                p.host_ctr[1] = seq;
                 __threadfence_system();
-                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.host_flag), "r"(p.host_seq) : "memory");
+                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.host_flag), "r"(seq) : "memory");
             }
         }
     }

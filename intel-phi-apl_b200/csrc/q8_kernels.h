@@ -95,14 +95,15 @@ struct GemvParamsT {
     unsigned gate_value;
     // A round whose y also goes straight to the host (rt_b200_push of a held round, one job):
     // every output is stored at y_host[the same index] as well (mapped pinned host memory, the
-    // device's address of it), and the last CTA to finish writes host_seq into *host_flag (mapped
-    // host memory, which the host polls) after a system-scope fence, so that the host sees y
-    // whole once it sees the flag. host_ctr counts the finished CTAs (device memory, left at 0).
+    // device's address of it), and the last CTA to finish advances host_ctr[1] (the direct
+    // rounds so far, device memory) and writes its new value into *host_flag (mapped host memory,
+    // which the host polls) after a system-scope fence, so that the host sees y whole once it
+    // sees the flag. host_ctr[0] counts the finished CTAs (left at 0). The parameters hold no
+    // per-launch value, so a CUDA graph of the round can be launched again as it is.
     // Null y_host: none of it.
     float *y_host;
     unsigned *host_flag;
     unsigned *host_ctr;
-    unsigned host_seq;
 };
 using GemvParams = GemvParamsT<MAX_JOBS>;
 

@@ -14,6 +14,8 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <string>
+#include <unordered_map>
 #include <new>
 #include <vector>
 
@@ -117,8 +119,10 @@ struct Ctx {
     bool round_open = false;
     // direct pushes (rt_b200_set_push_direct): a round of one CUDA-core product that rt_gemv_go
     // held back instead of launching, its launch left to the next call on R; the host word the
-    // product's last CTA raises (mapped, beside the error mirror), its device address, the CTA
-    // counter behind it and the rounds pushed so far
+    // product's last CTA raises (mapped, beside the error mirror), its device address, the
+    // device counters behind it (finished CTAs, direct rounds) and the direct rounds launched so
+    // far; the rounds' kernels as CUDA graphs (captured once on a private stream, launched as
+    // they are for a round seen before)
     bool direct = false;
     bool held = false;
     Item held_item;
@@ -126,6 +130,8 @@ struct Ctx {
     unsigned *h_flag_dev = nullptr;
     unsigned *d_hctr = nullptr;
     unsigned host_seq = 0;
+    cudaStream_t cap = nullptr;
+    std::unordered_map<std::string, cudaGraphExec_t> graphs;
 };
 
 // cuStreamWriteValue32 (the driver's stream memory operation: executed by the GPU's front end in
@@ -530,7 +536,7 @@ bool launch_held(Ctx *c) {
 }
 
 // The device's address of host memory the GPU can write (pinned and mapped), else null.
-float *mapped(void *host) {
+float *mapped(const void *host) {
     cudaPointerAttributes a;
     if (cudaPointerGetAttributes(&a, host) != cudaSuccess) {
         cudaGetLastError(); // (an unregistered pointer: not an error of R's)
@@ -539,27 +545,52 @@ float *mapped(void *host) {
     return a.type == cudaMemoryTypeHost ? static_cast<float *>(a.devicePointer) : nullptr;
 }
 
-// The held round, launched with its y also stored into host memory (the device address yh) and a
-// host flag raised by its last CTA; returns once the flag is up (y is on the host) or the launch
-// ended without it. The host polls the flag and, now and then, whether the stream has finished: a
-// kernel that faulted raises no flag, and the wait then ends through the stream's error.
+// The held round, launched with the product's y also stored into host memory (the device address
+// yh) and a host flag raised by its last CTA; returns once the flag is up (y is on the host) or the
+// launch ended without it. The kernel runs as a CUDA graph, captured the first time this round
+// (same product, same y) comes and launched as it is afterwards: an engine repeats its rounds
+// every token, and the graph's launch skips the kernel's 2.4 KB of parameters. (The round's pull
+// stays a copy of its own, issued at rt_b200_pull: as a node of the graph it measured 6.6 us a
+// round against 2.5.) The host polls the flag and, now and then, whether the stream has finished:
+// a kernel that faulted raises no flag, and the wait then ends through the stream's error.
 int push_direct(Ctx *c, const Item &it, float *yh) {
     q8::GemvParams p;
     memset(&p, 0, sizeof p);
     p.err = c->d_err;
-    p.early = c->overlap ? 1 : 0;
     p.njobs = 1;
     p.job[0] = cuda_core_job(it, 0, it.rows, 0);
-    unsigned seq = ++c->host_seq;
-    if (seq == 0) // (0 is the flag's initial value)
-        seq = c->host_seq = 1;
     p.y_host = yh;
     p.host_flag = c->h_flag_dev;
     p.host_ctr = c->d_hctr;
-    p.host_seq = seq;
+    const std::string key(reinterpret_cast<const char *>(&p), sizeof p);
     c->synced = false;
-    if (!cuda_ok(c, q8::launch_gemv(p, c->num_sms, 0, c->stream, c->overlap), "gemv launch"))
+    cudaGraphExec_t exec = nullptr;
+    auto found = c->graphs.find(key);
+    if (found != c->graphs.end()) {
+        exec = found->second;
+    } else {
+        if (c->graphs.size() >= 4096) { // (a bound on what a changing engine could pile up)
+            for (auto &g : c->graphs)
+                cudaGraphExecDestroy(g.second);
+            c->graphs.clear();
+        }
+        cudaGraph_t g = nullptr;
+        bool ok = cuda_ok(c, cudaStreamBeginCapture(c->cap, cudaStreamCaptureModeThreadLocal), "capture a round");
+        if (ok) {
+            ok = cuda_ok(c, q8::launch_gemv(p, c->num_sms, 0, c->cap, false), "gemv launch");
+            const cudaError_t e = cudaStreamEndCapture(c->cap, &g);
+            ok = ok && cuda_ok(c, e, "capture a round");
+        }
+        ok = ok && cuda_ok(c, cudaGraphInstantiate(&exec, g, 0), "instantiate a round");
+        if (g)
+            cudaGraphDestroy(g);
+        if (!ok)
+            return c->status;
+        c->graphs.emplace(key, exec);
+    }
+    if (!cuda_ok(c, cudaGraphLaunch(exec, c->stream), "launch a round"))
         return c->status;
+    const unsigned seq = ++c->host_seq; // the kernel's count of direct rounds, one ahead now
     bool up = false;
     for (unsigned long i = 1;; ++i) {
         if (*c->h_flag == seq) {
@@ -952,7 +983,8 @@ int rt_init(struct rt *R, int threads) {
         cudaMemcpy(c->d_err + 2, &h_err_dev, sizeof h_err_dev, cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMalloc(&c->d_round, sizeof(unsigned) * q8::ROUND_CTR_STRIDE * q8::MAX_CHAIN_JOBS) != cudaSuccess ||
         cudaMalloc(&c->d_gate, sizeof(unsigned)) != cudaSuccess || cudaMemset(c->d_gate, 0, sizeof(unsigned)) != cudaSuccess ||
-        cudaMalloc(&c->d_hctr, sizeof(unsigned)) != cudaSuccess || cudaMemset(c->d_hctr, 0, sizeof(unsigned)) != cudaSuccess ||
+        cudaMalloc(&c->d_hctr, 2 * sizeof(unsigned)) != cudaSuccess || cudaMemset(c->d_hctr, 0, 2 * sizeof(unsigned)) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&c->cap, cudaStreamNonBlocking) != cudaSuccess ||
         cudaStreamCreateWithFlags(&c->link, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&c->ev_before, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&c->ev_link, cudaEventDisableTiming) != cudaSuccess) {
@@ -961,6 +993,8 @@ int rt_init(struct rt *R, int threads) {
         cudaFree(c->d_round);
         cudaFree(c->d_gate);
         cudaFree(c->d_hctr);
+        if (c->cap)
+            cudaStreamDestroy(c->cap);
         if (c->link)
             cudaStreamDestroy(c->link);
         if (c->ev_before)
@@ -996,6 +1030,10 @@ void rt_b200_free(struct rt *R) {
     cudaFree(c->d_round);
     cudaFree(c->d_gate);
     cudaFree(c->d_hctr);
+    for (auto &g : c->graphs)
+        cudaGraphExecDestroy(g.second);
+    c->graphs.clear();
+    cudaStreamDestroy(c->cap);
     cudaFree(c->scratch);
     cudaFree(c->d_err);
     cudaEventDestroy(c->ev_before);
@@ -1038,9 +1076,11 @@ void rt_gemv_open(struct rt *R) {
 }
 
 void rt_gemv_go(struct rt *R) {
-    Ctx *c = ctx_of(R);
+    Ctx *c = ctx_raw(R);
     if (!c)
         return;
+    if (c->held) // a round held before goes first
+        launch_held(c);
     std::vector<Item> items;
     items.swap(c->queue);
     bool ok = true;

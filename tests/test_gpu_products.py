@@ -267,7 +267,8 @@ def test_opened_round_without_go_gives_up_and_recovers(cuda, rtb, oracle):
 def test_direct_push(cuda, rtb, oracle):
     """rt_b200_set_push_direct: a round of one product, held back by rt_gemv_go, then pushed into
     mapped pinned host memory, writes y there from its own kernel and raises a host flag; push
-    returns with y whole on the host. Checked bit for bit on the host and in device memory over
+    returns with y whole on the host. The product runs as a CUDA graph cached by its arguments:
+    the later rounds reuse the graphs, with new x pulled into the same buffer. Checked bit for bit on the host and in device memory over
     back-to-back rounds (a gemv, a SwiGLU pair, a row gather, a 2-token product, the 151936-row
     head), and the rounds that must take the usual path: a push of part of y, a push into
     pageable memory, a held round followed by another call instead of a push, and a 16-token
@@ -295,9 +296,10 @@ def test_direct_push(cuda, rtb, oracle):
     with rtb.Runtime() as rt:
         rt.set_async(True)
         rt.set_push_direct(True)
-        for k in range(3):
+        hx = cuda.empty((16, cols), dtype=cuda.float32).pin_memory()
+        for k in range(3):  # the same buffers each time: from the second, the rounds' cached graphs
             x = xs(oracle, 16, cols, 215 + k)
-            hx = cuda.from_numpy(x).pin_memory()
+            hx.copy_(cuda.from_numpy(x))
             want = oracle.gemm(a.q8, 8192, cols, x, 2)
             # a gemv, pushed whole into pinned memory: direct
             fresh()
