@@ -246,8 +246,8 @@ class Bench:
             rt.gemm_silu(L["gate"].data_ptr(), L["up"].data_ptr(), WL.FF, WL.D, xd, m, y[("h", m)].data_ptr())
             rt.gemm(L["down"].data_ptr(), WL.D, WL.FF, xf, m, y[("down", m)].data_ptr())
         rt.gemm(self.head.data_ptr(), WL.VOCAB, WL.D, xd, m, y[("head", m)].data_ptr())
-        rt.flush()  # with row shards: the head's gather finishes inside the step (one kernel)
-        return 4 * len(self.w) + 1 + (1 if self.world > 1 and rt.peer_gather() else 0)
+        rt.flush()  # with row shards: the step waits for its last gathers (side stream)
+        return (4 * len(self.w) + 1) * (2 if self.world > 1 and rt.peer_gather() else 1)
 
     def barrier(self):
         if self.world > 1:

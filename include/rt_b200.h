@@ -242,14 +242,15 @@ RTB_API void rt_b200_free(struct rt *R);
  * consecutive rows, rank-major, rows % world == 0) while rows, y and t keep the whole product's
  * meaning: each rank computes its rows and y is filled on every rank over NVLink.
  * - A single product of <= 4 tokens (rt_gemv, rt_gemm, rt_gemm_silu) gathers y over NVLink
- *   without NCCL: every output is also stored into each peer's staging buffer (CUDA IPC mappings
- *   set up by rt_b200_shard) and the last CTA raises a flag on every peer. The peers' rows are then
- *   copied into y by the next such product's own kernel, after its own rows (by then the peers'
- *   flags are normally up; the wait is bounded), or, before anything else is run, pulled or
- *   pushed, or when R is synchronized or flushed, by a small kernel of their own. So in async mode y is
- *   whole once the next call on R has been made; blocking calls return with y whole. A sequence
- *   captured into a CUDA graph must end with rt_b200_flush, so that the graph finishes its last
- *   gather itself.
+ *   without NCCL: the product kernel also stores every output into each peer's staging buffer
+ *   (CUDA IPC mappings set up by rt_b200_shard), and a small gather kernel on a side stream of
+ *   R's publishes the round, waits (bounded) for the peers', and copies their rows into y. R's
+ *   stream goes on with the next product at once; it waits for a gather only where it must: a
+ *   product whose x or y overlaps a y still being gathered, the product two rounds later (the
+ *   staging buffers' reuse), and whatever else runs, pulls or pushes on R, or R synchronized or
+ *   flushed. So in async mode y is whole, on R's stream, for what follows; blocking calls return
+ *   with y whole. A sequence captured into a CUDA graph must end with rt_b200_flush, which joins
+ *   the side stream back into the capture.
  * - Queued rounds, t > 4 and the tensor-core path all-gather y with NCCL.
  * All ranks must issue the same products in the same order. nccl_id is the 128-byte ncclUniqueId
  * from rt_b200_nccl_id on rank 0, passed to every rank by the caller. 0 or an RTB_E* code.

@@ -271,53 +271,6 @@ __device__ __noinline__ bool wait_gate(const unsigned *gate, unsigned value) {
     }
 }
 
-// Waits until *flag >= value, read at system scope (a peer GPU raises it over NVLink), bounded.
-__device__ __noinline__ bool wait_flag64(const unsigned long long *flag, unsigned long long value) {
-    const long long t0 = clock64();
-    for (;;) {
-        unsigned long long v;
-        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
-        if (v >= value)
-            return true;
-        const long long dt = clock64() - t0;
-        if (dt > WAIT_LIMIT_CYCLES)
-            return false;
-        if (dt > 20000)
-            __nanosleep(100);
-    }
-}
-
-// The previous row-sharded product's gather, run by every thread of a CTA after the CTA's own
-// tiles: thread 0 waits, bounded, for the peers' flags of that product's round (they are normally
-// long up: the peers are past that round too), then the CTA copies its share of the peers' rows
-// from this GPU's staging image of the round into that product's y. This launch's own round is
-// not published yet, so the local round counter still names that product's round.
-__device__ __noinline__ void peer_finish_epilogue(const PeerOut &po, unsigned *err, int nthreads) {
-    __shared__ int ok;
-    const unsigned char *mine = po.region[po.rank];
-    const unsigned long long round = *reinterpret_cast<const volatile unsigned long long *>(mine + 72);
-    if (threadIdx.x == 0) {
-        bool good = true;
-        for (int w = 0; w < po.world && good; ++w)
-            if (w != po.rank)
-                good = wait_flag64(reinterpret_cast<const unsigned long long *>(mine) + w, round);
-        if (!good)
-            report(err, ERR_TIMEOUT_PEER);
-        ok = good;
-    }
-    __syncthreads();
-    if (!ok)
-        return;
-    const float *stage = reinterpret_cast<const float *>(mine + peer_image(round));
-    const long long rows = po.fin_rows, lr = rows / po.world, own0 = (long long)po.rank * lr;
-    const long long n = (long long)po.fin_t * rows;
-    for (long long e = (long long)blockIdx.x * nthreads + threadIdx.x; e < n; e += (long long)gridDim.x * nthreads) {
-        const long long tok = e / rows, row = e - tok * rows;
-        if (row < own0 || row >= own0 + lr)
-            po.fin_y[tok * rows + row] = __ldcg(stage + e);
-    }
-}
-
 // The failure path's self-test: one thread waits on a device counter that nothing advances, then
 // on an mbarrier that nothing arrives on. Each wait gives up after WAIT_LIMIT_CYCLES (about a
 // second) and reports its bit, as a stuck wait in a product kernel does; the kernel then returns.
@@ -511,7 +464,7 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
             // programmatic launch this kernel may start before it does
             grid_wait();
             const unsigned long long round0 =
-                *reinterpret_cast<const volatile unsigned long long *>(po.region[po.rank] + 72);
+                *reinterpret_cast<const volatile unsigned long long *>(po.region[po.rank] + PEER_PRODUCED);
             stage_off = peer_image(round0 + 1);
         }
         float *const yh = p.y_host;
@@ -684,29 +637,17 @@ __global__ void __launch_bounds__(Cfg<MT, CTAS>::NT, CTAS) gemv_exact_kernel(con
     }
 
     if (p.peer.on) {
-        // The previous product's gather first (its rows land before this round is published),
-        // then the last CTA to finish publishes the round: the CTA's peer stores are ordered
-        // (barrier, then one system-scope fence) before its count, the last count before the flags.
+        // The last CTA to finish advances the round count (every CTA has read it by then: its
+        // chain warps read it before the CTA's barrier below). The gather kernel on the side
+        // stream publishes the round, after this kernel has completed.
         __syncthreads();
-        if (p.peer.fin_on) {
-            peer_finish_epilogue(p.peer, p.err, C::NT);
-            __syncthreads();
-        }
         if (tid == 0) {
             unsigned char *mine = p.peer.region[p.peer.rank];
-            unsigned *done = reinterpret_cast<unsigned *>(mine + 64);
-            __threadfence_system();
+            unsigned *done = reinterpret_cast<unsigned *>(mine + PEER_PCTAS);
             if (atomicAdd(done, 1u) == gridDim.x - 1) {
-                __threadfence_system();
-                volatile unsigned long long *round = reinterpret_cast<volatile unsigned long long *>(mine + 72);
-                const unsigned long long e = *round + 1;
-                *round = e;
+                unsigned long long *round = reinterpret_cast<unsigned long long *>(mine + PEER_PRODUCED);
+                *round = *round + 1;
                 *done = 0;
-                for (int w = 0; w < p.peer.world; ++w)
-                    if (w != p.peer.rank) {
-                        unsigned long long *flag = reinterpret_cast<unsigned long long *>(p.peer.region[w]) + p.peer.rank;
-                        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(flag), "l"(e) : "memory");
-                    }
             }
         }
     }

@@ -41,26 +41,34 @@ struct GemvJob {
 // other rounds do not share it).
 constexpr int ROUND_CTR_STRIDE = 32;
 
-// ---- the fused all-gather of a row-sharded product over NVLink (one job per launch)
+// ---- the all-gather of a row-sharded product over NVLink (one job per launch)
 // Each rank owns a peer region, mapped by every other rank (CUDA IPC):
-//   [0, 64)            flags: uint64 per writer rank, the last round that rank published here
-//   [64, 68)           uint32 completion counter of the product kernel's CTAs (local use)
-//   [72, 80)           uint64 round: products completed by this rank (advanced on the device, so
-//                      CUDA-graph replays keep counting)
+//   [0, 64)     flags[w]: uint64, the last round rank w has published (w's gather kernel writes it)
+//   [64, 128)   reads[w]: uint64, the last round rank w has copied out of its own staging
+//   [128, 132)  uint32, the product kernel's finished CTAs (local use)
+//   [132, 136)  uint32, the gather kernel's finished CTAs (local use)
+//   [136, 144)  uint64, rounds produced by this rank (advanced by the product kernel's last CTA)
+//   [144, 152)  uint64, rounds gathered by this rank (advanced by the gather kernel's last CTA)
 //   [PEER_HDR, +PEER_IMAGES*PEER_STAGE_BYTES)  staging images of y, [t][rows] fp32, round r in
-//                      image r % PEER_IMAGES.
-// The product kernel of round r stores every output into its local y and into image r of every
-// peer; its last CTA advances `round` and raises its flag on every peer. Round r's gather is
-// finished by the next row-sharded product (at its end, after its own rows: by then the peers are
-// done with round r) or by launch_peer_finish: both wait (bounded) for all peers' flags of round r
-// and copy the peers' rows from image r into y. Three images: a rank's round r+1 ends only after
-// it has seen every peer's flag of round r, which that peer raised after copying out its round
-// r-1 rows, so no peer writes round r+2 into an image that is still being read.
+//               image r % PEER_IMAGES.
+// Round r: the product kernel (R's stream) stores each output into its local y and into image r
+// of every peer (NVLink stores), and its last CTA advances the round count; nothing else, so the
+// next product follows at once. A small gather kernel on a side stream, after the product (an
+// event), publishes round r (a system-scope fence, then its flag in every peer's region), waits
+// (bounded) for every peer's flag of round r, copies the peers' rows from its own image r into
+// y, tells every peer it has read round r, and waits (bounded) until every peer has read round
+// r - 1. The product of round r + PEER_IMAGES - 1 waits (on R's stream, an event) for the gather
+// of round r, so it overwrites the image of round r - 1 only after every rank has read it: with
+// 8 images that gather is long done and the wait costs nothing (with 3, a product waited on the
+// gather two rounds back and measured 2.26 ms for the 2-GPU step). No product kernel ever waits
+// on another GPU: the cross-GPU waits are all in the gather kernels.
 constexpr int MAX_PEERS = 8;
 constexpr size_t PEER_HDR = 256;
-constexpr int PEER_IMAGES = 3;
-constexpr size_t PEER_STAGE_BYTES = size_t(16) << 20;
+constexpr int PEER_IMAGES = 8;
+constexpr size_t PEER_STAGE_BYTES = size_t(8) << 20; // t * rows * 4 bytes at most (the head at t = 4: 2.4 MB)
 constexpr size_t PEER_REGION_BYTES = PEER_HDR + PEER_IMAGES * PEER_STAGE_BYTES;
+constexpr size_t PEER_FLAGS = 0, PEER_READS = 64, PEER_PCTAS = 128, PEER_GCTAS = 132, PEER_PRODUCED = 136,
+                 PEER_GATHERED = 144;
 __host__ __device__ constexpr size_t peer_image(unsigned long long round) {
     return PEER_HDR + size_t(round % PEER_IMAGES) * PEER_STAGE_BYTES;
 }
@@ -69,14 +77,6 @@ struct PeerOut {
     unsigned char *region[MAX_PEERS]; // every rank's region as mapped on this GPU (own: local)
     long long row0, rows_total;       // this rank's first output row; the product's rows
     int rank, world, on;              // on = 0: an unsharded launch
-    // The previous row-sharded product's gather, finished by this launch (fin_on): its y[t][rows]
-    // still lacks the peers' rows, which sit in this rank's staging image of that round. After its
-    // own tiles each CTA waits (bounded) for every peer's flag of that round and copies a share of
-    // those rows into fin_y, before the launch publishes its own round (this product's x and y do
-    // not overlap fin_y: the host finishes the gather with its own kernel otherwise).
-    float *fin_y;
-    long long fin_rows;
-    int fin_t, fin_on;
 };
 
 template <int NJ>
@@ -142,11 +142,9 @@ cudaError_t launch_scale_outer(float *z, const float *s, float g, const float *a
                                long long k, cudaStream_t stream);
 cudaError_t preload_prims();
 
-// After a peer-gathered launch: wait for every peer's flag of this round, then copy their rows
-// of y ([t][ldy], ldy = rows_total) from the staging image.
-// pdl: launch with programmatic stream serialization (overlaps the product's tail).
-cudaError_t launch_peer_finish(const PeerOut &po, float *y, long long ldy, int t, unsigned *err, cudaStream_t stream,
-                               bool pdl);
+// The gather of a peer-gathered product's round (the protocol above), on the side stream after
+// the product: y is the product's [t][rows_total] output, whose own rows are in place.
+cudaError_t launch_peer_gather(const PeerOut &po, float *y, int t, unsigned *err, cudaStream_t stream);
 
 // Launches the exact CUDA-core product over p.job[0..njobs) (all with the same m). Fills the
 // tile fields. grid_limit 0 = one CTA per SM. pdl: launch with programmatic stream serialization

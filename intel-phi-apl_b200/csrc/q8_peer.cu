@@ -1,6 +1,7 @@
-// q8_peer.cu: the receiving half of the fused all-gather of a row-sharded product (the sending
-// half is in the product kernel: q8_gemv.cu). The layout of a rank's peer region is in
-// q8_kernels.h.
+// q8_peer.cu: the gather kernel of a row-sharded product's round (the protocol and the region's
+// layout are in q8_kernels.h; the stores into the peers' staging images are in the product
+// kernel, q8_gemv.cu). It runs on a side stream after the product, so the next product on R's
+// stream does not wait for it.
 #include <cuda_runtime.h>
 
 #include "q8_kernels.h"
@@ -15,42 +16,83 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
     return v;
 }
 
-// Every CTA waits for the peers' flags (one thread per peer, bounded), then copies its share of
-// the peers' rows out of the staging image of this round.
-__global__ void peer_finish_kernel(const PeerOut po, float *y, long long ldy, int t, unsigned *err) {
-    // Under programmatic launch the next product may start now (it prefetches its weights and
-    // waits for this kernel before reading x); this kernel waits for the product before it.
-    if (threadIdx.x == 0)
-        grid_launch_dependents();
-    grid_wait();
+__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Waits (bounded, about a second) until every peer's word at `off` in this rank's region has
+// reached `value`; false if one never did.
+__device__ bool wait_peers(const PeerOut &po, size_t off, unsigned long long value) {
     const unsigned char *mine = po.region[po.rank];
-    const unsigned long long round =
-        *reinterpret_cast<const volatile unsigned long long *>(mine + 72); // advanced by the product kernel
-    __shared__ int ok;
-    if (threadIdx.x == 0)
-        ok = 1;
-    __syncthreads();
-    if (threadIdx.x < unsigned(po.world) && int(threadIdx.x) != po.rank) {
-        const unsigned long long *flag = reinterpret_cast<const unsigned long long *>(mine) + threadIdx.x;
+    for (int w = 0; w < po.world; ++w) {
+        if (w == po.rank)
+            continue;
+        const unsigned long long *word = reinterpret_cast<const unsigned long long *>(mine + off) + w;
         const long long t0 = clock64();
-        while (ld_acquire_sys(flag) < round) {
-            if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
-                report(err, ERR_TIMEOUT_PEER);
-                ok = 0;
-                break;
-            }
+        while (ld_acquire_sys(word) < value) {
+            const long long dt = clock64() - t0;
+            if (dt > WAIT_LIMIT_CYCLES)
+                return false;
+            if (dt > 20000)
+                __nanosleep(64);
+        }
+    }
+    return true;
+}
+
+constexpr int GATHER_THREADS = 128; // small, so its CTAs fit beside a product's on any SM
+
+// Round r = the rounds gathered so far + 1 (gathers run in order on their stream, one per
+// peer-gathered product). Every CTA: wait for the peers' flags of round r (CTA 0 first publishes
+// this rank's), copy its share of the peers' rows out of this GPU's image r into y; the last CTA
+// then tells the peers it has read round r, waits until every peer has read round r - 1 (so the
+// product of round r + 2, which waits for this kernel, may overwrite their images of round
+// r - 1), and advances the gathered count.
+__global__ void __launch_bounds__(GATHER_THREADS) peer_gather_kernel(const PeerOut po, float *y, int t, unsigned *err) {
+    __shared__ int ok;
+    __shared__ unsigned long long round_sh;
+    unsigned char *mine = po.region[po.rank];
+    if (threadIdx.x == 0) {
+        const unsigned long long r = *reinterpret_cast<const volatile unsigned long long *>(mine + PEER_GATHERED) + 1;
+        round_sh = r;
+        if (blockIdx.x == 0) {
+            // the product of round r has completed (this kernel follows it): its stores into the
+            // peers' images are made visible to them before the flag
+            __threadfence_system();
+            for (int w = 0; w < po.world; ++w)
+                if (w != po.rank)
+                    st_release_sys(reinterpret_cast<unsigned long long *>(po.region[w] + PEER_FLAGS) + po.rank, r);
+        }
+        ok = wait_peers(po, PEER_FLAGS, r) ? 1 : 0;
+        if (!ok)
+            report(err, ERR_TIMEOUT_PEER);
+    }
+    __syncthreads();
+    const unsigned long long r = round_sh;
+    if (ok) {
+        const float *stage = reinterpret_cast<const float *>(mine + peer_image(r));
+        const long long rows = po.rows_total, lr = rows / po.world, own0 = (long long)po.rank * lr;
+        const long long n = (long long)t * rows;
+        for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
+            const long long tok = e / rows, row = e - tok * rows;
+            if (row < own0 || row >= own0 + lr)
+                y[tok * rows + row] = __ldcg(stage + e);
         }
     }
     __syncthreads();
-    if (!ok)
-        return;
-    const float *stage = reinterpret_cast<const float *>(mine + peer_image(round));
-    const long long rows = po.rows_total, lr = rows / po.world, own0 = (long long)po.rank * lr;
-    const long long n = (long long)t * rows;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-        const long long tok = i / rows, row = i - tok * rows;
-        if (row < own0 || row >= own0 + lr)
-            y[tok * ldy + row] = stage[i];
+    if (threadIdx.x == 0) {
+        unsigned *done = reinterpret_cast<unsigned *>(mine + PEER_GCTAS);
+        __threadfence(); // this CTA's reads of the image are done before its count
+        if (atomicAdd(done, 1u) == gridDim.x - 1) {
+            *done = 0;
+            __threadfence();
+            for (int w = 0; w < po.world; ++w)
+                if (w != po.rank)
+                    st_release_sys(reinterpret_cast<unsigned long long *>(po.region[w] + PEER_READS) + po.rank, r);
+            if (!wait_peers(po, PEER_READS, r - 1))
+                report(err, ERR_TIMEOUT_PEER);
+            *reinterpret_cast<volatile unsigned long long *>(mine + PEER_GATHERED) = r;
+        }
     }
 }
 
@@ -58,27 +100,18 @@ __global__ void peer_finish_kernel(const PeerOut po, float *y, long long ldy, in
 
 cudaError_t preload_peer() {
     cudaFuncAttributes a;
-    return cudaFuncGetAttributes(&a, peer_finish_kernel);
+    return cudaFuncGetAttributes(&a, peer_gather_kernel);
 }
 
-cudaError_t launch_peer_finish(const PeerOut &po, float *y, long long ldy, int t, unsigned *err, cudaStream_t stream,
-                               bool pdl) {
+cudaError_t launch_peer_gather(const PeerOut &po, float *y, int t, unsigned *err, cudaStream_t stream) {
     if (!po.on || po.world < 2 || po.world > MAX_PEERS || t < 1 ||
         size_t(t) * size_t(po.rows_total) * sizeof(float) > PEER_STAGE_BYTES)
         return cudaErrorInvalidValue;
     const long long n = (long long)t * po.rows_total;
-    int grid = int((n + 1023) / 1024);
+    long long grid = (n + GATHER_THREADS * 16 - 1) / (GATHER_THREADS * 16); // ~16 outputs per thread
     grid = grid < 1 ? 1 : (grid > 64 ? 64 : grid);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(256);
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, peer_finish_kernel, po, y, ldy, t, err);
+    peer_gather_kernel<<<unsigned(grid), GATHER_THREADS, 0, stream>>>(po, y, t, err);
+    return cudaGetLastError();
 }
 
 } // namespace q8

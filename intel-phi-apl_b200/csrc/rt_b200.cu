@@ -97,11 +97,20 @@ struct Ctx {
     unsigned char *peer_local = nullptr;
     unsigned char *peer_map[q8::MAX_PEERS] = {};
     bool peer_ok = false;
-    // the last row-sharded product whose peers' rows are not in its y yet (its gather is finished
-    // by the next such product's kernel, or by the finish kernel at the next anything else)
-    bool pending = false;
-    float *pending_y = nullptr;
-    long long pending_rows = 0, pending_t = 0;
+    // the row-sharded products' gathers (q8_kernels.h), on a side stream: the stream, the events of
+    // the latest rounds (slot = round % PEER_IMAGES: the product done on R's stream, the gather
+    // done on the side stream), the capture each gather event was recorded in (0: none), the
+    // rounds issued, and the y whose gathers R's stream has not waited for yet
+    cudaStream_t gside = nullptr;
+    cudaEvent_t ev_prod[q8::PEER_IMAGES] = {}, ev_gath[q8::PEER_IMAGES] = {};
+    unsigned long long ev_cap[q8::PEER_IMAGES] = {};
+    unsigned long long prounds = 0;
+    struct PendingY {
+        const float *y;
+        size_t bytes;
+        unsigned long long round;
+    };
+    std::vector<PendingY> pending;
     void *scratch = nullptr; // grows on demand (the tensor-core path's fp16 x)
     size_t scratch_bytes = 0;
     // chains (rt_b200_chain_begin .. rt_b200_chain_end): recorded rounds, and the device counters
@@ -360,34 +369,58 @@ q8::PeerOut peer_out(const Ctx *c) {
     return po;
 }
 
-// Finishes the pending gather with its own kernel (waits for the peers' flags, copies their rows).
-bool flush_pending(Ctx *c) {
-    if (!c->pending)
-        return true;
-    c->pending = false;
-    q8::PeerOut po = peer_out(c);
-    po.on = 1;
-    po.rows_total = c->pending_rows;
-    return cuda_ok(c, q8::launch_peer_finish(po, c->pending_y, c->pending_rows, int(c->pending_t), c->d_err, c->stream,
-                                             c->overlap),
-                   "peer gather");
+// The capture R's stream is in (its id), or 0.
+unsigned long long capture_id(cudaStream_t s) {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    unsigned long long id = 0;
+    if (cudaStreamGetCaptureInfo(s, &st, &id) != cudaSuccess || st != cudaStreamCaptureStatusActive)
+        return 0;
+    return id;
 }
 
+// R's stream waits for the gather of round r (and with it every earlier one: the gathers run in
+// order). An event recorded in another capture context (or none, while capturing) cannot be waited
+// on: work from before a capture must have been synchronised, as graphs need anyway.
+bool wait_gather(Ctx *c, unsigned long long r, unsigned long long cap) {
+    const int slot = int(r % q8::PEER_IMAGES);
+    if (c->ev_cap[slot] != cap)
+        return true;
+    return cuda_ok(c, cudaStreamWaitEvent(c->stream, c->ev_gath[slot], 0), "wait for a gather");
+}
+
+// R's stream waits for every gather issued: y is whole on R's stream from here on.
+bool flush_pending(Ctx *c) {
+    if (c->pending.empty())
+        return true;
+    c->pending.clear();
+    return wait_gather(c, c->prounds, capture_id(c->stream));
+}
+
+// One row-sharded product: the product kernel on R's stream (its rows into y and into the peers'
+// staging), then its round's gather on the side stream. A product whose x overlaps a y still
+// being gathered, or whose y overlaps one other than its own (the same buffer and shape: its own
+// rows, which the gathers leave alone), waits for that gather first; the product of round r waits
+// for the gather of round r - PEER_IMAGES + 1 (the staging images' reuse, q8_kernels.h).
 bool run_peer_gathered(Ctx *c, const Item &it) {
     long long lr, r0;
     shard_rows(c, it.rows, &lr, &r0);
-    // The pending gather is finished inside this launch unless this product's x or y touches the
-    // pending y (then it must be complete first).
-    bool fin = c->pending;
-    if (fin) {
-        const size_t pb = size_t(c->pending_t * c->pending_rows) * 4;
-        if (overlaps(it.x, size_t(it.t * it.cols) * 4, c->pending_y, pb) ||
-            overlaps(it.y, size_t(it.t * it.rows) * 4, c->pending_y, pb)) {
-            if (!flush_pending(c))
-                return false;
-            fin = false;
-        }
-    }
+    const unsigned long long cap = capture_id(c->stream);
+    const size_t xb = size_t(it.t * it.cols) * 4, yb = size_t(it.t * it.rows) * 4;
+    unsigned long long need = 0;
+    for (const Ctx::PendingY &q : c->pending)
+        if (overlaps(it.x, xb, q.y, q.bytes) || (overlaps(it.y, yb, q.y, q.bytes) && !(it.y == q.y && yb == q.bytes)))
+            need = q.round > need ? q.round : need;
+    const unsigned long long r = ++c->prounds;
+    constexpr unsigned long long lag = q8::PEER_IMAGES - 1;
+    if (r > lag && r - lag > need)
+        need = r - lag;
+    if (need && !wait_gather(c, need, cap))
+        return false;
+    std::vector<Ctx::PendingY> keep; // the gathers not waited for yet
+    for (const Ctx::PendingY &q : c->pending)
+        if (q.round > need)
+            keep.push_back(q);
+    c->pending.swap(keep);
     q8::GemvParams p;
     memset(&p, 0, sizeof p);
     p.err = c->d_err;
@@ -409,19 +442,15 @@ bool run_peer_gathered(Ctx *c, const Item &it) {
     po.row0 = r0;
     po.rows_total = it.rows;
     po.on = 1;
-    if (fin) {
-        po.fin_on = 1;
-        po.fin_y = c->pending_y;
-        po.fin_rows = c->pending_rows;
-        po.fin_t = int(c->pending_t);
-        c->pending = false;
-    }
-    if (!cuda_ok(c, q8::launch_gemv(p, c->num_sms, 0, c->stream, c->overlap), "gemv launch"))
+    const int slot = int(r % q8::PEER_IMAGES);
+    if (!cuda_ok(c, q8::launch_gemv(p, c->num_sms, 0, c->stream, c->overlap), "gemv launch") ||
+        !cuda_ok(c, cudaEventRecord(c->ev_prod[slot], c->stream), "gather: event") ||
+        !cuda_ok(c, cudaStreamWaitEvent(c->gside, c->ev_prod[slot], 0), "gather: stream wait") ||
+        !cuda_ok(c, q8::launch_peer_gather(po, it.y, int(it.t), c->d_err, c->gside), "peer gather") ||
+        !cuda_ok(c, cudaEventRecord(c->ev_gath[slot], c->gside), "gather: event"))
         return false;
-    c->pending = true; // this product's gather: finished by whatever runs next
-    c->pending_y = it.y;
-    c->pending_rows = it.rows;
-    c->pending_t = it.t;
+    c->ev_cap[slot] = cap;
+    c->pending.push_back({it.y, yb, r});
     return true;
 }
 
@@ -882,6 +911,19 @@ bool release_gate(Ctx *c, bool more) {
 namespace {
 
 void drop_peers(Ctx *c) {
+    if (c->gside) {
+        cudaStreamSynchronize(c->gside);
+        cudaStreamDestroy(c->gside);
+        c->gside = nullptr;
+        for (int i = 0; i < q8::PEER_IMAGES; ++i) {
+            cudaEventDestroy(c->ev_prod[i]);
+            cudaEventDestroy(c->ev_gath[i]);
+            c->ev_prod[i] = c->ev_gath[i] = nullptr;
+            c->ev_cap[i] = 0;
+        }
+    }
+    c->pending.clear();
+    c->prounds = 0;
     for (int w = 0; w < q8::MAX_PEERS; ++w) {
         if (c->peer_map[w] && c->peer_map[w] != c->peer_local)
             cudaIpcCloseMemHandle(c->peer_map[w]);
@@ -903,10 +945,14 @@ void setup_peers(Ctx *c) {
         c->peer_local = nullptr;
         return;
     }
+    bool evs = cudaStreamCreateWithFlags(&c->gside, cudaStreamNonBlocking) == cudaSuccess;
+    for (int i = 0; evs && i < q8::PEER_IMAGES; ++i)
+        evs = cudaEventCreateWithFlags(&c->ev_prod[i], cudaEventDisableTiming) == cudaSuccess &&
+              cudaEventCreateWithFlags(&c->ev_gath[i], cudaEventDisableTiming) == cudaSuccess;
     cudaIpcMemHandle_t mine;
     void *d_handles = nullptr;
     std::vector<cudaIpcMemHandle_t> all(size_t(c->world));
-    bool ok = cudaMemset(c->peer_local, 0, q8::PEER_HDR) == cudaSuccess &&
+    bool ok = evs && cudaMemset(c->peer_local, 0, q8::PEER_HDR) == cudaSuccess &&
               cudaIpcGetMemHandle(&mine, c->peer_local) == cudaSuccess &&
               cudaMalloc(&d_handles, sizeof(cudaIpcMemHandle_t) * size_t(c->world)) == cudaSuccess;
     if (ok) {
