@@ -247,7 +247,8 @@ class Bench:
             rt.gemm(L["down"].data_ptr(), WL.D, WL.FF, xf, m, y[("down", m)].data_ptr())
         rt.gemm(self.head.data_ptr(), WL.VOCAB, WL.D, xd, m, y[("head", m)].data_ptr())
         rt.flush()  # with row shards: the step waits for its last gathers (side stream)
-        return (4 * len(self.w) + 1) * (2 if self.world > 1 and rt.peer_gather() else 1)
+        n = 4 * len(self.w) + 1
+        return n + ((n + 7) // 8 if self.world > 1 and rt.peer_gather() else 0)  # + a gather per 8 rounds
 
     def barrier(self):
         if self.world > 1:
@@ -838,6 +839,7 @@ def main() -> int:
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # stdout carries the one JSON line only
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local))
     b = Bench(args, rank, world)

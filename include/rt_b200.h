@@ -244,11 +244,11 @@ RTB_API void rt_b200_free(struct rt *R);
  * - A single product of <= 4 tokens (rt_gemv, rt_gemm, rt_gemm_silu) gathers y over NVLink
  *   without NCCL: the product kernel also stores every output into each peer's staging buffer
  *   (CUDA IPC mappings set up by rt_b200_shard), and a small gather kernel on a side stream of
- *   R's publishes the round, waits (bounded) for the peers', and copies their rows into y. R's
- *   stream goes on with the next product at once; it waits for a gather only where it must: a
- *   product whose x or y overlaps a y still being gathered, the product two rounds later (the
- *   staging buffers' reuse), and whatever else runs, pulls or pushes on R, or R synchronized or
- *   flushed. So in async mode y is whole, on R's stream, for what follows; blocking calls return
+ *   R's, once per 8 such products, publishes them, waits (bounded) for the peers', and copies
+ *   their rows into each product's y. R's stream goes on with the next product at once; it waits
+ *   for a gather only where it must: a product whose x or y overlaps a y still being gathered,
+ *   the product 16 rounds later (the staging buffers' reuse), and whatever else runs, pulls or
+ *   pushes on R, or R synchronized or flushed. So in async mode y is whole, on R's stream, for what follows; blocking calls return
  *   with y whole. A sequence captured into a CUDA graph must end with rt_b200_flush, which joins
  *   the side stream back into the capture.
  * - Queued rounds, t > 4 and the tensor-core path all-gather y with NCCL.

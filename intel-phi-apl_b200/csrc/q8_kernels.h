@@ -53,18 +53,21 @@ constexpr int ROUND_CTR_STRIDE = 32;
 //               image r % PEER_IMAGES.
 // Round r: the product kernel (R's stream) stores each output into its local y and into image r
 // of every peer (NVLink stores), and its last CTA advances the round count; nothing else, so the
-// next product follows at once. A small gather kernel on a side stream, after the product (an
-// event), publishes round r (a system-scope fence, then its flag in every peer's region), waits
-// (bounded) for every peer's flag of round r, copies the peers' rows from its own image r into
-// y, tells every peer it has read round r, and waits (bounded) until every peer has read round
-// r - 1. The product of round r + PEER_IMAGES - 1 waits (on R's stream, an event) for the gather
-// of round r, so it overwrites the image of round r - 1 only after every rank has read it: with
-// 8 images that gather is long done and the wait costs nothing (with 3, a product waited on the
-// gather two rounds back and measured 2.26 ms for the 2-GPU step). No product kernel ever waits
-// on another GPU: the cross-GPU waits are all in the gather kernels.
+// next product follows at once (with its programmatic early start). The rounds are gathered in
+// batches of up to GATHER_BATCH: after a batch's last product (an event), a small gather kernel on
+// a side stream publishes the batch (a system-scope fence, then its last round as its flag in
+// every peer's region), waits (bounded) for every peer's flag, copies the peers' rows of each
+// round from its own images into that round's y, tells every peer it has read the batch, and
+// waits (bounded) until every peer has read it too. A product whose image was last used by round
+// q waits (on R's stream, an event) for the gather of the batch holding q: with 16 images and
+// batches of 8 that batch is long done. Batches, not rounds: an event between two products costs
+// the second one its early start, ~3.6 us a round on 2 GPUs (products alone 1.41 ms a step, with
+// an event pair per round 1.88, with a gather per round 2.14). No product kernel ever waits on
+// another GPU: the cross-GPU waits are all in the gather kernels.
 constexpr int MAX_PEERS = 8;
 constexpr size_t PEER_HDR = 256;
-constexpr int PEER_IMAGES = 8;
+constexpr int PEER_IMAGES = 16;
+constexpr int GATHER_BATCH = 8;
 constexpr size_t PEER_STAGE_BYTES = size_t(8) << 20; // t * rows * 4 bytes at most (the head at t = 4: 2.4 MB)
 constexpr size_t PEER_REGION_BYTES = PEER_HDR + PEER_IMAGES * PEER_STAGE_BYTES;
 constexpr size_t PEER_FLAGS = 0, PEER_READS = 64, PEER_PCTAS = 128, PEER_GCTAS = 132, PEER_PRODUCED = 136,
@@ -142,9 +145,15 @@ cudaError_t launch_scale_outer(float *z, const float *s, float g, const float *a
                                long long k, cudaStream_t stream);
 cudaError_t preload_prims();
 
-// The gather of a peer-gathered product's round (the protocol above), on the side stream after
-// the product: y is the product's [t][rows_total] output, whose own rows are in place.
-cudaError_t launch_peer_gather(const PeerOut &po, float *y, int t, unsigned *err, cudaStream_t stream);
+// A batch of consecutive peer-gathered rounds (the protocol above), gathered on the side stream
+// after the batch's last product: round i's y is [t[i]][rows[i]], its own rows in place.
+struct GatherBatch {
+    float *y[GATHER_BATCH];
+    long long rows[GATHER_BATCH];
+    int t[GATHER_BATCH];
+    int n;
+};
+cudaError_t launch_peer_gather(const PeerOut &po, const GatherBatch &b, unsigned *err, cudaStream_t stream);
 
 // Launches the exact CUDA-core product over p.job[0..njobs) (all with the same m). Fills the
 // tile fields. grid_limit 0 = one CTA per SM. pdl: launch with programmatic stream serialization

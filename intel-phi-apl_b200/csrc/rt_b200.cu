@@ -97,14 +97,24 @@ struct Ctx {
     unsigned char *peer_local = nullptr;
     unsigned char *peer_map[q8::MAX_PEERS] = {};
     bool peer_ok = false;
-    // the row-sharded products' gathers (q8_kernels.h), on a side stream: the stream, the events of
-    // the latest rounds (slot = round % PEER_IMAGES: the product done on R's stream, the gather
-    // done on the side stream), the capture each gather event was recorded in (0: none), the
-    // rounds issued, and the y whose gathers R's stream has not waited for yet
+    // the row-sharded products' gathers (q8_kernels.h), in batches on a side stream: the stream;
+    // the open batch (rounds launched, their gather not yet); the batches launched whose gathers
+    // R's stream has not waited for (each with its last round, its events' slot: the batch's last
+    // product done on R's stream, its gather done on the side stream, and the capture it was
+    // recorded in, 0: none); the rounds issued and those R's stream has waited for; and the y of
+    // the rounds not waited for (the hazards of later products)
+    static constexpr int NSLOT = 4;
     cudaStream_t gside = nullptr;
-    cudaEvent_t ev_prod[q8::PEER_IMAGES] = {}, ev_gath[q8::PEER_IMAGES] = {};
-    unsigned long long ev_cap[q8::PEER_IMAGES] = {};
-    unsigned long long prounds = 0;
+    cudaEvent_t ev_prod[NSLOT] = {}, ev_gath[NSLOT] = {};
+    q8::GatherBatch open_b = {};
+    unsigned long long open_first = 0;
+    struct Issued {
+        unsigned long long last, cap;
+        int slot;
+    };
+    std::vector<Issued> issued;
+    int next_slot = 0;
+    unsigned long long prounds = 0, waited = 0;
     struct PendingY {
         const float *y;
         size_t bytes;
@@ -378,49 +388,85 @@ unsigned long long capture_id(cudaStream_t s) {
     return id;
 }
 
-// R's stream waits for the gather of round r (and with it every earlier one: the gathers run in
-// order). An event recorded in another capture context (or none, while capturing) cannot be waited
-// on: work from before a capture must have been synchronised, as graphs need anyway.
-bool wait_gather(Ctx *c, unsigned long long r, unsigned long long cap) {
-    const int slot = int(r % q8::PEER_IMAGES);
-    if (c->ev_cap[slot] != cap)
+// The open batch's gather, on the side stream after the batch's last product.
+bool issue_batch(Ctx *c) {
+    if (c->open_b.n == 0)
         return true;
-    return cuda_ok(c, cudaStreamWaitEvent(c->stream, c->ev_gath[slot], 0), "wait for a gather");
+    if (int(c->issued.size()) == Ctx::NSLOT) { // (every slot in use: the oldest batch first)
+        const Ctx::Issued o = c->issued.front();
+        if (o.cap == capture_id(c->stream) &&
+            !cuda_ok(c, cudaStreamWaitEvent(c->stream, c->ev_gath[o.slot], 0), "wait for a gather"))
+            return false;
+        c->issued.erase(c->issued.begin());
+        c->waited = o.last;
+    }
+    const int slot = c->next_slot;
+    c->next_slot = (c->next_slot + 1) % Ctx::NSLOT;
+    q8::PeerOut po = peer_out(c);
+    po.on = 1;
+    const q8::GatherBatch b = c->open_b;
+    c->open_b.n = 0;
+    if (!cuda_ok(c, cudaEventRecord(c->ev_prod[slot], c->stream), "gather: event") ||
+        !cuda_ok(c, cudaStreamWaitEvent(c->gside, c->ev_prod[slot], 0), "gather: stream wait") ||
+        !cuda_ok(c, q8::launch_peer_gather(po, b, c->d_err, c->gside), "peer gather") ||
+        !cuda_ok(c, cudaEventRecord(c->ev_gath[slot], c->gside), "gather: event"))
+        return false;
+    c->issued.push_back({c->open_first + b.n - 1, capture_id(c->stream), slot});
+    return true;
 }
 
-// R's stream waits for every gather issued: y is whole on R's stream from here on.
-bool flush_pending(Ctx *c) {
-    if (c->pending.empty())
+// R's stream waits until the rounds up to r are gathered (a batch's gather waits for the peers'
+// reads of the whole batch, and the batches run in order). An event recorded in another capture
+// context (or none, while capturing) cannot be waited on: work from before a capture must have
+// been synchronised, as graphs need anyway.
+bool wait_upto(Ctx *c, unsigned long long r) {
+    if (r <= c->waited)
         return true;
-    c->pending.clear();
-    return wait_gather(c, c->prounds, capture_id(c->stream));
+    if (r >= c->open_first && c->open_b.n && !issue_batch(c)) // r not launched for gathering yet
+        return false;
+    const unsigned long long cap = capture_id(c->stream);
+    while (!c->issued.empty() && c->waited < r) {
+        const Ctx::Issued o = c->issued.front();
+        c->issued.erase(c->issued.begin());
+        if (o.last >= r && o.cap == cap &&
+            !cuda_ok(c, cudaStreamWaitEvent(c->stream, c->ev_gath[o.slot], 0), "wait for a gather"))
+            return false;
+        c->waited = o.last;
+    }
+    std::vector<Ctx::PendingY> keep;
+    for (const Ctx::PendingY &q : c->pending)
+        if (q.round > c->waited)
+            keep.push_back(q);
+    c->pending.swap(keep);
+    return true;
+}
+
+// R's stream waits for every round's gather: y is whole on R's stream from here on.
+bool flush_pending(Ctx *c) {
+    if (c->prounds <= c->waited)
+        return true;
+    return issue_batch(c) && wait_upto(c, c->prounds);
 }
 
 // One row-sharded product: the product kernel on R's stream (its rows into y and into the peers'
-// staging), then its round's gather on the side stream. A product whose x overlaps a y still
-// being gathered, or whose y overlaps one other than its own (the same buffer and shape: its own
-// rows, which the gathers leave alone), waits for that gather first; the product of round r waits
-// for the gather of round r - PEER_IMAGES + 1 (the staging images' reuse, q8_kernels.h).
+// staging), its round added to the open batch (gathered on the side stream once the batch is
+// full, or when something needs it). A product whose x overlaps a y not yet gathered, or whose y
+// overlaps one other than its own (the same buffer and shape: its own rows, which the gathers
+// leave alone), waits for that gather first; so does one whose staging image was last used
+// PEER_IMAGES rounds ago (the images' reuse, q8_kernels.h).
 bool run_peer_gathered(Ctx *c, const Item &it) {
     long long lr, r0;
     shard_rows(c, it.rows, &lr, &r0);
-    const unsigned long long cap = capture_id(c->stream);
     const size_t xb = size_t(it.t * it.cols) * 4, yb = size_t(it.t * it.rows) * 4;
     unsigned long long need = 0;
     for (const Ctx::PendingY &q : c->pending)
         if (overlaps(it.x, xb, q.y, q.bytes) || (overlaps(it.y, yb, q.y, q.bytes) && !(it.y == q.y && yb == q.bytes)))
             need = q.round > need ? q.round : need;
     const unsigned long long r = ++c->prounds;
-    constexpr unsigned long long lag = q8::PEER_IMAGES - 1;
-    if (r > lag && r - lag > need)
-        need = r - lag;
-    if (need && !wait_gather(c, need, cap))
+    if (r > (unsigned long long)q8::PEER_IMAGES && r - q8::PEER_IMAGES > need)
+        need = r - q8::PEER_IMAGES;
+    if (need && !wait_upto(c, need))
         return false;
-    std::vector<Ctx::PendingY> keep; // the gathers not waited for yet
-    for (const Ctx::PendingY &q : c->pending)
-        if (q.round > need)
-            keep.push_back(q);
-    c->pending.swap(keep);
     q8::GemvParams p;
     memset(&p, 0, sizeof p);
     p.err = c->d_err;
@@ -442,16 +488,16 @@ bool run_peer_gathered(Ctx *c, const Item &it) {
     po.row0 = r0;
     po.rows_total = it.rows;
     po.on = 1;
-    const int slot = int(r % q8::PEER_IMAGES);
-    if (!cuda_ok(c, q8::launch_gemv(p, c->num_sms, 0, c->stream, c->overlap), "gemv launch") ||
-        !cuda_ok(c, cudaEventRecord(c->ev_prod[slot], c->stream), "gather: event") ||
-        !cuda_ok(c, cudaStreamWaitEvent(c->gside, c->ev_prod[slot], 0), "gather: stream wait") ||
-        !cuda_ok(c, q8::launch_peer_gather(po, it.y, int(it.t), c->d_err, c->gside), "peer gather") ||
-        !cuda_ok(c, cudaEventRecord(c->ev_gath[slot], c->gside), "gather: event"))
+    if (!cuda_ok(c, q8::launch_gemv(p, c->num_sms, 0, c->stream, c->overlap), "gemv launch"))
         return false;
-    c->ev_cap[slot] = cap;
+    if (c->open_b.n == 0)
+        c->open_first = r;
+    const int i = c->open_b.n++;
+    c->open_b.y[i] = it.y;
+    c->open_b.rows[i] = it.rows;
+    c->open_b.t[i] = int(it.t);
     c->pending.push_back({it.y, yb, r});
-    return true;
+    return c->open_b.n < q8::GATHER_BATCH || issue_batch(c);
 }
 
 // The CUDA-core job of tokens [k, k + 4) of a product (rows lr from r0 on this rank).
@@ -915,15 +961,17 @@ void drop_peers(Ctx *c) {
         cudaStreamSynchronize(c->gside);
         cudaStreamDestroy(c->gside);
         c->gside = nullptr;
-        for (int i = 0; i < q8::PEER_IMAGES; ++i) {
+        for (int i = 0; i < Ctx::NSLOT; ++i) {
             cudaEventDestroy(c->ev_prod[i]);
             cudaEventDestroy(c->ev_gath[i]);
             c->ev_prod[i] = c->ev_gath[i] = nullptr;
-            c->ev_cap[i] = 0;
         }
     }
     c->pending.clear();
-    c->prounds = 0;
+    c->issued.clear();
+    c->open_b.n = 0;
+    c->next_slot = 0;
+    c->prounds = c->waited = 0;
     for (int w = 0; w < q8::MAX_PEERS; ++w) {
         if (c->peer_map[w] && c->peer_map[w] != c->peer_local)
             cudaIpcCloseMemHandle(c->peer_map[w]);
@@ -946,7 +994,7 @@ void setup_peers(Ctx *c) {
         return;
     }
     bool evs = cudaStreamCreateWithFlags(&c->gside, cudaStreamNonBlocking) == cudaSuccess;
-    for (int i = 0; evs && i < q8::PEER_IMAGES; ++i)
+    for (int i = 0; evs && i < Ctx::NSLOT; ++i)
         evs = cudaEventCreateWithFlags(&c->ev_prod[i], cudaEventDisableTiming) == cudaSuccess &&
               cudaEventCreateWithFlags(&c->ev_gath[i], cudaEventDisableTiming) == cudaSuccess;
     cudaIpcMemHandle_t mine;

@@ -125,12 +125,13 @@ def _gpu_rank_main(rank: int, world: int, nid: bytes, out) -> None:
             yk = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
             rt.gemv(w.data_ptr(), rows, cols, x[k].data_ptr(), yk.data_ptr())
             rounds.append(yk)
-        # and async: each product finishes the previous one's gather in its own kernel; a chain
-        # whose x is the previous y (x overlaps the pending y: finished by its own kernel first)
+        # and async, 21 rounds: the gathers run in batches of 8 on a side stream, the staging
+        # images (16) come round again; then a product whose x is part of the last y (not
+        # gathered yet: it waits for that gather)
         rt.set_async(True)
-        for k in range(5):
+        for k in range(21):
             yk = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
-            rt.gemv(w.data_ptr(), rows, cols, x[7 + k].data_ptr(), yk.data_ptr())
+            rt.gemv(w.data_ptr(), rows, cols, x[(7 + k) % 16].data_ptr(), yk.data_ptr())
             rounds.append(yk)
         ya = torch.full((rows // 2,), float("nan"), dtype=torch.float32, device="cuda")
         rt.gemv(w.data_ptr(), rows // 2, cols, rounds[-1].data_ptr(), ya.data_ptr())  # x: part of the pending y
@@ -195,7 +196,7 @@ def test_row_shards_on_two_gpus(cuda, rtb, oracle):
         rms = np.sqrt(np.mean(want16 ** 2))
         assert np.max(np.abs(y16 - want16)) / rms < 2e-3
         for k, yk in enumerate(rounds):
-            xk = x[k] if k < 5 else x[7 + k - 5]
+            xk = x[k] if k < 5 else x[(7 + k - 5) % 16]
             assert np.array_equal(yk.view(np.uint32), oracle.gemv(q8, rows, cols, xk).view(np.uint32)), k
         # the product of rows // 2 rows over each rank's first rows // 4 shard rows, its x the first
         # cols entries of the last async round's y: every rank's product is the big matrix's rows
