@@ -360,7 +360,8 @@ bool flush_tc(Ctx *c, std::vector<q8::GemmJob> &jobs) {
 }
 
 // One row-sharded product of <= 4 tokens on CUDA cores, its y gathered through the peers' staging
-// images in the same launch (plus the receiving kernel), instead of an NCCL all-gather.
+// images (the product's stores, then a batched gather kernel on the side stream), instead of an
+// NCCL all-gather.
 bool peer_gatherable(const Ctx *c, const std::vector<Item> &items) {
     if (c->world < 2 || !c->peer_ok || items.size() != 1)
         return false;
