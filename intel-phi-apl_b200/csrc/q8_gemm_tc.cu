@@ -738,7 +738,8 @@ int choose_bn(const GemmJob *jobs, int n) {
 }
 
 // K parts per job, from a cost model of the launch measured on B200: units run in waves of one
-// per CTA slot (one or two per SM); a unit costs its 64-column stages (~0.26 us each at 16 tokens, ~0.55 us at 256) plus its
+// per CTA slot (one or two per SM); a unit costs its 64-column stages (~0.52 us each at 16 tokens: the two-CTA shape's
+// ring waits on weight latency; ~0.55 us at 256: the tensor pipe) plus its
 // pipeline fill (~2 us) and epilogue drain (~7 us for a 128 x 256 fp32 tile, in proportion for
 // fewer tokens); a split job adds the reduce pass (a launch plus its partial planes read once and
 // y written, ~5 TB/s). The model picks the number of parts (1..16, each at least 4 stages long)
@@ -751,7 +752,7 @@ void choose_splits(const GemmJob *jobs, int n, int bn, int num_sms, bool allow, 
     };
     int best = 1;
     if (allow) {
-        const double ts = 0.26 + 0.29 * bn / 256.0, fill = 2.0 + 7.0 * bn / 256.0;
+        const double ts = 0.52 + 0.03 * bn / 256.0, fill = 2.0 + 7.0 * bn / 256.0;
         double best_t = 0.0;
         for (int k = 1; k <= 16; ++k) {
             long long units = 0;
