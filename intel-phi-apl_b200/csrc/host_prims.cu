@@ -25,40 +25,67 @@ __device__ __forceinline__ float lanes_sum(float l) {
     return u + __shfl_xor_sync(0xffffffffu, u, 1);           // their sum
 }
 
+// Output o of a launch: ip21 computes z[o] (row o of a against b's row o / per_h); ip21_kv runs
+// its outputs history-row-major with the query heads in kv-head order within a row, so the heads
+// that share a kv head read the same row at the same time (one load for the group).
+struct DotOut {
+    long long hh, i;
+};
 template <bool KV>
-__global__ void __launch_bounds__(256) dot8_kernel(float *z, const float *a, const float *b, long long n_out, long long per_h,
-                                                   long long c, long long n1, PrimHeads heads) {
+__device__ __forceinline__ DotOut dot_out(long long o, long long per_h, long long h, const PrimHeads &heads) {
+    if (KV) {
+        const long long i = o / h;
+        return {heads.ord[o - i * h], i};
+    }
+    const long long hh = o / per_h;
+    return {hh, o - hh * per_h};
+}
+
+// Thread 8*g + j holds lane j of output g. 16 steps' loads are issued before their fmas.
+template <bool KV>
+__global__ void __launch_bounds__(256, 4) dot8_kernel(float *z, const float *a, const float *b, long long n_out, long long per_h,
+                                                   long long c, long long n1, long long h, PrimHeads heads) {
     const long long g = (long long)blockIdx.x * (blockDim.x / 8) + threadIdx.x / 8;
     const int j = threadIdx.x % 8;
     const bool live = g < n_out;
-    const long long o = live ? g : 0;
-    const long long hh = o / per_h, i = o - hh * per_h;
+    const DotOut d = dot_out<KV>(live ? g : 0, per_h, h, heads);
     // ip21: row o of a, b's row hh; ip21_kv: history row i of kv head l[hh], b's row hh
-    const float *row = KV ? a + (i * n1 + heads.l[hh]) * c : a + o * c;
-    const float *v = b + hh * c;
+    const float *row = KV ? a + (d.i * n1 + heads.l[d.hh]) * c : a + (d.hh * per_h + d.i) * c;
+    const float *v = b + d.hh * c;
     float acc = 0.0f;
     if (live) {
         long long k = j;
-#pragma unroll 4
+        for (; k + 8 * 15 < c; k += 8 * 16) {
+            float r[16], q[16];
+#pragma unroll
+            for (int s = 0; s < 16; ++s) {
+                r[s] = __ldg(row + k + 8 * s);
+                q[s] = __ldg(v + k + 8 * s);
+            }
+#pragma unroll
+            for (int s = 0; s < 16; ++s)
+                acc = __fmaf_rn(r[s], q[s], acc);
+        }
         for (; k < c; k += 8)
             acc = __fmaf_rn(__ldg(row + k), __ldg(v + k), acc);
     }
     const float r = lanes_sum(acc);
     if (live && j == 0)
-        z[o] = r;
+        z[d.hh * per_h + d.i] = r;
 }
 
 // One thread per output, the 8 lanes in registers, 16-byte loads: for calls with outputs enough
 // to fill the GPU this way (more loads in flight per thread than one lane per thread gives).
 template <bool KV>
 __global__ void __launch_bounds__(256) dot8_wide_kernel(float *z, const float *a, const float *b, long long n_out,
-                                                        long long per_h, long long c, long long n1, PrimHeads heads) {
+                                                        long long per_h, long long c, long long n1, long long h,
+                                                        PrimHeads heads) {
     const long long o = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (o >= n_out)
         return;
-    const long long hh = o / per_h, i = o - hh * per_h;
-    const float4 *row = reinterpret_cast<const float4 *>(KV ? a + (i * n1 + heads.l[hh]) * c : a + o * c);
-    const float4 *v = reinterpret_cast<const float4 *>(b + hh * c);
+    const DotOut d = dot_out<KV>(o, per_h, h, heads);
+    const float4 *row = reinterpret_cast<const float4 *>(KV ? a + (d.i * n1 + heads.l[d.hh]) * c : a + o * c);
+    const float4 *v = reinterpret_cast<const float4 *>(b + d.hh * c);
     float l[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
     for (long long k = 0; k < c / 4; k += 2) {
@@ -72,7 +99,8 @@ __global__ void __launch_bounds__(256) dot8_wide_kernel(float *z, const float *a
         l[6] = __fmaf_rn(r1.z, v1.z, l[6]);
         l[7] = __fmaf_rn(r1.w, v1.w, l[7]);
     }
-    z[o] = __fadd_rn(__fadd_rn(__fadd_rn(l[0], l[4]), __fadd_rn(l[2], l[6])), __fadd_rn(__fadd_rn(l[1], l[5]), __fadd_rn(l[3], l[7])));
+    z[d.hh * per_h + d.i] = __fadd_rn(__fadd_rn(__fadd_rn(l[0], l[4]), __fadd_rn(l[2], l[6])),
+                                      __fadd_rn(__fadd_rn(l[1], l[5]), __fadd_rn(l[3], l[7])));
 }
 
 // Outputs from which one thread per output fills the GPU (148 SMs x 256 threads x 2). Below it
@@ -81,60 +109,81 @@ __global__ void __launch_bounds__(256) dot8_wide_kernel(float *z, const float *a
 constexpr long long DOT_WIDE_MIN = 148ll * 256 * 2;
 
 // ---------------------------------------------------------------- ip12_kv
-// A CTA: one kv head's group of query heads (one warp each) and a 32-column slice of c. The
-// slice of every history row, [t][32] floats, streams through a ring of SLOTS stages of ROWS rows
-// (cp.async, 16 bytes per thread and copy); each thread keeps z[h][k] for its head and column as
-// one fma chain over the rows in order.
-// 768 history rows in flight (6 stages of 128): at one row every few cycles per chain, enough to
-// cover DRAM latency (4 stages of 64 rows measured 56 us on a 4096-row history, 6 of 128: below).
-constexpr int IP12_ROWS = 128, IP12_SLOTS = 6, IP12_K = 32;
-__host__ __device__ constexpr size_t ip12_smem(int nh) { return size_t(IP12_SLOTS) * IP12_ROWS * (IP12_K + nh) * 4; }
+// A CTA: one kv head's group of query heads and a W-column slice of c (W = 32 where c allows,
+// else 8); thread W*hi + j keeps z[h][k] for head hi of the group and column j of the slice as
+// one fma chain over the history rows in order. The slice of every row (4W bytes) and the
+// group's weights for the same rows stream through a ring of SLOTS stages of ROWS rows
+// (cp.async). A warp runs alone on its scheduler and its chain takes one dependent fma per row,
+// so the rest of a row's work has to fit in the fma's latency: the operands of the next 16 rows
+// are loaded while the current 16 chain (two register sets in turn, nothing copied between
+// them), four rows' weights come in one 16-byte load (weight rows padded by 16 bytes so that four
+// heads' reads fall into different banks), and a copy's addresses are formed once per launch.
+constexpr int IP12_ROWS = 128, IP12_SLOTS = 8, IP12_WS = IP12_ROWS + 4;
+__host__ __device__ constexpr size_t ip12_smem(int w, int nh) {
+    return size_t(IP12_SLOTS) * (size_t(IP12_ROWS) * w + size_t(nh) * IP12_WS) * 4;
+}
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool ok) {
     const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
-    const int n = ok ? 16 : 0; // (a zero-size copy fills zeros: rows past t, columns past c)
+    const int n = ok ? 16 : 0; // (a zero-size copy fills zeros: rows past t)
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n) : "memory");
 }
+__device__ __forceinline__ void cp_async4(void *smem, const void *gmem, bool ok) {
+    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    const int n = ok ? 4 : 0;
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(s), "l"(gmem), "r"(n) : "memory");
+}
 
-__global__ void __launch_bounds__(32 * MAX_PRIM_GROUP) ip12_kv_kernel(float *z, const float *a, const float *kv,
-                                                                      long long n1, long long c, long long t,
-                                                                      PrimGroups groups) {
-    // dynamic: [SLOTS][ROWS][K] of history, then [SLOTS][nmax][ROWS] of a (nmax: the launch's
-    // largest group, blockDim.x / 32)
+template <int W>
+__global__ void __launch_bounds__(W * MAX_PRIM_GROUP, 1) ip12_kv_kernel(float *z, const float *a, const float *kv,
+                                                                        long long n1, long long c, long long t,
+                                                                        PrimGroups groups) {
+    // dynamic: [SLOTS][ROWS][W] of history, then [SLOTS][nmax][WS] of a (nmax = blockDim.x / W,
+    // at least the launch's largest group)
     extern __shared__ __align__(16) float dyn[];
-    float(*ring)[IP12_ROWS][IP12_K] = reinterpret_cast<float(*)[IP12_ROWS][IP12_K]>(dyn);
-    const int nmax = blockDim.x / 32;
-    float *wbase = dyn + size_t(IP12_SLOTS) * IP12_ROWS * IP12_K;
-    const int gi = blockIdx.y, warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    float(*ring)[IP12_ROWS][W] = reinterpret_cast<float(*)[IP12_ROWS][W]>(dyn);
+    const int nmax = blockDim.x / W;
+    float *wbase = dyn + size_t(IP12_SLOTS) * IP12_ROWS * W;
+    const int gi = blockIdx.y, hi = threadIdx.x / W, j = threadIdx.x % W;
     const int first = groups.first[gi], nh = groups.first[gi + 1] - first;
-    const long long kvh = groups.kv[gi];
-    const long long k0 = (long long)blockIdx.x * IP12_K;
-    // stage s: rows [s*ROWS, +ROWS) of the slice (8 copies of 16 bytes per row) and the same
-    // rows of a for each head of the group (16 copies of 16 bytes per head; a's rows are 4-byte
-    // aligned only, so a is copied 4 bytes at a time unless t is a multiple of 4 and a 16-aligned)
+    const long long k0 = (long long)blockIdx.x * W; // c % W == 0: the slice is whole
+    const long long rstride = n1 * c;               // floats from one history row to the next
+    // this thread's history copies, the same in every stage: 16 bytes at column 4 * (tid % (W/4))
+    // of rows tid / (W/4), + blockDim / (W/4), ... (blockDim is a multiple of 32, so of W/4); the
+    // source walks down the history, one stage of rows per stage. Of a: either 16-byte pieces
+    // (t % 4 == 0 and a 16-aligned) or single floats (a's rows are only 4-byte aligned otherwise).
+    const int row_step = blockDim.x / (W / 4), my_row = threadIdx.x / (W / 4), my_col = 4 * (threadIdx.x % (W / 4));
+    const float *kv_next = kv + groups.kv[gi] * c + k0 + my_row * rstride + my_col; // stage 0's first copy
+    const long long src_step = row_step * rstride;
     const bool a16 = (t % 4) == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0;
     auto issue = [&](long long stage) {
-        float(*slot)[IP12_K] = ring[stage % IP12_SLOTS];
-        for (int e = threadIdx.x; e < IP12_ROWS * 8; e += blockDim.x) {
-            const int rr = e / 8, q = e % 8;
-            const long long row = stage * IP12_ROWS + rr, col = k0 + 4 * q;
-            const bool ok = row < t && col < c;
-            cp_async16(&slot[rr][4 * q], ok ? kv + (row * n1 + kvh) * c + col : kv, ok);
-        }
-        float(*ws)[IP12_ROWS] = reinterpret_cast<float(*)[IP12_ROWS]>(wbase + size_t(stage % IP12_SLOTS) * nmax * IP12_ROWS);
+        const int sl = int(stage % IP12_SLOTS);
         const long long r0 = stage * IP12_ROWS;
+        float *dst = &ring[sl][my_row][my_col];
+        const float *src = kv_next;
+        long long row = r0 + my_row;
+        for (int rr = my_row; rr < IP12_ROWS; rr += row_step) {
+            const bool ok = row < t;
+            cp_async16(dst, ok ? src : kv, ok);
+            dst += row_step * W;
+            src += src_step;
+            row += row_step;
+        }
+        kv_next += IP12_ROWS * rstride;
+        float *ws = wbase + size_t(sl) * nmax * IP12_WS;
         if (a16) {
             for (int e = threadIdx.x; e < nh * (IP12_ROWS / 4); e += blockDim.x) {
-                const int hi = e / (IP12_ROWS / 4), q = e % (IP12_ROWS / 4);
+                const int h2 = e / (IP12_ROWS / 4), q = e % (IP12_ROWS / 4);
                 const long long row = r0 + 4 * q;
                 const bool ok = row < t;
-                cp_async16(&ws[hi][4 * q], ok ? a + (long long)groups.head[first + hi] * t + row : a, ok);
+                cp_async16(ws + h2 * IP12_WS + 4 * q, ok ? a + (long long)groups.head[first + h2] * t + row : a, ok);
             }
         } else {
             for (int e = threadIdx.x; e < nh * IP12_ROWS; e += blockDim.x) {
-                const int hi = e / IP12_ROWS, q = e % IP12_ROWS;
+                const int h2 = e / IP12_ROWS, q = e % IP12_ROWS;
                 const long long row = r0 + q;
-                ws[hi][q] = row < t ? __ldg(a + (long long)groups.head[first + hi] * t + row) : 0.0f;
+                const bool ok = row < t;
+                cp_async4(ws + h2 * IP12_WS + q, ok ? a + (long long)groups.head[first + h2] * t + row : a, ok);
             }
         }
     };
@@ -144,8 +193,7 @@ __global__ void __launch_bounds__(32 * MAX_PRIM_GROUP) ip12_kv_kernel(float *z, 
             issue(s);
         asm volatile("cp.async.commit_group;" ::: "memory");
     }
-    const bool mine = warp < nh && k0 + lane < c;
-    const long long hh = warp < nh ? groups.head[first + warp] : 0;
+    const bool mine = hi < nh;
     float acc = 0.0f;
     for (long long st = 0; st < nstages; ++st) {
         asm volatile("cp.async.wait_group %0;" ::"n"(IP12_SLOTS - 2) : "memory");
@@ -153,30 +201,50 @@ __global__ void __launch_bounds__(32 * MAX_PRIM_GROUP) ip12_kv_kernel(float *z, 
         if (st + IP12_SLOTS - 1 < nstages)
             issue(st + IP12_SLOTS - 1);
         asm volatile("cp.async.commit_group;" ::: "memory");
-        const float(*slot)[IP12_K] = ring[st % IP12_SLOTS];
-        const float *ws = wbase + (size_t(st % IP12_SLOTS) * nmax + (warp < nh ? warp : 0)) * IP12_ROWS;
-        const long long r0 = st * IP12_ROWS;
-        const int nr = int(t - r0 < IP12_ROWS ? t - r0 : IP12_ROWS);
-        if (mine) {
-            int rr = 0;
-            for (; rr + 16 <= nr; rr += 16) { // the operands of 16 steps first, then the chain
-                float w[16], x[16];
+        const int sl = int(st % IP12_SLOTS);
+        const float(*slot)[W] = ring[sl];
+        const float *ws = wbase + (size_t(sl) * nmax + (mine ? hi : 0)) * IP12_WS;
+        const int nr = int(t - st * IP12_ROWS < IP12_ROWS ? t - st * IP12_ROWS : IP12_ROWS);
+        if (!mine)
+            continue;
+        if (nr == IP12_ROWS) {
+            const float4 *w4 = reinterpret_cast<const float4 *>(ws);
+            float4 wa[4], wb[4];
+            float xa[16], xb[16];
+            auto load = [&](float4 *w, float *x, int g) {
 #pragma unroll
-                for (int q = 0; q < 16; ++q) {
-                    w[q] = ws[rr + q];
-                    x[q] = slot[rr + q][lane];
-                }
+                for (int q = 0; q < 4; ++q)
+                    w[q] = w4[4 * g + q];
 #pragma unroll
                 for (int q = 0; q < 16; ++q)
-                    acc = __fmaf_rn(w[q], x[q], acc);
+                    x[q] = slot[16 * g + q][j];
+            };
+            auto chain = [&](const float4 *w, const float *x) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    acc = __fmaf_rn(w[q].x, x[4 * q + 0], acc);
+                    acc = __fmaf_rn(w[q].y, x[4 * q + 1], acc);
+                    acc = __fmaf_rn(w[q].z, x[4 * q + 2], acc);
+                    acc = __fmaf_rn(w[q].w, x[4 * q + 3], acc);
+                }
+            };
+            load(wa, xa, 0);
+#pragma unroll
+            for (int g = 0; g < IP12_ROWS / 16; g += 2) {
+                load(wb, xb, g + 1);
+                chain(wa, xa);
+                if (g + 2 < IP12_ROWS / 16)
+                    load(wa, xa, g + 2);
+                chain(wb, xb);
             }
-            for (; rr < nr; ++rr)
-                acc = __fmaf_rn(ws[rr], slot[rr][lane], acc);
+        } else {
+            for (int rr = 0; rr < nr; ++rr)
+                acc = __fmaf_rn(ws[rr], slot[rr][j], acc);
         }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     if (mine)
-        z[hh * c + k0 + lane] = acc;
+        z[(long long)groups.head[first + hi] * c + k0 + j] = acc;
 }
 
 // ---------------------------------------------------------------- scale_outer
@@ -203,9 +271,9 @@ cudaError_t launch_ip21(float *z, const float *a, long long h, long long r, long
     const long long n = h * r;
     PrimHeads none = {};
     if (n >= DOT_WIDE_MIN && aligned16(a) && aligned16(b))
-        dot8_wide_kernel<false><<<grid_of(n, 256), 256, 0, stream>>>(z, a, b, n, r, c, 0, none);
+        dot8_wide_kernel<false><<<grid_of(n, 256), 256, 0, stream>>>(z, a, b, n, r, c, 0, h, none);
     else
-        dot8_kernel<false><<<grid_of(n * 8, 256), 256, 0, stream>>>(z, a, b, n, r, c, 0, none);
+        dot8_kernel<false><<<grid_of(n * 8, 256), 256, 0, stream>>>(z, a, b, n, r, c, 0, h, none);
     return cudaGetLastError();
 }
 
@@ -213,23 +281,32 @@ cudaError_t launch_ip21_kv(float *z, const float *kv, long long n1, long long c,
                            long long t, const float *b, cudaStream_t stream) {
     const long long n = h * t;
     if (n >= DOT_WIDE_MIN && aligned16(kv) && aligned16(b))
-        dot8_wide_kernel<true><<<grid_of(n, 256), 256, 0, stream>>>(z, kv, b, n, t, c, n1, heads);
+        dot8_wide_kernel<true><<<grid_of(n, 256), 256, 0, stream>>>(z, kv, b, n, t, c, n1, h, heads);
     else
-        dot8_kernel<true><<<grid_of(n * 8, 256), 256, 0, stream>>>(z, kv, b, n, t, c, n1, heads);
+        dot8_kernel<true><<<grid_of(n * 8, 256), 256, 0, stream>>>(z, kv, b, n, t, c, n1, h, heads);
     return cudaGetLastError();
 }
 
 cudaError_t launch_ip12_kv(float *z, const float *a, const float *kv, long long n1, long long c, const PrimGroups &groups,
                            long long t, cudaStream_t stream) {
-    if (groups.n < 1 || groups.n > MAX_PRIM_HEADS)
+    if (groups.n < 1 || groups.n > MAX_PRIM_HEADS || c < 8 || c % 8)
         return cudaErrorInvalidValue;
     int most = 0;
     for (int g = 0; g < groups.n; ++g)
         most = groups.first[g + 1] - groups.first[g] > most ? groups.first[g + 1] - groups.first[g] : most;
     if (most < 1 || most > MAX_PRIM_GROUP)
         return cudaErrorInvalidValue;
-    const dim3 grid(unsigned((c + IP12_K - 1) / IP12_K), unsigned(groups.n));
-    ip12_kv_kernel<<<grid, 32 * most, ip12_smem(most), stream>>>(z, a, kv, n1, c, t, groups);
+    // 32-column slices (128-byte history pieces) where c allows: measured faster than 8 on the
+    // attention shapes, with four warps of one head each per CTA
+    if (c % 32 == 0) {
+        const int threads = 32 * most;
+        ip12_kv_kernel<32><<<dim3(unsigned(c / 32), unsigned(groups.n)), threads, ip12_smem(32, most), stream>>>(
+            z, a, kv, n1, c, t, groups);
+    } else {
+        const int threads = (8 * most + 31) / 32 * 32;
+        ip12_kv_kernel<8><<<dim3(unsigned(c / 8), unsigned(groups.n)), threads, ip12_smem(8, threads / 8), stream>>>(
+            z, a, kv, n1, c, t, groups);
+    }
     return cudaGetLastError();
 }
 
@@ -249,8 +326,10 @@ cudaError_t preload_prims() {
         (e = cudaFuncGetAttributes(&at, dot8_kernel<true>)) != cudaSuccess ||
         (e = cudaFuncGetAttributes(&at, dot8_wide_kernel<false>)) != cudaSuccess ||
         (e = cudaFuncGetAttributes(&at, dot8_wide_kernel<true>)) != cudaSuccess ||
-        (e = cudaFuncSetAttribute(ip12_kv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  int(ip12_smem(MAX_PRIM_GROUP)))) != cudaSuccess)
+        (e = cudaFuncSetAttribute(ip12_kv_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  int(ip12_smem(32, MAX_PRIM_GROUP)))) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(ip12_kv_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  int(ip12_smem(8, MAX_PRIM_GROUP)))) != cudaSuccess)
         return e;
     return cudaFuncGetAttributes(&at, scale_outer_kernel);
 }

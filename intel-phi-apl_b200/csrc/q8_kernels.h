@@ -123,9 +123,10 @@ cudaError_t launch_wait_probe(const unsigned *ctr, unsigned *err, cudaStream_t s
 
 // ---- the host-half primitives beside the products (host_prims.cu)
 constexpr int MAX_PRIM_HEADS = 128; // query heads of one call
-constexpr int MAX_PRIM_GROUP = 16;  // query heads of one kv head in one ip12_kv CTA (a warp each)
+constexpr int MAX_PRIM_GROUP = 16;  // query heads of one kv head in one ip12_kv CTA (8 threads each)
 struct PrimHeads {
     long long l[MAX_PRIM_HEADS]; // the kv head of each query head
+    int ord[MAX_PRIM_HEADS];     // the query heads sorted by kv head (stable): neighbours share rows
 };
 // The query heads grouped by kv head, each group <= MAX_PRIM_GROUP heads: group g is heads
 // head[first[g] .. first[g+1]) of kv head kv[g].

@@ -7,6 +7,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <atomic>
 #include <bitset>
 #include <cstdarg>
@@ -1338,8 +1339,12 @@ void rt_ip21_kv(struct rt *R, float *z, const float *kv, long n1, long c_cols, c
     }
     q8::PrimHeads heads;
     memset(&heads, 0, sizeof heads);
-    for (long i = 0; i < h; ++i)
+    for (long i = 0; i < h; ++i) {
         heads.l[i] = l[i];
+        heads.ord[i] = int(i);
+    }
+    // the heads that share a kv head side by side: their threads then read each row together
+    std::stable_sort(heads.ord, heads.ord + h, [&](int x, int y) { return l[x] < l[y]; });
     c->synced = false;
     if (cuda_ok(c, q8::launch_ip21_kv(z, kv, n1, c_cols, heads, h, t, b, c->stream), "rt_ip21_kv"))
         finish(c);

@@ -29,6 +29,9 @@ SHAPES = [
     (3, 3, 40, 0, 2, 4, 24),            # an empty history
     (64, 8, 128, 2048, 300, 64, 8),     # one thread per output for the dot products (131072 of them)
     (7, 7, 16, 4098, 3, 2, 8),          # t % 4 != 0: the weights' rows are copied 4 bytes at a time
+    (6, 8, 64, 300, 5, 7, 9),           # kv heads 1 and 6 never read
+    (64, 128, 8, 1200, 2, 3, 8),        # half the kv heads read, 76800 outputs
+    (4, 4, 8192, 3, 1, 2, 8),           # 128 KB history rows, 256 ip12_kv slices of 32 columns
 ]
 
 
