@@ -550,7 +550,7 @@ __global__ void __launch_bounds__(TcShape<CPS>::NT, CPS) gemm_tc_kernel(const __
 // largest |x| of the token gives s_t (|x| * 2^s_t <= 2^15 at that entry; s_t <= 126), then
 // xh = fp16(x * 2^s_t) and tokf[t] = 2^-s_t. Blocks from t: the matrix rows (W's rows, then a
 // pair's up rows), a half-warp per row: the row's largest scale gives r_o (row_exponent) into rexp.
-constexpr int PREP_THREADS = 256;
+constexpr int PREP_THREADS = 256, PREP_HELD = 16;
 
 // RPB rows per half-warp and batch: 8 where the matrix has rows enough to give every SM a block
 // of 16-row warps, else 1 (a few deep blocks on a small matrix leave most SMs idle).
@@ -568,9 +568,27 @@ __global__ void __launch_bounds__(PREP_THREADS) tc_prep_kernel(const float *x, l
         __shared__ float part[PREP_THREADS / 32];
         __shared__ int s_sh;
         const float *xt = x + (long long)blockIdx.x * ldx;
+        __half *ht = xh + (long long)blockIdx.x * cols;
+        // 16-byte pieces where the row allows, the whole row held in registers between the scan
+        // and the conversion (rows of up to PREP_HELD * 4 * PREP_THREADS columns)
+        const bool vec = cols % 4 == 0 && (reinterpret_cast<uintptr_t>(xt) & 15) == 0 &&
+                         cols <= PREP_HELD * 4 * PREP_THREADS;
+        float4 v[PREP_HELD];
         float amax = 0.0f;
-        for (int c = threadIdx.x; c < cols; c += PREP_THREADS)
-            amax = fmaxf(amax, fabsf(xt[c]));
+        if (vec) {
+            const float4 *x4 = reinterpret_cast<const float4 *>(xt);
+#pragma unroll
+            for (int q = 0; q < PREP_HELD; ++q) {
+                const int c = threadIdx.x + q * PREP_THREADS;
+                v[q] = c < cols / 4 ? __ldg(x4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int q = 0; q < PREP_HELD; ++q)
+                amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[q].x), fabsf(v[q].y)), fmaxf(fabsf(v[q].z), fabsf(v[q].w))));
+        } else {
+            for (int c = threadIdx.x; c < cols; c += PREP_THREADS)
+                amax = fmaxf(amax, fabsf(xt[c]));
+        }
         for (int o = 16; o; o >>= 1)
             amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         if (threadIdx.x % 32 == 0)
@@ -592,9 +610,23 @@ __global__ void __launch_bounds__(PREP_THREADS) tc_prep_kernel(const float *x, l
         }
         __syncthreads();
         const float f = pow2i(s_sh);
-        __half *ht = xh + (long long)blockIdx.x * cols;
-        for (int c = threadIdx.x; c < cols; c += PREP_THREADS)
-            ht[c] = __float2half_rn(xt[c] * f);
+        if (vec) {
+#pragma unroll
+            for (int q = 0; q < PREP_HELD; ++q) {
+                const int c = threadIdx.x + q * PREP_THREADS;
+                if (c < cols / 4) {
+                    const __half2 lo = __halves2half2(__float2half_rn(v[q].x * f), __float2half_rn(v[q].y * f));
+                    const __half2 hi = __halves2half2(__float2half_rn(v[q].z * f), __float2half_rn(v[q].w * f));
+                    uint2 u;
+                    u.x = *reinterpret_cast<const unsigned *>(&lo);
+                    u.y = *reinterpret_cast<const unsigned *>(&hi);
+                    *reinterpret_cast<uint2 *>(ht + 4 * c) = u; // (cols % 4 == 0: 8-byte aligned)
+                }
+            }
+        } else {
+            for (int c = threadIdx.x; c < cols; c += PREP_THREADS)
+                ht[c] = __float2half_rn(xt[c] * f);
+        }
         return;
     }
     // The row exponents: a half-warp per row, 16-byte chunks of the row's scales, RPB rows per
@@ -640,25 +672,81 @@ __global__ void __launch_bounds__(PREP_THREADS) tc_prep_kernel(const float *x, l
 }
 
 // y[tok][row] = sum over K parts k (in order) of part[k][tok][row]; for a SwiGLU pair the gate
-// planes come first, then the up planes, and y = silu(gate sum) * (up sum).
-__global__ void splitk_reduce_kernel(const float *part, int ks, int pair, long long rows, int t, float *y,
-                                     long long ldy) {
+// planes come first, then the up planes, and y = silu(gate sum) * (up sum). Tokens on the grid's
+// y dimension; four rows per thread in 16-byte loads and stores where rows and ldy are multiples
+// of 4 and y is 16-aligned (vec), else one row per thread.
+__device__ __forceinline__ float reduce_one(const float *p, long long plane, int ks, int pair) {
+    float g = p[0];
+#pragma unroll 1
+    for (int k = 1; k < ks; ++k)
+        g += p[k * plane];
+    if (pair) {
+        float u = p[ks * plane];
+#pragma unroll 1
+        for (int k = 1; k < ks; ++k)
+            u += p[(ks + k) * plane];
+        g = g / (1.0f + expf(-g)) * u;
+    }
+    return g;
+}
+
+// Parts [0, ks) of four rows added in K order; all loads of a batch of up to B parts are issued
+// before their sums.
+template <int B>
+__device__ __forceinline__ float4 sum_parts(const float4 *p, long long pl4, int ks) {
+    float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k0 = 0; k0 < ks; k0 += B) {
+        float4 q[B];
+#pragma unroll
+        for (int k = 0; k < B; ++k)
+            if (k0 + k < ks)
+                q[k] = p[(k0 + k) * pl4];
+#pragma unroll
+        for (int k = 0; k < B; ++k)
+            if (k0 + k < ks) {
+                if (k0 + k == 0) {
+                    g = q[0];
+                } else {
+                    g.x += q[k].x;
+                    g.y += q[k].y;
+                    g.z += q[k].z;
+                    g.w += q[k].w;
+                }
+            }
+    }
+    return g;
+}
+
+template <bool PAIR>
+__global__ void __launch_bounds__(128, PAIR ? 4 : 8) splitk_reduce_kernel(const float *part, int ks, long long rows, int t,
+                                                                          float *y, long long ldy, int vec) {
+    const int pair = PAIR;
     if (threadIdx.x == 0)
         grid_launch_dependents();
     grid_wait(); // the product's partial planes
-    const long long n = (long long)t * rows, plane = n;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-        const long long tok = i / rows, row = i - tok * rows;
-        float g = part[i];
-        for (int k = 1; k < ks; ++k)
-            g += part[k * plane + i];
-        if (pair) {
-            float u = part[ks * plane + i];
-            for (int k = 1; k < ks; ++k)
-                u += part[(ks + k) * plane + i];
-            g = g / (1.0f + expf(-g)) * u;
+    const long long plane = (long long)t * rows;
+    for (long long tok = blockIdx.y; tok < t; tok += gridDim.y) {
+        const float *pt = part + tok * rows;
+        float *yt = y + tok * ldy;
+        if (vec) {
+            for (long long r4 = (long long)blockIdx.x * blockDim.x + threadIdx.x; r4 < rows / 4;
+                 r4 += (long long)gridDim.x * blockDim.x) {
+                const float4 *p4 = reinterpret_cast<const float4 *>(pt) + r4;
+                const long long pl4 = plane / 4;
+                float4 g = sum_parts<PAIR ? 8 : 4>(p4, pl4, ks);
+                if (pair) {
+                    const float4 u = sum_parts<8>(p4 + ks * pl4, pl4, ks);
+                    g.x = g.x / (1.0f + expf(-g.x)) * u.x;
+                    g.y = g.y / (1.0f + expf(-g.y)) * u.y;
+                    g.z = g.z / (1.0f + expf(-g.z)) * u.z;
+                    g.w = g.w / (1.0f + expf(-g.w)) * u.w;
+                }
+                reinterpret_cast<float4 *>(yt)[r4] = g;
+            }
+        } else {
+            for (long long r = (long long)blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += (long long)gridDim.x * blockDim.x)
+                yt[r] = reduce_one(pt + r, plane, ks, pair);
         }
-        y[tok * ldy + row] = g;
     }
 }
 
@@ -676,6 +764,22 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, 
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// The reduce pass on a 2-D grid (row groups x tokens), programmatic when pdl.
+cudaError_t launch_reduce(dim3 grid, cudaStream_t stream, bool pdl, const float *part, int ks, int pair, long long rows,
+                          int t, float *y, long long ldy, int vec) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(128);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return pair ? cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<true>, part, ks, rows, t, y, ldy, vec)
+                : cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<false>, part, ks, rows, t, y, ldy, vec);
 }
 
 // ---------------------------------------------------------------- host: tensor maps
@@ -839,7 +943,9 @@ cudaError_t preload_gemm_tc() {
     if ((e = cudaFuncGetAttributes(&a, tc_prep_kernel<1>)) != cudaSuccess ||
         (e = cudaFuncGetAttributes(&a, tc_prep_kernel<8>)) != cudaSuccess)
         return e;
-    return cudaFuncGetAttributes(&a, splitk_reduce_kernel);
+    if ((e = cudaFuncGetAttributes(&a, splitk_reduce_kernel<true>)) != cudaSuccess)
+        return e;
+    return cudaFuncGetAttributes(&a, splitk_reduce_kernel<false>);
 }
 
 size_t gemm_tc_scratch_bytes(const GemmJob *jobs, int n, int num_sms, bool split_k) {
@@ -946,11 +1052,13 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
         const TcJobDev &J = p.job[j];
         if (J.ks < 2)
             continue;
-        const long long outs = (long long)J.t * J.rows;
-        int g = int((outs + 255) / 256);
-        g = g > 8192 ? 8192 : g;
-        if ((e = launch_pdl(splitk_reduce_kernel, unsigned(g), 256, stream, pdl, static_cast<const float *>(J.part), J.ks,
-                            int(J.pair), J.rows, J.t, J.y, J.ldy)) != cudaSuccess)
+        const int vec = J.rows % 4 == 0 && J.ldy % 4 == 0 && (reinterpret_cast<uintptr_t>(J.y) & 15) == 0;
+        const long long per_tok = vec ? J.rows / 4 : J.rows;
+        long long gx = (per_tok + 127) / 128;
+        gx = gx > 1024 ? 1024 : gx;
+        const dim3 grid(unsigned(gx), unsigned(J.t < 65535 ? J.t : 65535));
+        if ((e = launch_reduce(grid, stream, pdl, static_cast<const float *>(J.part), J.ks, int(J.pair), J.rows, J.t, J.y,
+                               J.ldy, vec)) != cudaSuccess)
             return e;
     }
     return cudaSuccess;
