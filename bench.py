@@ -712,6 +712,45 @@ def probe(args) -> None:
     rt.close()
 
 
+def prim_probe(args) -> None:
+    """One host-half primitive at the prims section's attention sizes (16 query heads on 4 kv
+    heads, 256 columns, a history of `args.t` rows, 4096 unless given) through the C ABI,
+    `args.launches` launches each timed with CUDA events after one warm-up launch: for profiler
+    captures. Prints the mean time per launch and its algorithmic bytes."""
+    import torch
+
+    import rtb200
+    h, n1, c = 16, 4, 256
+    t = args.t if args.t > 1 else 4096
+    l = [q * n1 // h for q in range(h)]
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    kv = torch.randn(t * n1 * c, device="cuda", generator=gen)
+    q = torch.randn(h * c, device="cuda", generator=gen)
+    a = torch.randn(h * t, device="cuda", generator=gen)
+    z = torch.empty(h * max(t, c), device="cuda")
+    rt = rtb200.Runtime()
+    rt.set_async(True)
+    rt.set_stream(torch.cuda.current_stream().cuda_stream)
+    if args.probe == "ip21_kv":
+        launch = lambda: rt.ip21_kv(z.data_ptr(), kv.data_ptr(), n1, c, l, h, t, q.data_ptr())  # noqa: E731
+    else:
+        launch = lambda: rt.ip12_kv(z.data_ptr(), a.data_ptr(), kv.data_ptr(), n1, c, l, h, t)  # noqa: E731
+    launch()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.launches)]
+    for e0, e1 in ev:
+        e0.record()
+        launch()
+        e1.record()
+    torch.cuda.synchronize()
+    rt.sync()
+    us = sum(e0.elapsed_time(e1) for e0, e1 in ev) / len(ev) * 1e3
+    nbytes = (t * n1 * c + h * c + h * t) * 4
+    print(json.dumps({"probe": args.probe, "h": h, "n1": n1, "c": c, "t": t, "us_per_launch": round(us, 2),
+                      "bytes": nbytes, "GB_s": round(nbytes / us / 1e3, 1)}), flush=True)
+    rt.close()
+
+
 def load_probe(args) -> None:
     """rt_b200_load_gguf on a synthetic GGUF of `args.load_layers` decode layers (QKV, out, gate, up,
     down; Q8_0 with random quants and fp16 scales) plus the 151936 x 4096 head: O_DIRECT reads into
@@ -799,8 +838,9 @@ def main() -> int:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--layers", type=int, default=WL.LAYERS)
     ap.add_argument("--no-prompt", action="store_true", help="skip the config-4 prompt gemm section")
-    ap.add_argument("--probe", choices=[p.name for p in WL.SWEEP] + ["draft_head"],
-                    help="time one product kernel on this BASELINE shape (profiler captures)")
+    ap.add_argument("--probe", choices=[p.name for p in WL.SWEEP] + ["draft_head", "ip21_kv", "ip12_kv"],
+                    help="time one product kernel on this BASELINE shape, or one host-half primitive at "
+                         "the prims section's attention sizes (profiler captures)")
     ap.add_argument("--t", type=int, default=1, help="--probe: tokens")
     ap.add_argument("--launches", type=int, default=3, help="--probe: timed launches")
     ap.add_argument("--load", action="store_true", help="time the weight loader on a synthetic GGUF file")
@@ -808,7 +848,7 @@ def main() -> int:
     ap.add_argument("--dir", default="/tmp", help="--load: where the file is written")
     args = ap.parse_args()
     if args.probe:
-        probe(args)
+        (prim_probe if args.probe in ("ip21_kv", "ip12_kv") else probe)(args)
         return 0
     if args.load:
         load_probe(args)

@@ -550,11 +550,11 @@ __global__ void __launch_bounds__(TcShape<CPS>::NT, CPS) gemm_tc_kernel(const __
 // largest |x| of the token gives s_t (|x| * 2^s_t <= 2^15 at that entry; s_t <= 126), then
 // xh = fp16(x * 2^s_t) and tokf[t] = 2^-s_t. Blocks from t: the matrix rows (W's rows, then a
 // pair's up rows), a half-warp per row: the row's largest scale gives r_o (row_exponent) into rexp.
-constexpr int PREP_THREADS = 256, PREP_HELD = 16;
+constexpr int PREP_THREADS = 256;
 
 // RPB rows per half-warp and batch: 8 where the matrix has rows enough to give every SM a block
 // of 16-row warps, else 1 (a few deep blocks on a small matrix leave most SMs idle).
-template <int RPB>
+template <int RPB, int HELD>
 __global__ void __launch_bounds__(PREP_THREADS) tc_prep_kernel(const float *x, long long ldx, int cols, int t,
                                                                __half *xh, float *tokf, const uint8_t *w,
                                                                const uint8_t *w2, long long rows, int8_t *rexp) {
@@ -570,20 +570,21 @@ __global__ void __launch_bounds__(PREP_THREADS) tc_prep_kernel(const float *x, l
         const float *xt = x + (long long)blockIdx.x * ldx;
         __half *ht = xh + (long long)blockIdx.x * cols;
         // 16-byte pieces where the row allows, the whole row held in registers between the scan
-        // and the conversion (rows of up to PREP_HELD * 4 * PREP_THREADS columns)
+        // and the conversion (rows of up to HELD * 4 * PREP_THREADS columns; HELD = 4 for rows of
+        // 4096 columns or fewer, so that the blocks' registers leave room for more blocks per SM)
         const bool vec = cols % 4 == 0 && (reinterpret_cast<uintptr_t>(xt) & 15) == 0 &&
-                         cols <= PREP_HELD * 4 * PREP_THREADS;
-        float4 v[PREP_HELD];
+                         cols <= HELD * 4 * PREP_THREADS;
+        float4 v[HELD];
         float amax = 0.0f;
         if (vec) {
             const float4 *x4 = reinterpret_cast<const float4 *>(xt);
 #pragma unroll
-            for (int q = 0; q < PREP_HELD; ++q) {
+            for (int q = 0; q < HELD; ++q) {
                 const int c = threadIdx.x + q * PREP_THREADS;
                 v[q] = c < cols / 4 ? __ldg(x4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
-            for (int q = 0; q < PREP_HELD; ++q)
+            for (int q = 0; q < HELD; ++q)
                 amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[q].x), fabsf(v[q].y)), fmaxf(fabsf(v[q].z), fabsf(v[q].w))));
         } else {
             for (int c = threadIdx.x; c < cols; c += PREP_THREADS)
@@ -612,7 +613,7 @@ __global__ void __launch_bounds__(PREP_THREADS) tc_prep_kernel(const float *x, l
         const float f = pow2i(s_sh);
         if (vec) {
 #pragma unroll
-            for (int q = 0; q < PREP_HELD; ++q) {
+            for (int q = 0; q < HELD; ++q) {
                 const int c = threadIdx.x + q * PREP_THREADS;
                 if (c < cols / 4) {
                     const __half2 lo = __halves2half2(__float2half_rn(v[q].x * f), __float2half_rn(v[q].y * f));
@@ -940,8 +941,10 @@ cudaError_t preload_gemm_tc() {
     if ((e = setup_shape<1>()) != cudaSuccess || (e = setup_shape<2>()) != cudaSuccess)
         return e;
     cudaFuncAttributes a;
-    if ((e = cudaFuncGetAttributes(&a, tc_prep_kernel<1>)) != cudaSuccess ||
-        (e = cudaFuncGetAttributes(&a, tc_prep_kernel<8>)) != cudaSuccess)
+    if ((e = cudaFuncGetAttributes(&a, tc_prep_kernel<1, 4>)) != cudaSuccess ||
+        (e = cudaFuncGetAttributes(&a, tc_prep_kernel<1, 16>)) != cudaSuccess ||
+        (e = cudaFuncGetAttributes(&a, tc_prep_kernel<8, 4>)) != cudaSuccess ||
+        (e = cudaFuncGetAttributes(&a, tc_prep_kernel<8, 16>)) != cudaSuccess)
         return e;
     if ((e = cudaFuncGetAttributes(&a, splitk_reduce_kernel<true>)) != cudaSuccess)
         return e;
@@ -1006,10 +1009,11 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
             const long long rows_per_block = (PREP_THREADS / 32) * 2 * (deep ? 8 : 1);
             long long rblocks = (nrows + rows_per_block - 1) / rows_per_block;
             rblocks = rblocks > 1184 ? 1184 : rblocks;
-            cudaError_t e = deep ? launch_pdl(tc_prep_kernel<8>, unsigned(G.t + rblocks), PREP_THREADS, stream, pdl, G.x,
-                                              G.ldx, G.cols, G.t, xh, tokf, G.w, G.w2, G.rows, rexp)
-                                 : launch_pdl(tc_prep_kernel<1>, unsigned(G.t + rblocks), PREP_THREADS, stream, pdl, G.x,
-                                              G.ldx, G.cols, G.t, xh, tokf, G.w, G.w2, G.rows, rexp);
+            const bool narrow = G.cols <= 4 * 4 * PREP_THREADS;
+            auto kern = deep ? (narrow ? tc_prep_kernel<8, 4> : tc_prep_kernel<8, 16>)
+                             : (narrow ? tc_prep_kernel<1, 4> : tc_prep_kernel<1, 16>);
+            cudaError_t e = launch_pdl(kern, unsigned(G.t + rblocks), PREP_THREADS, stream, pdl, G.x, G.ldx, G.cols, G.t,
+                                       xh, tokf, G.w, G.w2, G.rows, rexp);
             if (e != cudaSuccess)
                 return e;
         }
