@@ -10,6 +10,10 @@
 //     cannot be split, so each thread keeps one chain per query head it serves while the key
 //     slice streams through shared memory, shared by the query heads of one kv head;
 //   - rt_scale_outer is z = fma(g, s, a*b) with the product rounded first (rt_host.c:261-279).
+#include <cuda.h>
+
+#include <cstring>
+
 #include "q8_kernels.h"
 #include "q8_ptx.cuh"
 
@@ -111,13 +115,16 @@ constexpr long long DOT_WIDE_MIN = 148ll * 256 * 2;
 // ---------------------------------------------------------------- ip12_kv
 // A CTA: one kv head's group of query heads and a W-column slice of c (W = 32 where c allows,
 // else 8); thread W*hi + j keeps z[h][k] for head hi of the group and column j of the slice as
-// one fma chain over the history rows in order. The slice of every row (4W bytes) and the
-// group's weights for the same rows stream through a ring of SLOTS stages of ROWS rows
-// (cp.async). A warp runs alone on its scheduler and its chain takes one dependent fma per row,
-// so the rest of a row's work has to fit in the fma's latency: the operands of the next 16 rows
-// are loaded while the current 16 chain (two register sets in turn, nothing copied between
-// them), four rows' weights come in one 16-byte load (weight rows padded by 16 bytes so that four
-// heads' reads fall into different banks), and a copy's addresses are formed once per launch.
+// one fma chain over the history rows in order. The slice streams through a ring of SLOTS stages
+// of ROWS rows, one 2-D tensor copy per stage (a W x ROWS box of the history seen as [t][n1*c],
+// rows past t filled with zeros) issued by thread 0 and counted on the slot's barrier; the
+// group's weights for the same rows come by per-thread cp.async. A warp runs alone on its
+// scheduler and its chain takes one dependent fma per row, so the rest of a row's work has to
+// fit in the fma's latency: the operands of the next 16 rows are loaded while the current 16
+// chain (two register sets in turn, nothing copied between them), and four rows' weights come in
+// one 16-byte load (weight rows padded by 16 bytes so that four heads' reads fall into different
+// banks). Every wait is bounded: a slice that never lands sets ERR_TIMEOUT_FULL, the CTA stops
+// issuing, thread 0 waits (bounded) for the copies it issued, and z is left unwritten.
 constexpr int IP12_ROWS = 128, IP12_SLOTS = 8, IP12_WS = IP12_ROWS + 4;
 __host__ __device__ constexpr size_t ip12_smem(int w, int nh) {
     return size_t(IP12_SLOTS) * (size_t(IP12_ROWS) * w + size_t(nh) * IP12_WS) * 4;
@@ -133,43 +140,48 @@ __device__ __forceinline__ void cp_async4(void *smem, const void *gmem, bool ok)
     const int n = ok ? 4 : 0;
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(s), "l"(gmem), "r"(n) : "memory");
 }
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, int c0, int c1, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(tm), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
 
 template <int W>
-__global__ void __launch_bounds__(W * MAX_PRIM_GROUP, 1) ip12_kv_kernel(float *z, const float *a, const float *kv,
-                                                                        long long n1, long long c, long long t,
-                                                                        PrimGroups groups) {
+__global__ void __launch_bounds__(W * MAX_PRIM_GROUP, 1) ip12_kv_kernel(float *z, const float *a, long long c, long long t,
+                                                                        PrimGroups groups,
+                                                                        const __grid_constant__ CUtensorMap tkv,
+                                                                        unsigned *err) {
     // dynamic: [SLOTS][ROWS][W] of history, then [SLOTS][nmax][WS] of a (nmax = blockDim.x / W,
     // at least the launch's largest group)
-    extern __shared__ __align__(16) float dyn[];
+    extern __shared__ __align__(128) float dyn[];
+    __shared__ __align__(8) uint64_t full[IP12_SLOTS];
+    __shared__ int s_bad;
     float(*ring)[IP12_ROWS][W] = reinterpret_cast<float(*)[IP12_ROWS][W]>(dyn);
     const int nmax = blockDim.x / W;
     float *wbase = dyn + size_t(IP12_SLOTS) * IP12_ROWS * W;
     const int gi = blockIdx.y, hi = threadIdx.x / W, j = threadIdx.x % W;
     const int first = groups.first[gi], nh = groups.first[gi + 1] - first;
-    const long long k0 = (long long)blockIdx.x * W; // c % W == 0: the slice is whole
-    const long long rstride = n1 * c;               // floats from one history row to the next
-    // this thread's history copies, the same in every stage: 16 bytes at column 4 * (tid % (W/4))
-    // of rows tid / (W/4), + blockDim / (W/4), ... (blockDim is a multiple of 32, so of W/4); the
-    // source walks down the history, one stage of rows per stage. Of a: either 16-byte pieces
-    // (t % 4 == 0 and a 16-aligned) or single floats (a's rows are only 4-byte aligned otherwise).
-    const int row_step = blockDim.x / (W / 4), my_row = threadIdx.x / (W / 4), my_col = 4 * (threadIdx.x % (W / 4));
-    const float *kv_next = kv + groups.kv[gi] * c + k0 + my_row * rstride + my_col; // stage 0's first copy
-    const long long src_step = row_step * rstride;
+    const long long k0 = (long long)blockIdx.x * W;     // c % W == 0: the slice is whole
+    const int kx = int(groups.kv[gi] * c + k0);         // the slice's first column in [t][n1*c]
     const bool a16 = (t % 4) == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < IP12_SLOTS; ++s)
+            mbar_init(&full[s], 1);
+        fence_barrier_init();
+        s_bad = 0;
+    }
+    __syncthreads();
+    long long issued = 0, landed0 = 0; // (thread 0: stages issued, stages whose slice it saw land)
     auto issue = [&](long long stage) {
         const int sl = int(stage % IP12_SLOTS);
         const long long r0 = stage * IP12_ROWS;
-        float *dst = &ring[sl][my_row][my_col];
-        const float *src = kv_next;
-        long long row = r0 + my_row;
-        for (int rr = my_row; rr < IP12_ROWS; rr += row_step) {
-            const bool ok = row < t;
-            cp_async16(dst, ok ? src : kv, ok);
-            dst += row_step * W;
-            src += src_step;
-            row += row_step;
+        if (threadIdx.x == 0) {
+            mbar_arrive_expect_tx(&full[sl], uint32_t(IP12_ROWS * W * 4));
+            tma_load_2d(&ring[sl][0][0], &tkv, kx, int(r0), &full[sl]);
+            issued = stage + 1;
         }
-        kv_next += IP12_ROWS * rstride;
         float *ws = wbase + size_t(sl) * nmax * IP12_WS;
         if (a16) {
             for (int e = threadIdx.x; e < nh * (IP12_ROWS / 4); e += blockDim.x) {
@@ -197,11 +209,20 @@ __global__ void __launch_bounds__(W * MAX_PRIM_GROUP, 1) ip12_kv_kernel(float *z
     float acc = 0.0f;
     for (long long st = 0; st < nstages; ++st) {
         asm volatile("cp.async.wait_group %0;" ::"n"(IP12_SLOTS - 2) : "memory");
-        __syncthreads(); // stage st landed for every thread; slot (st - 1) % SLOTS is free again
+        __syncthreads(); // stage st's weights landed for every thread; slot (st - 1) % SLOTS is free again
+        if (*reinterpret_cast<volatile int *>(&s_bad))
+            break; // (read by every thread after the same barrier: all leave together)
         if (st + IP12_SLOTS - 1 < nstages)
             issue(st + IP12_SLOTS - 1);
         asm volatile("cp.async.commit_group;" ::: "memory");
         const int sl = int(st % IP12_SLOTS);
+        if (!mbar_wait(&full[sl], uint32_t((st / IP12_SLOTS) & 1))) {
+            report(err, ERR_TIMEOUT_FULL);
+            *reinterpret_cast<volatile int *>(&s_bad) = 1;
+            continue;
+        }
+        if (threadIdx.x == 0)
+            landed0 = st + 1;
         const float(*slot)[W] = ring[sl];
         const float *ws = wbase + (size_t(sl) * nmax + (mine ? hi : 0)) * IP12_WS;
         const int nr = int(t - st * IP12_ROWS < IP12_ROWS ? t - st * IP12_ROWS : IP12_ROWS);
@@ -243,7 +264,11 @@ __global__ void __launch_bounds__(W * MAX_PRIM_GROUP, 1) ip12_kv_kernel(float *z
         }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
-    if (mine)
+    if (threadIdx.x == 0) // copies thread 0 issued and did not see land (only after a timeout)
+        for (long long s = landed0; s < issued; ++s)
+            if (!mbar_wait(&full[s % IP12_SLOTS], uint32_t((s / IP12_SLOTS) & 1)))
+                break;
+    if (mine && !*reinterpret_cast<volatile int *>(&s_bad))
         z[(long long)groups.head[first + hi] * c + k0 + j] = acc;
 }
 
@@ -288,8 +313,8 @@ cudaError_t launch_ip21_kv(float *z, const float *kv, long long n1, long long c,
 }
 
 cudaError_t launch_ip12_kv(float *z, const float *a, const float *kv, long long n1, long long c, const PrimGroups &groups,
-                           long long t, cudaStream_t stream) {
-    if (groups.n < 1 || groups.n > MAX_PRIM_HEADS || c < 8 || c % 8)
+                           long long t, unsigned *err, cudaStream_t stream) {
+    if (groups.n < 1 || groups.n > MAX_PRIM_HEADS || c < 8 || c % 8 || n1 * c >= (1ll << 31))
         return cudaErrorInvalidValue;
     int most = 0;
     for (int g = 0; g < groups.n; ++g)
@@ -298,14 +323,20 @@ cudaError_t launch_ip12_kv(float *z, const float *a, const float *kv, long long 
         return cudaErrorInvalidValue;
     // 32-column slices (128-byte history pieces) where c allows: measured faster than 8 on the
     // attention shapes, with four warps of one head each per CTA
-    if (c % 32 == 0) {
+    const int w = c % 32 == 0 ? 32 : 8;
+    alignas(64) CUtensorMap tkv;
+    memset(&tkv, 0, sizeof tkv);
+    if (t > 0 && !map_f32_2d(&tkv, kv, uint64_t(n1 * c), uint64_t(t), uint64_t(n1 * c) * 4, uint32_t(w),
+                             uint32_t(IP12_ROWS)))
+        return cudaErrorInvalidValue;
+    if (w == 32) {
         const int threads = 32 * most;
         ip12_kv_kernel<32><<<dim3(unsigned(c / 32), unsigned(groups.n)), threads, ip12_smem(32, most), stream>>>(
-            z, a, kv, n1, c, t, groups);
+            z, a, c, t, groups, tkv, err);
     } else {
         const int threads = (8 * most + 31) / 32 * 32;
         ip12_kv_kernel<8><<<dim3(unsigned(c / 8), unsigned(groups.n)), threads, ip12_smem(8, threads / 8), stream>>>(
-            z, a, kv, n1, c, t, groups);
+            z, a, c, t, groups, tkv, err);
     }
     return cudaGetLastError();
 }

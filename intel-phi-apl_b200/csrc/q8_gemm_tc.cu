@@ -1068,4 +1068,10 @@ cudaError_t launch_gemm_tc(const GemmJob *jobs, int n, void *scratch, size_t scr
     return cudaSuccess;
 }
 
+bool map_f32_2d(void *map, const float *base, uint64_t inner, uint64_t outer, uint64_t stride_bytes,
+                uint32_t box_inner, uint32_t box_outer) {
+    return make_map(static_cast<CUtensorMap *>(map), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, inner, outer, stride_bytes,
+                    box_inner, box_outer, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 } // namespace q8

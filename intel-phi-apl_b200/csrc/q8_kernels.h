@@ -141,7 +141,11 @@ cudaError_t launch_ip21(float *z, const float *a, long long h, long long r, long
 cudaError_t launch_ip21_kv(float *z, const float *kv, long long n1, long long c, const PrimHeads &heads, long long h,
                            long long t, const float *b, cudaStream_t stream);
 cudaError_t launch_ip12_kv(float *z, const float *a, const float *kv, long long n1, long long c, const PrimGroups &groups,
-                           long long t, cudaStream_t stream);
+                           long long t, unsigned *err, cudaStream_t stream);
+// A 2-D fp32 tensor map (no swizzle, zero fill) into `map` (a CUtensorMap, 64-byte aligned):
+// `outer` rows of `inner` floats, `stride_bytes` apart, boxes of box_inner x box_outer.
+bool map_f32_2d(void *map, const float *base, uint64_t inner, uint64_t outer, uint64_t stride_bytes,
+                uint32_t box_inner, uint32_t box_outer);
 cudaError_t launch_scale_outer(float *z, const float *s, float g, const float *a, const float *b, long long m,
                                long long k, cudaStream_t stream);
 cudaError_t preload_prims();

@@ -1386,7 +1386,7 @@ void rt_ip12_kv(struct rt *R, float *z, const float *a, const float *kv, long n1
     }
     g.first[g.n] = nh;
     c->synced = false;
-    if (cuda_ok(c, q8::launch_ip12_kv(z, a, kv, n1, c_cols, g, t, c->stream), "rt_ip12_kv"))
+    if (cuda_ok(c, q8::launch_ip12_kv(z, a, kv, n1, c_cols, g, t, c->d_err, c->stream), "rt_ip12_kv"))
         finish(c);
 }
 
