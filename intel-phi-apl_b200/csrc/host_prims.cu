@@ -273,8 +273,27 @@ __global__ void __launch_bounds__(W * MAX_PRIM_GROUP, 1) ip12_kv_kernel(float *z
 }
 
 // ---------------------------------------------------------------- scale_outer
-__global__ void scale_outer_kernel(float *z, const float *s, float g, const float *a, const float *b, long long m,
-                                   long long k) {
+// One element per thread, or four in 16-byte accesses (vec: k % 4 == 0, z, s and b 16-aligned,
+// m * k < 2^31), the row and column from 32-bit index arithmetic where the size allows.
+__global__ void __launch_bounds__(256) scale_outer_kernel(float *z, const float *s, float g, const float *a, const float *b,
+                                                          long long m, long long k, int vec) {
+    if (vec) {
+        const int nq4 = int(k / 4), n4 = int(m) * nq4;
+        const float4 *s4 = reinterpret_cast<const float4 *>(s), *b4 = reinterpret_cast<const float4 *>(b);
+        float4 *z4 = reinterpret_cast<float4 *>(z);
+        for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n4; e += gridDim.x * blockDim.x) {
+            const int i = e / nq4, q = e - i * nq4;
+            const float ai = __ldg(a + i);
+            const float4 sv = __ldg(s4 + e), bv = __ldg(b4 + q);
+            float4 r;
+            r.x = __fmaf_rn(g, sv.x, __fmul_rn(ai, bv.x));
+            r.y = __fmaf_rn(g, sv.y, __fmul_rn(ai, bv.y));
+            r.z = __fmaf_rn(g, sv.z, __fmul_rn(ai, bv.z));
+            r.w = __fmaf_rn(g, sv.w, __fmul_rn(ai, bv.w));
+            z4[e] = r;
+        }
+        return;
+    }
     const long long n = m * k;
     for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
         const long long i = e / k, q = e - i * k;
@@ -344,9 +363,10 @@ cudaError_t launch_ip12_kv(float *z, const float *a, const float *kv, long long 
 cudaError_t launch_scale_outer(float *z, const float *s, float g, const float *a, const float *b, long long m,
                                long long k, cudaStream_t stream) {
     const long long n = m * k;
-    unsigned grid = grid_of(n, 256);
+    const int vec = k % 4 == 0 && n < (1ll << 31) && aligned16(z) && aligned16(s) && aligned16(b);
+    unsigned grid = grid_of(vec ? n / 4 : n, 256);
     grid = grid > 148u * 16 ? 148u * 16 : grid;
-    scale_outer_kernel<<<grid, 256, 0, stream>>>(z, s, g, a, b, m, k);
+    scale_outer_kernel<<<grid, 256, 0, stream>>>(z, s, g, a, b, m, k, vec);
     return cudaGetLastError();
 }
 
